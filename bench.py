@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark of the soinfer B200 decode hot path on BASELINE.json's headline
+metric: INT4 g128 GEMV HBM throughput (GB/s, % of measured HBM peak).
+
+Workload (configs[0] shapes, run on the GPU): per layer copy, the gate_proj
+GEMV [6144 x 2048] followed by the down_proj GEMV [2048 x 6144] that consumes
+its output; one step = one pass over LAYERS distinct layer copies (default
+64 -> 128 GEMVs over 858 MB of packed weights, far above the 126 MB L2, so no
+L2 flush is needed).  Weights ~N(0, 0.02) quantized to group-128 INT4 on the
+GPU with soinfer.quant; x ~N(0, 1) fp16; seeded.  The step is replayed as a
+CUDA graph and timed with CUDA events; `value` = algorithmic bytes (packed
+weights + fp32 scales + x + y per GEMV, 6,701,056 B) of all ranks / max rank
+time.
+
+`e2e`: the same chain through the public streaming API (WeightPipeline: packed
+weights streamed from the pinned host arena by the copy engine, double
+buffered, x uploaded from pinned memory and the result read back every step).
+
+`--impl reference`: the reference's CPU path (formats.dequantize + fp32
+matvec, restated in oracle/) on this host's cores, same metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "sparse-offload-infer_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+H, I, G = 2048, 6144, 128
+METRIC = "INT4 g128 GEMV HBM GB/s"
+UNIT = "GB/s"
+
+
+def gemv_bytes(n: int, k: int, g: int = G) -> int:
+    """Algorithmic bytes of one GEMV: packed INT4 weights + fp32 scales + fp16 x + fp16 y."""
+    return n * (-(-k // 8) * 4) + n * (-(-k // g)) * 4 + 2 * k + 2 * n
+
+
+BYTES_PER_GEMV = gemv_bytes(I, H)  # == gemv_bytes(H, I) == 6,701,056
+assert BYTES_PER_GEMV == gemv_bytes(H, I) == 6_701_056
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def profile_traffic(kernel_tag: str):
+    """Per-launch DRAM traffic recorded from an ncu capture in profiles/ (a line
+    'traffic_bytes_per_launch[<tag>]: <int>'), or None."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    key = f"traffic_bytes_per_launch[{kernel_tag}]:"
+    for name in sorted(os.listdir(pdir)):
+        try:
+            for line in open(os.path.join(pdir, name)):
+                if line.strip().startswith(key):
+                    return int(float(line.split(":", 1)[1].strip()))
+        except (OSError, ValueError):
+            continue
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every ~10 ms."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device_index: int):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[device_index]) if vis else device_index
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: clocks unreported
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(get_reasons(self._h)) & ~0x1
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict | None:
+        if self._nv is None:
+            return None
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": float(np.median(self.samples)) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------- CPU side
+def cpu_gemv_sample(seconds: float, threads: int):
+    """The reference's CPU path restated (oracle): fp32 matvec of the
+    pre-dequantized INT4 weights, dequantization outside the timer
+    (tests/test_m4_kernels.py:157-168 oracle; BASELINE.md CPU plan).
+    Returns (GB/s of algorithmic INT4 bytes, sample description, gemvs run)."""
+    from oracle import reference_port as port
+
+    rng = np.random.default_rng(0)
+    mats = []
+    for i, (n, k) in enumerate([(I, H), (H, I), (I, H), (H, I)]):
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+        q, s = port.quantize_group(w, G)
+        mats.append(port.dequant_int4(port.pack_int4(q), s, k, G))
+    x0 = rng.standard_normal(H).astype(np.float16).astype(np.float32)
+    n_gemv = 0
+    t0 = time.perf_counter()
+    while True:
+        x = x0
+        for j in range(0, 4, 2):
+            y = mats[j] @ x
+            x = (mats[j + 1] @ y.astype(np.float16).astype(np.float32)).astype(np.float32)
+            n_gemv += 2
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    gbs = n_gemv * BYTES_PER_GEMV / dt / 1e9
+    desc = (f"{n_gemv} fp32 matvecs (2x gate {I}x{H} + 2x down {H}x{I}, dequantized outside the timer) "
+            f"in {dt:.2f} s on {threads} threads")
+    return gbs, desc, n_gemv
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    # warmup + K timed steps; one step = 4 GEMVs (two layer copies) of the same workload
+    per_step = []
+    from oracle import reference_port as port
+
+    rng = np.random.default_rng(0)
+    mats = []
+    for n, k in [(I, H), (H, I), (I, H), (H, I)]:
+        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+        q, s = port.quantize_group(w, G)
+        mats.append(port.dequant_int4(port.pack_int4(q), s, k, G))
+    x0 = rng.standard_normal(H).astype(np.float16).astype(np.float32)
+
+    def step():
+        x = x0
+        for j in range(0, 4, 2):
+            y = (mats[j] @ x).astype(np.float16).astype(np.float32)
+            x = mats[j + 1] @ y
+        return x
+
+    for _ in range(args.warmup):
+        step()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        per_step.append(time.perf_counter() - t0)
+    total = sum(per_step)
+    value = 4 * args.steps * BYTES_PER_GEMV / total / 1e9
+    sample = (f"per step 4 fp32 matvecs (2x gate {I}x{H} + 2x down {H}x{I}) of pre-dequantized INT4 weights, "
+              f"numpy BLAS on {threads} threads; dequantization outside the timer")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "configs[0]: INT4 g128 GEMV gate_proj 6144x2048 + down_proj 2048x6144 (CPU port)",
+                   "gemvs_per_step": 4, "bytes_per_gemv": BYTES_PER_GEMV, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- GPU side
+def build_layers(layers: int, device, seed: int):
+    """Per layer: (gate packed [I, H/2], gate scale [I, 16], down packed [H, I/2], down scale [H, 48]) on device."""
+    from soinfer.quant import formats, pack
+
+    cfg = formats.QuantConfig(bits=4, granularity="group", group_size=G)
+    out = []
+    gen = torch.Generator(device=device)
+    for layer in range(layers):
+        mats = []
+        for n, k in ((I, H), (H, I)):
+            gen.manual_seed(seed * 1000 + 2 * layer + (n == H))
+            w = torch.randn(n, k, generator=gen, device=device) * 0.02
+            qt = formats.quantize(w, cfg)
+            packed, _ = pack.pack_int4(qt.qweight)
+            mats += [packed.contiguous(), qt.scale.contiguous()]
+            del w, qt
+        out.append(tuple(mats))
+    torch.cuda.synchronize(device)
+    return out
+
+
+def run_ours(args) -> None:
+    import torch.distributed as dist
+
+    from soinfer import _C
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    _C.lib()  # fail loudly if the CUDA library is missing
+
+    L = args.layers
+    layers = build_layers(L, device, seed=rank + 1)
+    gen = torch.Generator(device=device).manual_seed(12345 + rank)
+    x = (torch.randn(H, generator=gen, device=device)).half()
+    ys = [torch.empty(I, dtype=torch.float16, device=device) for _ in range(L)]
+    outs = [torch.empty(H, dtype=torch.float16, device=device) for _ in range(L)]
+
+    def step():
+        for li, (gw, gs, dw, ds) in enumerate(layers):
+            _C.gemv_w4a16_group_lop3(gw, gs, x, H, G, out=ys[li], pdl=args.pdl)
+            _C.gemv_w4a16_group_lop3(dw, ds, ys[li], I, G, out=outs[li], pdl=args.pdl)
+
+    # correctness spot check of the chain's first pair against the oracle
+    step()
+    torch.cuda.synchronize(device)
+    from oracle import reference_port as port
+
+    gw, gs, dw, ds = layers[0]
+    y_ref = port.gemv_w4a16(gw.cpu().numpy(), gs.cpu().numpy(), x.cpu().numpy(), H, G)
+    err = float(np.abs(ys[0].double().cpu().numpy() - y_ref).max())
+    assert err < 1e-2, f"gemv spot check failed: max-abs {err}"
+
+    stream = torch.cuda.Stream(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+        stream.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+    torch.cuda.synchronize(device)
+
+    launches_per_step = 2 * L
+    bytes_per_step = launches_per_step * BYTES_PER_GEMV
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with sampler:
+        cur = torch.cuda.current_stream(device)
+        start.record(cur)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(cur)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    value = world * args.steps * bytes_per_step / (max_ms / 1e3) / 1e9
+    per_launch_s = (elapsed_ms / 1e3) / (args.steps * launches_per_step)
+    achieved = BYTES_PER_GEMV / per_launch_s / 1e9
+
+    # ---- e2e through the public streaming API (weights from the pinned arena)
+    e2e = run_e2e(args, layers, device, world, dist)
+
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        gbs, desc, _ = cpu_gemv_sample(args.cpu_seconds, threads)
+        cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4w-f16a-f32acc", "data": "synthetic",
+        "config": {"workload": "configs[0]: INT4 g128 GEMV, gate_proj 6144x2048 then down_proj 2048x6144 per layer "
+                               f"copy, chained over {L} layer copies",
+                   "layers": L, "gemvs_per_step": launches_per_step, "bytes_per_gemv": BYTES_PER_GEMV,
+                   "weights_bytes": L * 2 * (I * H // 2),
+                   "l2": "inputs larger than L2 (weights far above the 126 MB L2), no flush", "cuda_graph": True,
+                   "pdl": bool(args.pdl), "parallelism": f"{world} independent replicas (no collective)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                     "traffic": profile_traffic("gemv_w4_mma"),
+                     "kernel": "gemv_w4_mma_kernel (INT4 g128, mma.sync m16n8k16 dot products)"},
+        "e2e": e2e,
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": sampler.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, layers, device, world, dist) -> dict:
+    from soinfer.offload.load_hf_checkpoint import LoadedMatrix
+    from soinfer.offload.weight_store import PinnedWeightStore
+    from soinfer.runtime.generate import StreamingModel, WeightPipeline
+
+    L = len(layers)
+    total = sum(t[0].numel() + t[2].numel() for t in layers)
+    store = PinnedWeightStore(total)
+    matrices = {}
+    for li, (gw, gs, dw, ds) in enumerate(layers):
+        for suffix, w, s, n, k in (("mlp.gate_proj.weight", gw, gs, I, H), ("mlp.down_proj.weight", dw, ds, H, I)):
+            name = f"model.layers.{li}.{suffix}"
+            matrices[name] = LoadedMatrix(store.register(name, w.cpu()), s, k, n, k)
+    torch.cuda.synchronize(device)
+    model = StreamingModel(store=store, matrices=matrices, num_layers=L, embed_tokens=None, lm_head=None,
+                           final_norm=None, layer_norms=[], hidden_size=H, num_attention_heads=16,
+                           num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6, rope_theta=1e6, group_size=G)
+    pipe = WeightPipeline(model, suffixes=("mlp.gate_proj.weight", "mlp.down_proj.weight"))
+    x_host = torch.randn(H, generator=torch.Generator().manual_seed(7)).half().pin_memory()
+    out_host = torch.empty(H, dtype=torch.float16).pin_memory()
+    x_dev = torch.empty(H, dtype=torch.float16, device=device)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        o = None
+        for _ in range(L):
+            y = pipe.next_gemv(x_dev)
+            o = pipe.next_gemv(y)
+        out_host.copy_(o, non_blocking=True)
+
+    steps = max(3, min(args.steps, args.e2e_steps))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    cur = torch.cuda.current_stream(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(cur)
+    for _ in range(steps):
+        e2e_step()
+    e.record(cur)
+    torch.cuda.synchronize(device)
+    ms = s.elapsed_time(e)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    h2d = 2 * L * (I * H // 2) + 2 * H
+    value = world * steps * 2 * L * BYTES_PER_GEMV / (ms / 1e3) / 1e9
+    return {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 2 * H,
+            "steps": steps, "ms_per_step": round(ms / steps, 3), "h2d_gbs": round(world * steps * h2d / (ms / 1e3) / 1e9, 2),
+            "path": "soinfer.runtime.generate.WeightPipeline (copy-engine double buffering from the pinned arena)"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=64)
+    ap.add_argument("--pdl", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

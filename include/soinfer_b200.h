@@ -1,0 +1,249 @@
+/*
+ * soinfer_b200.h -- C ABI of the B200 (sm_100a) decode hot path of soinfer.
+ *
+ * Every entry point takes plain device/host pointers, 64-bit sizes and a CUDA
+ * stream handle (`void* stream`, a cudaStream_t; NULL = legacy default
+ * stream), launches asynchronously on that stream, and returns a status code
+ * (SOINFER_OK == 0).  No entry point aborts the process: argument errors are
+ * reported as SOINFER_ERR_INVALID_ARGUMENT before anything is launched, and
+ * launch failures as SOINFER_ERR_CUDA.  soinfer_last_error() returns the
+ * message of the most recent failure on the calling thread.
+ *
+ * Data formats (identical to the reference's packing contract,
+ * csrc/include/layout.h:19-67 of sparse-offload-infer):
+ *   - INT4 weights: uint8 [N, ceil(K/8)*4]; each 4-byte group holds 8 signed
+ *     two's-complement nibbles in AWQ order [0,2,4,6,1,3,5,7]
+ *     (byte0 = v0|v2<<4, byte1 = v4|v6<<4, byte2 = v1|v3<<4, byte3 = v5|v7<<4).
+ *   - INT8 weights: int8 [N, K], one value per byte.
+ *   - scales: fp32 [N, num_groups] row-major, element k of row n uses
+ *     scale[n, k / group_size]; num_groups == ceil(K / group_size).
+ *   - activations / outputs: IEEE fp16 (stored as uint16_t bit patterns).
+ *
+ * Each declaration names the reference interface it replaces as
+ * path:line inside the sparse-offload-infer repository.
+ */
+#ifndef SOINFER_B200_H_
+#define SOINFER_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t soinfer_half; /* IEEE binary16 bit pattern */
+
+enum soinfer_status {
+  SOINFER_OK = 0,
+  SOINFER_ERR_INVALID_ARGUMENT = 1, /* a precondition failed; nothing launched */
+  SOINFER_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed     */
+  SOINFER_ERR_UNSUPPORTED = 3,      /* valid request this build cannot serve    */
+  SOINFER_ERR_HOST = 4              /* host-side failure (thread pool, memcpy)  */
+};
+
+/* ABI version of this header (bumped on any signature change). */
+int soinfer_abi_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char* soinfer_last_error(void);
+/* Static name of a status code. */
+const char* soinfer_status_string(int status);
+
+/* ---------------------------------------------------------------- GEMV --- */
+
+/* y[n] = fp16( sum_k scale[n, k/g] * q[n,k] * x[k] ), fp32 accumulation.
+ * Wq: uint8 [N, ceil(K/8)*4]; scale: fp32 [N, num_groups]; x: fp16 [K];
+ * y: fp16 [N].  group_size must be a positive multiple of 8 and num_groups
+ * == ceil(K/group_size).
+ * Replaces: csrc/bindings.cpp:300-303 (gemv_w4a16_group) and
+ *           csrc/kernels/gemv_w4a16_group.cu:23-63. */
+int soinfer_gemv_w4a16_group(const uint8_t* Wq, const float* scale, const soinfer_half* x,
+                             soinfer_half* y, int64_t N, int64_t K, int64_t group_size,
+                             int64_t num_groups, void* stream);
+
+/* Same contract and same kernel as soinfer_gemv_w4a16_group (the two reference
+ * variants differ only in how the nibbles are unpacked; here both names run
+ * the one sm_100a kernel, so their outputs are identical by construction).
+ * Replaces: csrc/bindings.cpp:305-309 (gemv_w4a16_group_lop3) and
+ *           csrc/kernels/gemv_w4a16_group.cu:77-134. */
+int soinfer_gemv_w4a16_group_lop3(const uint8_t* Wq, const float* scale, const soinfer_half* x,
+                                  soinfer_half* y, int64_t N, int64_t K, int64_t group_size,
+                                  int64_t num_groups, void* stream);
+
+/* Launch flags for the *_ex entry points. */
+#define SOINFER_FLAG_PDL 1u /* programmatic dependent launch: the kernel may start before the
+                               previous kernel in the stream has finished and streams its weights
+                               meanwhile; only x is waited for.  Set it only when the weights are
+                               not written by the kernel that precedes this one in the stream. */
+
+/* soinfer_gemv_w4a16_group_lop3 with launch flags (SOINFER_FLAG_*).
+ * No reference counterpart (the reference launches on the legacy stream). */
+int soinfer_gemv_w4a16_group_ex(const uint8_t* Wq, const float* scale, const soinfer_half* x,
+                                soinfer_half* y, int64_t N, int64_t K, int64_t group_size,
+                                int64_t num_groups, uint32_t flags, void* stream);
+
+/* Row-indirect INT4 GEMV over HBM-resident weights: y[r] = row rows[r] of
+ * dequant(Wq, scale) dotted with x, for r in [0, num_sel).  Equivalent to
+ * gathering rows (Wq[rows], scale[rows]) and calling
+ * soinfer_gemv_w4a16_group_lop3 on them (bit-identical), without the copy.
+ * rows: int32 [num_sel] device, each in [0, N).
+ * Replaces the pair at runtime/generate.py:286-302 (gather_rows_staged of the
+ * selected up_proj rows + gemv_w4a16_group_lop3 with N = k) when the matrix is
+ * resident in device memory. */
+int soinfer_gemv_w4a16_rows(const uint8_t* Wq, const float* scale, int64_t N, const int32_t* rows,
+                            int64_t num_sel, const soinfer_half* x, soinfer_half* y, int64_t K,
+                            int64_t group_size, int64_t num_groups, void* stream);
+
+/* y = dequant(Wq, scale) @ x for symmetric INT8 weights.
+ * Wq: int8 [N, K]; scale: fp32 [N or 1, num_groups]; scale_row_stride = 0
+ * broadcasts one scale row (per-tensor) else num_groups.  num_groups is 1
+ * (per-tensor / per-channel) or ceil(K/group_size) with group_size % 4 == 0.
+ * Replaces: csrc/bindings.cpp:239-262, csrc/kernels/gemv_w8a16.cu:22-70. */
+int soinfer_gemv_w8a16(const int8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y,
+                       int64_t N, int64_t K, int64_t group_size, int64_t num_groups,
+                       int64_t scale_row_stride, void* stream);
+
+/* ------------------------------------------------------------ selection --- */
+
+/* Reference-compatible DIP channel selector ("ref mode", bit-exact with the
+ * reference): lo = 0, hi = max(0, max v) + 1e-3f, 24 fp32 bisection steps
+ * mid = 0.5f*(lo+hi) keeping count(v >= lo) >= k, tau = lo; out_idx receives
+ * the first min(k, count(v >= tau)) indices i in ascending order with
+ * v[i] >= tau and *out_count the number written.  Entries of out_idx past
+ * *out_count are set to -1.  abs_g: fp32 [n] device; out_idx: int32 [k];
+ * out_count: int32 [1].  Requires 1 <= k <= n.  Values are expected to be
+ * non-negative magnitudes (not checked, as in the reference).
+ * Replaces: csrc/bindings.cpp:507-518, csrc/kernels/topk_select.cu:10-102. */
+int soinfer_topk_threshold_select(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx,
+                                  int32_t* out_count, void* stream);
+
+/* Exact top-k ("exact mode"): the k largest values, ties at the k-th value
+ * broken by the lower index, written in ascending index order; *out_count = k.
+ * NaN ranks below every number.  Same buffers as the ref-mode selector.
+ * No reference counterpart (the reference selector is threshold-based). */
+int soinfer_topk_select_exact(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx,
+                              int32_t* out_count, void* stream);
+
+/* Cache descriptors: desc[j] = slot_of[sel[j]] when >= 0 (hot-cache hit),
+ * else (m | 0x80000000) where m is the miss position; miss[m] = sel[j].
+ * Misses are compacted in ascending j order (deterministic; the reference's
+ * atomic order is arbitrary).  *miss_count = number of misses.
+ * sel: int32 [k], each in [0, I); slot_of: int32 [I].
+ * Replaces: csrc/bindings.cpp:341-359, csrc/kernels/gemv_dip_fused.cu:17-42. */
+int soinfer_build_dip_descriptors(const int32_t* sel, int64_t k, const int32_t* slot_of, int64_t I,
+                                  int32_t* desc, int32_t* miss, int32_t* miss_count, void* stream);
+
+/* ------------------------------------------------- DIP fused GEMVs ------- */
+
+/* 'Up' direction of cache-or-stream DIP: y[j] = row j of the selected matrix
+ * dotted with x, where row j lives in cache (desc[j] >= 0: cache row
+ * desc[j]) or in staging (desc[j] < 0: staging row desc[j] & 0x7fffffff).
+ * Bit-identical to soinfer_gemv_w4a16_group_lop3 on the same logical rows.
+ * cache_Wq: uint8 [C, ceil(K/8)*4]; staging_Wq: uint8 [M, ...]; scales fp32
+ * [C|M, num_groups]; desc: int32 [k]; x: fp16 [K]; y: fp16 [k].
+ * Replaces: csrc/bindings.cpp:388-408, csrc/kernels/gemv_dip_fused.cu:48-102. */
+int soinfer_gemv_dip_fused_up(const uint8_t* cache_Wq, const float* cache_scale, int64_t C,
+                              const uint8_t* staging_Wq, const float* staging_scale, int64_t M,
+                              const int32_t* desc, int64_t k, const soinfer_half* x, soinfer_half* y,
+                              int64_t K, int64_t group_size, int64_t num_groups, void* stream);
+
+/* Bytes of zero-initialised device workspace the sparse 'down' GEMVs need for
+ * an output width H over k selected rows.  The kernels leave the workspace
+ * zeroed again on return, so a caller allocates (and clears) it once and
+ * reuses it for every call on one stream. */
+int64_t soinfer_sparse_workspace_bytes(int64_t H, int64_t k);
+
+/* 'Down' direction: y[c] = fp16( sum_{i<k} h[i] * scale[i, c/g] * q[i, c] )
+ * over k selected (already gathered) rows of the transposed down_proj.
+ * Wq_sel: uint8 [k, ceil(H/8)*4]; scale_sel: fp32 [k, num_groups];
+ * h: fp16 [k]; y: fp16 [H].  Deterministic fixed-order reduction.
+ * Replaces: csrc/bindings.cpp:311-339, csrc/kernels/gemv_sparse_accumulate.cu:10-47. */
+int soinfer_gemv_w4a16_sparse_accumulate(const uint8_t* Wq_sel, const float* scale_sel,
+                                         const soinfer_half* h, soinfer_half* y, int64_t H, int64_t k,
+                                         int64_t group_size, int64_t num_groups, void* workspace,
+                                         int64_t workspace_bytes, void* stream);
+
+/* Row-indirect form of the sparse 'down' GEMV over a resident transposed
+ * matrix: row j of the sum is Wq_T[rows[j]] with scale_T[rows[j]].
+ * Bit-identical to gathering those rows and calling
+ * soinfer_gemv_w4a16_sparse_accumulate.  rows: int32 [k] in [0, I). */
+int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, int64_t I,
+                                   const int32_t* rows, const soinfer_half* h, soinfer_half* y,
+                                   int64_t H, int64_t k, int64_t group_size, int64_t num_groups,
+                                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Cache-or-stream 'down' direction: same as the sparse accumulate with each
+ * row resolved through desc (see soinfer_gemv_dip_fused_up).  Bit-identical
+ * to soinfer_gemv_w4a16_sparse_accumulate on the same logical rows.
+ * Replaces: csrc/bindings.cpp:410-432, csrc/kernels/gemv_dip_fused.cu:116-164. */
+int soinfer_gemv_dip_fused_down(const uint8_t* cache_Wq, const float* cache_scale, int64_t C,
+                                const uint8_t* staging_Wq, const float* staging_scale, int64_t M,
+                                const int32_t* desc, const soinfer_half* h, soinfer_half* y, int64_t H,
+                                int64_t k, int64_t group_size, int64_t num_groups, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------- gathers --- */
+
+/* Copies rows indices[0..k) of a pinned host matrix [num_rows, row_nbytes]
+ * into pinned staging (host memcpy, multi-threaded for large k), then one
+ * cudaMemcpyAsync of k*row_nbytes bytes to gpu_dst on `stream`.  Byte-exact.
+ * indices: int64 host; staging: pinned host >= k*row_nbytes bytes.  The host
+ * copy is complete on return; the H2D copy is asynchronous.
+ * Replaces: csrc/bindings.cpp:538-549, csrc/kernels/gather_rows.cu:6-13. */
+int soinfer_gather_rows_staged(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
+                               const int64_t* indices, int64_t k, uint8_t* staging,
+                               int64_t staging_bytes, uint8_t* gpu_dst, int64_t dst_bytes, void* stream);
+
+/* One cudaMemcpyAsync per selected row straight from the pinned matrix.
+ * Replaces: csrc/bindings.cpp:551-559, csrc/kernels/gather_rows.cu:15-21. */
+int soinfer_gather_rows_naive(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
+                              const int64_t* indices, int64_t k, uint8_t* gpu_dst, int64_t dst_bytes,
+                              void* stream);
+
+/* Device-driven gather: an SM kernel copies rows rows[0..k) (int32, device
+ * memory) of `matrix` into gpu_dst.  `matrix` may be device memory or pinned
+ * host memory mapped into the device address space (zero-copy over PCIe), so
+ * the selection never has to visit the host.  No reference counterpart (the
+ * reference gathers on the host after an index download, generate.py:282). */
+int soinfer_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
+                               const int32_t* rows, int64_t k, uint8_t* gpu_dst, void* stream);
+
+/* ---------------------------------------------- attention-side glue ------ */
+
+/* out[r, :] = fp16( x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * weight ), fp32 math.
+ * x, out: fp16 [rows, hidden]; weight: fp16 [hidden]; hidden even.
+ * Replaces: csrc/bindings.cpp:141-152, csrc/kernels/rmsnorm.cu:9-48. */
+int soinfer_rmsnorm(const soinfer_half* x, const soinfer_half* weight, soinfer_half* out, int64_t rows,
+                    int64_t hidden, float eps, void* stream);
+
+/* Rotate-half RoPE in place on x: fp16 [num_heads, head_dim]; cos/sin: fp32
+ * [head_dim/2].  Replaces: csrc/bindings.cpp:490-505, csrc/kernels/rope.cu:5-25. */
+int soinfer_rope_apply(soinfer_half* x, const float* cos_vals, const float* sin_vals, int64_t num_heads,
+                       int64_t head_dim, void* stream);
+
+/* k_cache/v_cache: fp16 [num_kv_heads, max_seq_len, head_dim]; k_new/v_new:
+ * fp16 [num_kv_heads, head_dim] written at position pos (0 <= pos < max_seq_len).
+ * Replaces: csrc/bindings.cpp:450-466, csrc/kernels/kv_cache.cu:7-27. */
+int soinfer_kv_cache_append(soinfer_half* k_cache, soinfer_half* v_cache, const soinfer_half* k_new,
+                            const soinfer_half* v_new, int64_t num_kv_heads, int64_t max_seq_len,
+                            int64_t head_dim, int64_t pos, void* stream);
+
+/* Bytes of device workspace soinfer_decode_attention needs (split-KV partials). */
+int64_t soinfer_decode_attention_workspace_bytes(int64_t num_q_heads, int64_t max_seq_len,
+                                                 int64_t head_dim);
+
+/* Single-query GQA attention: q fp16 [NQ, hd]; caches fp16 [NKV, max_seq, hd];
+ * query head h reads kv head h / (NQ/NKV); scale 1/sqrt(hd); softmax in fp32
+ * over positions [0, cur_len); out fp16 [NQ, hd].  head_dim must be a
+ * multiple of 8 and at most 256.
+ * Replaces: csrc/bindings.cpp:468-488, csrc/kernels/decode_attention.cu:17-63. */
+int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
+                             const soinfer_half* v_cache, soinfer_half* out, int64_t num_q_heads,
+                             int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim, int64_t cur_len,
+                             void* workspace, int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* SOINFER_B200_H_ */

@@ -1,0 +1,272 @@
+// Single-query GQA decode attention over a contiguous fp16 KV cache.
+//
+// Reference semantics (csrc/kernels/decode_attention.cu:17-55): query head qh
+// reads kv head qh / (NQ/NKV); scores q.k * (1/sqrt(hd)); online softmax in
+// fp32; out = fp16(sum p v / sum p).  The reference runs one CTA per query
+// head with a block-wide reduction and two __syncthreads per cached position,
+// re-reading K/V once per query head.
+//
+// Here (split-KV / flash-decoding): CTA (kv head, position split, head group)
+// reads each K and V row of its split exactly once with 16-byte loads and
+// serves all REP query heads of the group from registers.  A team of hd/8
+// lanes owns one position (8 dims per lane); scores go to shared memory in
+// the log2 domain, the split's max / exp2 / sum are taken per head, V rows are
+// accumulated in fp32, and the split writes (m, l, acc[hd]) to the workspace.
+// A combine kernel rescales and sums the splits in a fixed order.  With a
+// single split the CTA writes the output directly.
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+
+namespace soinfer {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kMaxSplits = 64;
+constexpr int kTargetCtas = 296;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int TEAM, int REP>
+__global__ void __launch_bounds__(kThreads)
+    attn_split_kernel(const half* __restrict__ q, const half* __restrict__ kc, const half* __restrict__ vc,
+                      half* __restrict__ out, float* __restrict__ ws_acc, float* __restrict__ ws_ml, const int nq,
+                      const int nkv, const int64_t max_seq, const int hd, const int cur_len, const int L,
+                      const float scale_log2) {
+  constexpr int kTeams = kThreads / TEAM;
+  extern __shared__ float smem[];
+  float* s_p = smem;                        // [REP][L] scores, then probabilities
+  float* s_red = smem + REP * L;            // [kTeams][REP][hd]
+  __shared__ float s_m[REP], s_l[REP];
+
+  const int kvh = blockIdx.x;
+  const int split = blockIdx.y;
+  const int nsplit = gridDim.y;
+  const int n_rep = nq / nkv;
+  const int qh0 = kvh * n_rep + blockIdx.z * REP;
+  const int t0 = split * L;
+  const int t1 = (t0 + L < cur_len) ? t0 + L : cur_len;
+  const int team = threadIdx.x / TEAM;
+  const int tl = threadIdx.x % TEAM;
+  const int d0 = tl * 8;
+  const bool lane_on = d0 < hd;
+  const half* kb = kc + (int64_t)kvh * max_seq * hd;
+  const half* vb = vc + (int64_t)kvh * max_seq * hd;
+
+  pdl_launch_dependents();
+  pdl_wait();
+
+  float qf[REP][8];
+#pragma unroll
+  for (int h = 0; h < REP; ++h) {
+    if (lane_on) {
+      const uint4 u = *reinterpret_cast<const uint4*>(q + (int64_t)(qh0 + h) * hd + d0);
+      const half2* p = reinterpret_cast<const half2*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(p[i]);
+        qf[h][2 * i] = f.x;
+        qf[h][2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qf[h][i] = 0.f;
+    }
+  }
+
+  // phase A: scores (trip count uniform across the warp: the team shuffles
+  // below need every lane)
+  for (int tb = t0; tb < t1; tb += kTeams) {
+    const int t = tb + team;
+    const bool pos_on = t < t1;
+    float kf[8];
+    if (lane_on && pos_on) {
+      const uint4 u = ldg_stream_u4(kb + (int64_t)t * hd + d0);
+      const half2* p = reinterpret_cast<const half2*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(p[i]);
+        kf[2 * i] = f.x;
+        kf[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kf[i] = 0.f;
+    }
+#pragma unroll
+    for (int h = 0; h < REP; ++h) {
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dot = fmaf(qf[h][i], kf[i], dot);
+#pragma unroll
+      for (int o = TEAM / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (tl == 0 && pos_on) s_p[h * L + (t - t0)] = dot * scale_log2;
+    }
+  }
+  __syncthreads();
+
+  // phase B: per-head max, exp2, sum over the split
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_pos = t1 - t0;
+  for (int h = warp; h < REP; h += kThreads / 32) {
+    float m = -INFINITY;
+    for (int i = lane; i < n_pos; i += 32) m = fmaxf(m, s_p[h * L + i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int i = lane; i < n_pos; i += 32) {
+      const float p = exp2f(s_p[h * L + i] - m);
+      s_p[h * L + i] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      s_m[h] = m;
+      s_l[h] = l;
+    }
+  }
+  __syncthreads();
+
+  // phase C: acc = sum p v
+  float acc[REP][8];
+#pragma unroll
+  for (int h = 0; h < REP; ++h)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[h][i] = 0.f;
+  for (int t = t0 + team; t < t1; t += kTeams) {
+    if (!lane_on) continue;
+    const uint4 u = ldg_stream_u4(vb + (int64_t)t * hd + d0);
+    const half2* p = reinterpret_cast<const half2*>(&u);
+    float vf[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(p[i]);
+      vf[2 * i] = f.x;
+      vf[2 * i + 1] = f.y;
+    }
+#pragma unroll
+    for (int h = 0; h < REP; ++h) {
+      const float pr = s_p[h * L + (t - t0)];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[h][i] = fmaf(pr, vf[i], acc[h][i]);
+    }
+  }
+  if (lane_on) {
+#pragma unroll
+    for (int h = 0; h < REP; ++h)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s_red[(team * REP + h) * hd + d0 + i] = acc[h][i];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < REP * hd; e += kThreads) {
+    const int h = e / hd, d = e - h * hd;
+    float sum = 0.f;
+    for (int tm = 0; tm < kTeams; ++tm) sum += s_red[(tm * REP + h) * hd + d];
+    const int qh = qh0 + h;
+    if (nsplit == 1) {
+      out[(int64_t)qh * hd + d] = __float2half_rn(sum / s_l[h]);
+    } else {
+      ws_acc[((int64_t)qh * kMaxSplits + split) * hd + d] = sum;
+      if (d == 0) {
+        ws_ml[((int64_t)qh * kMaxSplits + split) * 2 + 0] = s_m[h];
+        ws_ml[((int64_t)qh * kMaxSplits + split) * 2 + 1] = s_l[h];
+      }
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
+                                    half* __restrict__ out, const int hd, const int nsplit) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int qh = blockIdx.x;
+  const float* ml = ws_ml + (int64_t)qh * kMaxSplits * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = exp2f(ml[2 * s] - M);
+      num = fmaf(w, ws_acc[((int64_t)qh * kMaxSplits + s) * hd + d], num);
+      den = fmaf(w, ml[2 * s + 1], den);
+    }
+    out[(int64_t)qh * hd + d] = __float2half_rn(num / den);
+  }
+}
+
+template <int TEAM, int REP>
+cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* out, float* ws_acc, float* ws_ml,
+                         int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L, float scale_log2,
+                         int groups, cudaStream_t stream) {
+  constexpr int kTeams = kThreads / TEAM;
+  const size_t smem = (size_t)(REP * L + kTeams * REP * hd) * sizeof(float);
+  auto kernel = attn_split_kernel<TEAM, REP>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_ex(kernel, dim3(nkv, nsplit, groups), dim3(kThreads), smem, stream, 1, false, q, kc, vc, out, ws_acc,
+                   ws_ml, nq, nkv, max_seq, hd, cur_len, L, scale_log2);
+}
+
+template <int TEAM>
+cudaError_t dispatch_rep(int rep, const half* q, const half* kc, const half* vc, half* out, float* ws_acc,
+                         float* ws_ml, int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L,
+                         float sl2, int groups, cudaStream_t st) {
+  switch (rep) {
+    case 1: return launch_split<TEAM, 1>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+    case 2: return launch_split<TEAM, 2>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+    case 4: return launch_split<TEAM, 4>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+    case 5: return launch_split<TEAM, 5>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+    case 8: return launch_split<TEAM, 8>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+int64_t attention_workspace_bytes(int64_t nq, int64_t max_seq, int64_t hd) {
+  (void)max_seq;
+  return nq * kMaxSplits * (hd + 2) * (int64_t)sizeof(float);
+}
+
+cudaError_t launch_decode_attention(const half* q, const half* kc, const half* vc, half* out, int64_t nq, int64_t nkv,
+                                    int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
+                                    cudaStream_t stream) {
+  const int n_rep = (int)(nq / nkv);
+  int rep;
+  if (n_rep == 1 || n_rep == 2 || n_rep == 4 || n_rep == 5 || n_rep == 8)
+    rep = n_rep;
+  else if (n_rep % 4 == 0)
+    rep = 4;
+  else if (n_rep % 2 == 0)
+    rep = 2;
+  else
+    rep = 1;
+  const int groups = n_rep / rep;
+  int64_t want = (kTargetCtas + nkv * groups - 1) / (nkv * groups);
+  if (want > kMaxSplits) want = kMaxSplits;
+  const int64_t by_len = (cur_len + 15) / 16;
+  if (want > by_len) want = by_len;
+  if (want < 1) want = 1;
+  const int L = (int)((cur_len + want - 1) / want);
+  const int nsplit = (int)((cur_len + L - 1) / L);
+  float* ws_acc = reinterpret_cast<float*>(workspace);
+  float* ws_ml = ws_acc + nq * kMaxSplits * hd;
+  const float sl2 = (1.0f / sqrtf((float)hd)) * kLog2e;
+  const int chunks = (int)((hd + 7) / 8);
+  int team = 4;
+  while (team < chunks) team <<= 1;
+  cudaError_t e;
+  const int inq = (int)nq, inkv = (int)nkv, ihd = (int)hd, icl = (int)cur_len;
+  switch (team) {
+    case 4: e = dispatch_rep<4>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
+    case 8: e = dispatch_rep<8>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
+    case 16: e = dispatch_rep<16>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
+    case 32: e = dispatch_rep<32>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess || nsplit == 1) return e;
+  const int threads = ihd < 32 ? 32 : (ihd > 256 ? 256 : ihd);
+  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, false, ws_acc, ws_ml, out, ihd, nsplit);
+}
+
+}  // namespace soinfer

@@ -1,0 +1,365 @@
+// C ABI entry points (include/soinfer_b200.h): argument validation with the
+// reference binding's preconditions (csrc/bindings.cpp:176-559), then the
+// sm_100a launchers.  Nothing here aborts; failures return a status and set
+// the thread's last-error message.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/soinfer_b200.h"
+#include "capi_util.h"
+#include "kernels.h"
+
+namespace soinfer {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_result(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SOINFER_OK;
+  (void)cudaGetLastError();  // clear a non-sticky launch error
+  return set_error(SOINFER_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+const char* last_error() { return g_last_error.c_str(); }
+
+}  // namespace soinfer
+
+using namespace soinfer;
+
+#define REQUIRE(cond, ...)                                               \
+  do {                                                                   \
+    if (!(cond)) return set_error(SOINFER_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+  } while (0)
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline const half* as_half(const soinfer_half* p) { return reinterpret_cast<const half*>(p); }
+inline half* as_half(soinfer_half* p) { return reinterpret_cast<half*>(p); }
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t int4_row_bytes(int64_t K) { return cdiv(K, 8) * 4; }
+
+int check_int4_layout(const char* name, int64_t K, int64_t group_size, int64_t num_groups) {
+  REQUIRE(K >= 1, "%s: K must be >= 1", name);
+  REQUIRE(group_size >= 1 && group_size % 8 == 0, "%s: group_size must be a positive multiple of 8", name);
+  REQUIRE(num_groups == cdiv(K, group_size),
+          "%s: scale's num_groups must be ceil(K/group_size) for the given K and group_size, got %lld but expected %lld",
+          name, (long long)num_groups, (long long)cdiv(K, group_size));
+  return SOINFER_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int soinfer_abi_version(void) { return 1; }
+
+const char* soinfer_last_error(void) { return soinfer::last_error(); }
+
+const char* soinfer_status_string(int status) {
+  switch (status) {
+    case SOINFER_OK: return "SOINFER_OK";
+    case SOINFER_ERR_INVALID_ARGUMENT: return "SOINFER_ERR_INVALID_ARGUMENT";
+    case SOINFER_ERR_CUDA: return "SOINFER_ERR_CUDA";
+    case SOINFER_ERR_UNSUPPORTED: return "SOINFER_ERR_UNSUPPORTED";
+    case SOINFER_ERR_HOST: return "SOINFER_ERR_HOST";
+  }
+  return "SOINFER_ERR_UNKNOWN";
+}
+
+static int gemv_w4_plain(const char* name, const uint8_t* Wq, const float* scale, const soinfer_half* x,
+                         soinfer_half* y, int64_t N, int64_t K, int64_t group_size, int64_t num_groups, void* stream,
+                         uint32_t flags = 0) {
+  if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
+  REQUIRE(N >= 0, "%s: N must be >= 0", name);
+  if (N == 0) return SOINFER_OK;
+  REQUIRE(Wq && scale && x && y, "%s: null pointer", name);
+  REQUIRE(aligned(Wq, 4) && aligned(x, 2) && aligned(y, 2) && aligned(scale, 4), "%s: misaligned pointer", name);
+  RowSource src;
+  src.W = Wq;
+  src.S = scale;
+  src.rows1 = N;
+  src.row_bytes = int4_row_bytes(K);
+  src.num_groups = num_groups;
+  LaunchOpts opts;
+  opts.pdl = (flags & SOINFER_FLAG_PDL) != 0;
+  return cuda_result(
+      launch_gemv_w4(RowMode::kPlain, src, as_half(x), as_half(y), N, K, group_size, as_stream(stream), opts), name);
+}
+
+int soinfer_gemv_w4a16_group_ex(const uint8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y,
+                                int64_t N, int64_t K, int64_t group_size, int64_t num_groups, uint32_t flags,
+                                void* stream) {
+  REQUIRE((flags & ~SOINFER_FLAG_PDL) == 0, "gemv_w4a16_group_ex: unknown flags 0x%x", flags);
+  return gemv_w4_plain("gemv_w4a16_group_ex", Wq, scale, x, y, N, K, group_size, num_groups, stream, flags);
+}
+
+int soinfer_gemv_w4a16_group(const uint8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y, int64_t N,
+                             int64_t K, int64_t group_size, int64_t num_groups, void* stream) {
+  return gemv_w4_plain("gemv_w4a16_group", Wq, scale, x, y, N, K, group_size, num_groups, stream);
+}
+
+int soinfer_gemv_w4a16_group_lop3(const uint8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y,
+                                  int64_t N, int64_t K, int64_t group_size, int64_t num_groups, void* stream) {
+  return gemv_w4_plain("gemv_w4a16_group_lop3", Wq, scale, x, y, N, K, group_size, num_groups, stream);
+}
+
+int soinfer_gemv_w4a16_rows(const uint8_t* Wq, const float* scale, int64_t N, const int32_t* rows, int64_t num_sel,
+                            const soinfer_half* x, soinfer_half* y, int64_t K, int64_t group_size, int64_t num_groups,
+                            void* stream) {
+  const char* name = "gemv_w4a16_rows";
+  if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
+  REQUIRE(num_sel >= 0 && N >= 0, "%s: sizes must be >= 0", name);
+  if (num_sel == 0) return SOINFER_OK;
+  REQUIRE(N >= 1, "%s: cannot select rows of an empty matrix", name);
+  REQUIRE(Wq && scale && rows && x && y, "%s: null pointer", name);
+  REQUIRE(aligned(Wq, 4) && aligned(rows, 4) && aligned(scale, 4), "%s: misaligned pointer", name);
+  RowSource src;
+  src.W = Wq;
+  src.S = scale;
+  src.idx = rows;
+  src.rows1 = N;
+  src.row_bytes = int4_row_bytes(K);
+  src.num_groups = num_groups;
+  return cuda_result(
+      launch_gemv_w4(RowMode::kIndexed, src, as_half(x), as_half(y), num_sel, K, group_size, as_stream(stream)), name);
+}
+
+int soinfer_gemv_w8a16(const int8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y, int64_t N,
+                       int64_t K, int64_t group_size, int64_t num_groups, int64_t scale_row_stride, void* stream) {
+  const char* name = "gemv_w8a16";
+  REQUIRE(K >= 1 && N >= 0, "%s: invalid sizes", name);
+  REQUIRE(group_size >= 1, "%s: group_size must be >= 1", name);
+  REQUIRE(num_groups >= 1, "%s: num_groups must be >= 1", name);
+  REQUIRE(num_groups == 1 || group_size % 4 == 0,
+          "%s: group_size must be a multiple of 4 when num_groups > 1 (a 4-byte word never spans two groups)", name);
+  REQUIRE(num_groups == 1 || num_groups == cdiv(K, group_size),
+          "%s: scale's num_groups must be 1 (per-tensor broadcast) or ceil(K/group_size) for the given K and "
+          "group_size, got %lld but expected %lld",
+          name, (long long)num_groups, (long long)cdiv(K, group_size));
+  REQUIRE(scale_row_stride == 0 || scale_row_stride == num_groups, "%s: scale_row_stride must be 0 or num_groups",
+          name);
+  if (N == 0) return SOINFER_OK;
+  REQUIRE(Wq && scale && x && y, "%s: null pointer", name);
+  return cuda_result(launch_gemv_w8(Wq, scale, as_half(x), as_half(y), N, K, group_size, num_groups,
+                                    scale_row_stride, as_stream(stream)),
+                     name);
+}
+
+static int topk_common(const char* name, bool exact, const float* v, int64_t n, int64_t k, int32_t* idx,
+                       int32_t* count, void* stream) {
+  REQUIRE(n >= 1 && n < (1ll << 31), "%s: abs_g must hold 1 .. 2^31-1 values", name);
+  REQUIRE(k >= 1 && k <= n, "%s: k must be in [1, I]", name);
+  REQUIRE(v && idx && count, "%s: null pointer", name);
+  return cuda_result(launch_topk(exact, v, n, k, idx, count, as_stream(stream)), name);
+}
+
+int soinfer_topk_threshold_select(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
+                                  void* stream) {
+  return topk_common("topk_threshold_select", false, abs_g, n, k, out_idx, out_count, stream);
+}
+
+int soinfer_topk_select_exact(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
+                              void* stream) {
+  return topk_common("topk_select_exact", true, abs_g, n, k, out_idx, out_count, stream);
+}
+
+int soinfer_build_dip_descriptors(const int32_t* sel, int64_t k, const int32_t* slot_of, int64_t I, int32_t* desc,
+                                  int32_t* miss, int32_t* miss_count, void* stream) {
+  const char* name = "build_dip_descriptors";
+  REQUIRE(k >= 0 && k < (1ll << 31) && I >= 0 && I < (1ll << 31), "%s: invalid sizes", name);
+  REQUIRE(miss_count, "%s: null miss_count", name);
+  REQUIRE(k == 0 || I >= 1, "%s: slot_of must be non-empty when channels are selected", name);
+  REQUIRE(k == 0 || (sel && slot_of && desc && miss), "%s: null pointer", name);
+  return cuda_result(launch_build_descriptors(sel, k, slot_of, I, desc, miss, miss_count, as_stream(stream)), name);
+}
+
+int soinfer_gemv_dip_fused_up(const uint8_t* cache_Wq, const float* cache_scale, int64_t C, const uint8_t* staging_Wq,
+                              const float* staging_scale, int64_t M, const int32_t* desc, int64_t k,
+                              const soinfer_half* x, soinfer_half* y, int64_t K, int64_t group_size,
+                              int64_t num_groups, void* stream) {
+  const char* name = "gemv_dip_fused_up";
+  if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
+  REQUIRE(C >= 0 && M >= 0 && k >= 0, "%s: sizes must be >= 0", name);
+  if (k == 0) return SOINFER_OK;
+  REQUIRE(C + M >= 1, "%s: descriptors given but both cache and staging are empty", name);
+  REQUIRE(desc && x && y, "%s: null pointer", name);
+  REQUIRE((C == 0 || (cache_Wq && cache_scale)) && (M == 0 || (staging_Wq && staging_scale)), "%s: null row buffer",
+          name);
+  RowSource src;
+  src.W = cache_Wq;
+  src.S = cache_scale;
+  src.W2 = staging_Wq;
+  src.S2 = staging_scale;
+  src.idx = desc;
+  src.rows1 = C;
+  src.rows2 = M;
+  src.row_bytes = int4_row_bytes(K);
+  src.num_groups = num_groups;
+  return cuda_result(launch_gemv_w4(RowMode::kDesc, src, as_half(x), as_half(y), k, K, group_size, as_stream(stream)),
+                     name);
+}
+
+int64_t soinfer_sparse_workspace_bytes(int64_t H, int64_t k) {
+  if (H < 1 || k < 0) return 0;
+  return sparse_workspace_bytes(H, k > 0 ? k : 1);
+}
+
+static int sparse_common(const char* name, RowMode mode, const RowSource& src, const soinfer_half* h, soinfer_half* y,
+                         int64_t H, int64_t k, int64_t group_size, int64_t num_groups, void* ws, int64_t ws_bytes,
+                         void* stream) {
+  if (int st = check_int4_layout(name, H, group_size, num_groups)) return st;
+  REQUIRE(k >= 0, "%s: k must be >= 0", name);
+  REQUIRE(y, "%s: null output", name);
+  if (k == 0) return cuda_result(cudaMemsetAsync(y, 0, (size_t)H * 2, as_stream(stream)), name);
+  REQUIRE(h, "%s: null h", name);
+  REQUIRE(ws && ws_bytes >= sparse_workspace_bytes(H, k), "%s: workspace too small (need %lld bytes)", name,
+          (long long)sparse_workspace_bytes(H, k));
+  REQUIRE(aligned(ws, 16), "%s: workspace must be 16-byte aligned", name);
+  return cuda_result(launch_sparse_down(mode, src, as_half(h), as_half(y), H, k, group_size, ws, as_stream(stream)),
+                     name);
+}
+
+int soinfer_gemv_w4a16_sparse_accumulate(const uint8_t* Wq_sel, const float* scale_sel, const soinfer_half* h,
+                                         soinfer_half* y, int64_t H, int64_t k, int64_t group_size, int64_t num_groups,
+                                         void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_w4a16_sparse_accumulate";
+  REQUIRE(k == 0 || (Wq_sel && scale_sel), "%s: null pointer", name);
+  REQUIRE(aligned(Wq_sel, 4), "%s: misaligned weights", name);
+  RowSource src;
+  src.W = Wq_sel;
+  src.S = scale_sel;
+  src.rows1 = k;
+  src.row_bytes = int4_row_bytes(H);
+  src.num_groups = num_groups;
+  return sparse_common(name, RowMode::kPlain, src, h, y, H, k, group_size, num_groups, workspace, workspace_bytes,
+                       stream);
+}
+
+int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, int64_t I, const int32_t* rows,
+                                   const soinfer_half* h, soinfer_half* y, int64_t H, int64_t k, int64_t group_size,
+                                   int64_t num_groups, void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_w4a16_sparse_rows";
+  REQUIRE(k == 0 || (I >= 1 && Wq_T && scale_T && rows), "%s: null pointer or empty matrix", name);
+  REQUIRE(aligned(Wq_T, 4), "%s: misaligned weights", name);
+  RowSource src;
+  src.W = Wq_T;
+  src.S = scale_T;
+  src.idx = rows;
+  src.rows1 = I;
+  src.row_bytes = int4_row_bytes(H);
+  src.num_groups = num_groups;
+  return sparse_common(name, RowMode::kIndexed, src, h, y, H, k, group_size, num_groups, workspace, workspace_bytes,
+                       stream);
+}
+
+int soinfer_gemv_dip_fused_down(const uint8_t* cache_Wq, const float* cache_scale, int64_t C,
+                                const uint8_t* staging_Wq, const float* staging_scale, int64_t M, const int32_t* desc,
+                                const soinfer_half* h, soinfer_half* y, int64_t H, int64_t k, int64_t group_size,
+                                int64_t num_groups, void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_dip_fused_down";
+  REQUIRE(C >= 0 && M >= 0, "%s: sizes must be >= 0", name);
+  REQUIRE(k == 0 || (C + M >= 1 && desc), "%s: descriptors given but both cache and staging are empty", name);
+  REQUIRE((C == 0 || (cache_Wq && cache_scale)) && (M == 0 || (staging_Wq && staging_scale)), "%s: null row buffer",
+          name);
+  REQUIRE(aligned(cache_Wq, 4) && aligned(staging_Wq, 4), "%s: misaligned weights", name);
+  RowSource src;
+  src.W = cache_Wq;
+  src.S = cache_scale;
+  src.W2 = staging_Wq;
+  src.S2 = staging_scale;
+  src.idx = desc;
+  src.rows1 = C;
+  src.rows2 = M;
+  src.row_bytes = int4_row_bytes(H);
+  src.num_groups = num_groups;
+  return sparse_common(name, RowMode::kDesc, src, h, y, H, k, group_size, num_groups, workspace, workspace_bytes,
+                       stream);
+}
+
+int soinfer_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes, const int32_t* rows,
+                               int64_t k, uint8_t* gpu_dst, void* stream) {
+  const char* name = "gather_rows_device";
+  REQUIRE(num_rows >= 0 && row_nbytes >= 0 && k >= 0, "%s: sizes must be >= 0", name);
+  if (k == 0 || row_nbytes == 0) return SOINFER_OK;
+  REQUIRE(num_rows >= 1 && matrix && rows && gpu_dst, "%s: null pointer or empty matrix", name);
+  return cuda_result(launch_gather_rows_device(matrix, num_rows, row_nbytes, rows, k, gpu_dst, as_stream(stream)),
+                     name);
+}
+
+int soinfer_rmsnorm(const soinfer_half* x, const soinfer_half* weight, soinfer_half* out, int64_t rows, int64_t hidden,
+                    float eps, void* stream) {
+  const char* name = "rmsnorm";
+  REQUIRE(rows >= 0 && rows < (1ll << 31), "%s: invalid rows", name);
+  REQUIRE(hidden >= 2 && hidden % 2 == 0, "%s: hidden dim must be even (half2 vectorization)", name);
+  if (rows == 0) return SOINFER_OK;
+  REQUIRE(x && weight && out, "%s: null pointer", name);
+  REQUIRE(aligned(x, 4) && aligned(weight, 4) && aligned(out, 4), "%s: misaligned pointer", name);
+  return cuda_result(launch_rmsnorm(as_half(x), as_half(weight), as_half(out), rows, hidden, eps, as_stream(stream)),
+                     name);
+}
+
+int soinfer_rope_apply(soinfer_half* x, const float* cos_vals, const float* sin_vals, int64_t num_heads,
+                       int64_t head_dim, void* stream) {
+  const char* name = "rope_apply";
+  REQUIRE(num_heads >= 0 && num_heads < (1ll << 31), "%s: invalid num_heads", name);
+  REQUIRE(head_dim >= 2 && head_dim % 2 == 0, "%s: head_dim must be even", name);
+  if (num_heads == 0) return SOINFER_OK;
+  REQUIRE(x && cos_vals && sin_vals, "%s: null pointer", name);
+  return cuda_result(launch_rope(as_half(x), cos_vals, sin_vals, num_heads, head_dim, as_stream(stream)), name);
+}
+
+int soinfer_kv_cache_append(soinfer_half* k_cache, soinfer_half* v_cache, const soinfer_half* k_new,
+                            const soinfer_half* v_new, int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim,
+                            int64_t pos, void* stream) {
+  const char* name = "kv_cache_append";
+  REQUIRE(num_kv_heads >= 0 && max_seq_len >= 1 && head_dim >= 1, "%s: invalid cache shape", name);
+  REQUIRE(pos >= 0 && pos < max_seq_len, "%s: pos out of range for max_seq_len", name);
+  if (num_kv_heads == 0) return SOINFER_OK;
+  REQUIRE(k_cache && v_cache && k_new && v_new, "%s: null pointer", name);
+  return cuda_result(launch_kv_append(as_half(k_cache), as_half(v_cache), as_half(k_new), as_half(v_new), num_kv_heads,
+                                      max_seq_len, head_dim, pos, as_stream(stream)),
+                     name);
+}
+
+int64_t soinfer_decode_attention_workspace_bytes(int64_t num_q_heads, int64_t max_seq_len, int64_t head_dim) {
+  if (num_q_heads < 1 || head_dim < 1) return 0;
+  return attention_workspace_bytes(num_q_heads, max_seq_len, head_dim);
+}
+
+int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache, const soinfer_half* v_cache,
+                             soinfer_half* out, int64_t num_q_heads, int64_t num_kv_heads, int64_t max_seq_len,
+                             int64_t head_dim, int64_t cur_len, void* workspace, int64_t workspace_bytes,
+                             void* stream) {
+  const char* name = "decode_attention";
+  REQUIRE(num_kv_heads >= 1 && num_q_heads >= 1, "%s: head counts must be >= 1", name);
+  REQUIRE(num_q_heads % num_kv_heads == 0, "%s: num_q_heads must be a multiple of num_kv_heads", name);
+  REQUIRE(head_dim >= 8 && head_dim % 8 == 0 && head_dim <= 256, "%s: head_dim must be a multiple of 8 in [8, 256]",
+          name);
+  REQUIRE(cur_len >= 1 && cur_len <= max_seq_len, "%s: cur_len out of range for max_seq_len", name);
+  REQUIRE(num_q_heads < (1 << 20) && max_seq_len < (1ll << 31), "%s: sizes too large", name);
+  REQUIRE(q && k_cache && v_cache && out, "%s: null pointer", name);
+  REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16), "%s: q and caches must be 16-byte aligned",
+          name);
+  REQUIRE(workspace && workspace_bytes >= attention_workspace_bytes(num_q_heads, max_seq_len, head_dim),
+          "%s: workspace too small", name);
+  return cuda_result(launch_decode_attention(as_half(q), as_half(k_cache), as_half(v_cache), as_half(out), num_q_heads,
+                                             num_kv_heads, max_seq_len, head_dim, cur_len, workspace,
+                                             as_stream(stream)),
+                     name);
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// Internal launcher interface between the C ABI (capi.cu) and the kernels.
+// Launchers validate nothing (capi.cu does) and return the launch status.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace soinfer {
+
+// How a logical output row of an INT4 GEMV finds its packed bytes and scales.
+enum class RowMode : int { kPlain = 0, kIndexed = 1, kDesc = 2 };
+
+struct RowSource {
+  const uint8_t* W = nullptr;   // plain rows / indexed matrix / hot-cache rows
+  const float* S = nullptr;
+  const uint8_t* W2 = nullptr;  // staging rows (descriptor mode)
+  const float* S2 = nullptr;
+  const int32_t* idx = nullptr; // row indices (indexed) or descriptors (desc)
+  int64_t rows1 = 0;            // rows available behind W/S (bounds clamp)
+  int64_t rows2 = 0;            // rows available behind W2/S2
+  int64_t row_bytes = 0;        // packed bytes per row = ceil(K/8)*4
+  int64_t num_groups = 0;       // scale columns per row
+};
+
+struct LaunchOpts {
+  bool pdl = false;  // programmatic dependent launch (weights not produced by the previous kernel)
+};
+
+// y[r] = dot(row r of src, x) for r < nrows (INT4, AWQ order, fp32 accumulation).
+cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, half* y, int64_t nrows,
+                           int64_t K, int64_t group_size, cudaStream_t stream, LaunchOpts opts = {});
+
+// INT8 GEMV (per-tensor / per-channel / grouped scales).
+cudaError_t launch_gemv_w8(const int8_t* Wq, const float* scale, const half* x, half* y, int64_t N,
+                           int64_t K, int64_t group_size, int64_t num_groups, int64_t scale_row_stride,
+                           cudaStream_t stream, LaunchOpts opts = {});
+
+// Sparse 'down' accumulate: y[c] = sum_j h[j] * scale(j, c/g) * q(j, c).
+int64_t sparse_workspace_bytes(int64_t H, int64_t k);
+cudaError_t launch_sparse_down(RowMode mode, const RowSource& src, const half* h, half* y, int64_t H,
+                               int64_t k, int64_t group_size, void* workspace, cudaStream_t stream,
+                               LaunchOpts opts = {});
+
+// Selectors.
+cudaError_t launch_topk(bool exact, const float* v, int64_t n, int64_t k, int32_t* out_idx,
+                        int32_t* out_count, cudaStream_t stream);
+cudaError_t launch_build_descriptors(const int32_t* sel, int64_t k, const int32_t* slot_of, int64_t I,
+                                     int32_t* desc, int32_t* miss, int32_t* miss_count, cudaStream_t stream);
+
+// Gathers.
+cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
+                                      const int32_t* rows, int64_t k, uint8_t* dst, cudaStream_t stream);
+
+// Attention-side glue.
+cudaError_t launch_rmsnorm(const half* x, const half* w, half* out, int64_t rows, int64_t hidden, float eps,
+                           cudaStream_t stream);
+cudaError_t launch_rope(half* x, const float* cos_v, const float* sin_v, int64_t heads, int64_t head_dim,
+                        cudaStream_t stream);
+cudaError_t launch_kv_append(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
+                             int64_t hd, int64_t pos, cudaStream_t stream);
+int64_t attention_workspace_bytes(int64_t nq, int64_t max_seq, int64_t hd);
+cudaError_t launch_decode_attention(const half* q, const half* kc, const half* vc, half* out, int64_t nq,
+                                    int64_t nkv, int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
+                                    cudaStream_t stream);
+
+}  // namespace soinfer

@@ -1,0 +1,237 @@
+// Sparse 'down' GEMV over k selected rows of the transposed down_proj:
+//   y[c] = fp16( sum_{j<k} (h[j] * scale[j, c/g]) * q[j, c] )
+// (reference csrc/kernels/gemv_sparse_accumulate.cu:10-38 and the
+// descriptor-sourced csrc/kernels/gemv_dip_fused.cu:116-154, which run one
+// thread per output column serially over j -- 8 CTAs at H=2048).
+//
+// Here the k rows are split into row slabs and the H columns into column
+// slabs; each thread owns a 32-column (16-byte) slice of a row and walks the
+// slab's rows with a fixed stride, so every row is read exactly once with
+// fully coalesced 128-bit loads.  Each value is converted to fp32 exactly
+// without a conversion instruction: OR-ing nibble n (at bit offset p) under
+// the exponent of 2^23 gives 2^23 + n*2^p, and one FADD removes the bias,
+// leaving s*2^p; the FFMA then uses the coefficient pre-scaled by 2^-p, so
+// the product equals coef*s exactly, as in the reference's fp32 expression.
+// Partials: per-thread registers -> fixed-order shared-memory reduction over
+// the CTA's row phases -> one fp32 partial row per (row slab, column slab)
+// in the workspace -> the last CTA of each column slab (atomic ticket) sums
+// the slab partials in row-slab order.  The reduction order depends only on
+// (H, k), never on which buffer a row came from, so cache / staging /
+// indexed / plain sources give bit-identical outputs.
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+
+namespace soinfer {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kColChunks = 8;            // 16-byte column chunks per column slab (256 columns)
+constexpr int kPhases = kThreads / kColChunks;
+constexpr int kTargetCtas = 296;
+constexpr int64_t kCounterBytes = 4096;  // room for 1024 column-slab tickets
+
+struct DownShape {
+  int64_t H, k;
+  int vec;         // 4: 16-byte chunks of 32 columns; 1: 4-byte chunks of 8 columns
+  int64_t chunks;  // column chunks per row
+  int64_t col_slabs, row_slabs, rows_per_slab;
+};
+
+DownShape down_shape(int64_t H, int64_t k, bool vec4) {
+  DownShape s;
+  s.H = H;
+  s.k = k;
+  s.vec = vec4 ? 4 : 1;
+  s.chunks = vec4 ? H / 32 : (H + 7) / 8;
+  s.col_slabs = (s.chunks + kColChunks - 1) / kColChunks;
+  int64_t want_rows = (kTargetCtas + s.col_slabs - 1) / s.col_slabs;
+  if (want_rows < 1) want_rows = 1;
+  s.rows_per_slab = (k + want_rows - 1) / want_rows;
+  if (s.rows_per_slab < kPhases) s.rows_per_slab = kPhases < k ? kPhases : k;
+  if (s.rows_per_slab < 1) s.rows_per_slab = 1;
+  s.row_slabs = (k + s.rows_per_slab - 1) / s.rows_per_slab;
+  return s;
+}
+
+template <RowMode M>
+__device__ __forceinline__ void down_row(const RowSource& src, int64_t j, const uint8_t*& w, const float*& s) {
+  if constexpr (M == RowMode::kPlain) {
+    w = src.W + j * src.row_bytes;
+    s = src.S + j * src.num_groups;
+  } else if constexpr (M == RowMode::kIndexed) {
+    int64_t r = src.idx[j];
+    r = r < 0 ? 0 : (r >= src.rows1 ? src.rows1 - 1 : r);
+    w = src.W + r * src.row_bytes;
+    s = src.S + r * src.num_groups;
+  } else {
+    const int32_t d = src.idx[j];
+    const bool staging = (desc_is_staging(d) && src.rows2 > 0) || src.rows1 == 0;
+    int64_t r = desc_offset(d);
+    const int64_t rows = staging ? src.rows2 : src.rows1;
+    r = r >= rows ? rows - 1 : r;
+    w = (staging ? src.W2 : src.W) + r * src.row_bytes;
+    s = (staging ? src.S2 : src.S) + r * src.num_groups;
+  }
+}
+
+// acc[8] += coef * values of word w (logical K order v0..v7).
+__device__ __forceinline__ void fma_word(uint32_t w, const float c[5], float* acc) {
+  // nibble slots 0..4 sit at bit offsets 0,4,8,12,16; slots 5..7 are brought
+  // to offsets 8,12,16 by w >> 12.  slot -> logical index: 0,2,4,6,1,3,5,7.
+  const uint32_t top = w >> 12;
+  const float f0 = __uint_as_float(lop3_and_xor(w, 0x0000000fu, 0x4b000008u)) - 8388616.0f;         // v0
+  const float f1 = __uint_as_float(lop3_and_xor(w, 0x000000f0u, 0x4b000080u)) - 8388736.0f;         // v2 *16
+  const float f2 = __uint_as_float(lop3_and_xor(w, 0x00000f00u, 0x4b000800u)) - 8390656.0f;         // v4 *256
+  const float f3 = __uint_as_float(lop3_and_xor(w, 0x0000f000u, 0x4b008000u)) - 8421376.0f;         // v6 *4096
+  const float f4 = __uint_as_float(lop3_and_xor(w, 0x000f0000u, 0x4b080000u)) - 8912896.0f;         // v1 *65536
+  const float f5 = __uint_as_float(lop3_and_xor(top, 0x00000f00u, 0x4b000800u)) - 8390656.0f;       // v3 *256
+  const float f6 = __uint_as_float(lop3_and_xor(top, 0x0000f000u, 0x4b008000u)) - 8421376.0f;       // v5 *4096
+  const float f7 = __uint_as_float(lop3_and_xor(top, 0x000f0000u, 0x4b080000u)) - 8912896.0f;       // v7 *65536
+  acc[0] = fmaf(c[0], f0, acc[0]);
+  acc[1] = fmaf(c[4], f4, acc[1]);
+  acc[2] = fmaf(c[1], f1, acc[2]);
+  acc[3] = fmaf(c[2], f5, acc[3]);
+  acc[4] = fmaf(c[2], f2, acc[4]);
+  acc[5] = fmaf(c[3], f6, acc[5]);
+  acc[6] = fmaf(c[3], f3, acc[6]);
+  acc[7] = fmaf(c[4], f7, acc[7]);
+}
+
+template <RowMode M, int VEC>
+__global__ void __launch_bounds__(kThreads)
+    sparse_down_kernel(const RowSource src, const half* __restrict__ h, half* __restrict__ y, const int64_t H,
+                       const int64_t k, const int64_t gsz, const int64_t chunks, const int64_t rows_per_slab,
+                       float* __restrict__ partials, int* __restrict__ tickets) {
+  constexpr int kCols = VEC * 8;  // columns per chunk
+  extern __shared__ float red[];  // [kPhases][kColChunks * kCols]
+  __shared__ int is_last;
+
+  const int cl = threadIdx.x % kColChunks;
+  const int phase = threadIdx.x / kColChunks;
+  const int64_t col_slab = blockIdx.x;
+  const int64_t row_slab = blockIdx.y;
+  const int64_t chunk = col_slab * kColChunks + cl;
+  const bool active = chunk < chunks;
+  const int64_t j0 = row_slab * rows_per_slab;
+  const int64_t j1 = (j0 + rows_per_slab < k) ? j0 + rows_per_slab : k;
+  const int64_t col0 = chunk * kCols;
+  const int64_t grp = active ? col0 / gsz : 0;  // g % kCols == 0 on the vector path
+
+  pdl_launch_dependents();
+  pdl_wait();  // h and the row indices come from preceding kernels
+
+  float acc[kCols];
+#pragma unroll
+  for (int i = 0; i < kCols; ++i) acc[i] = 0.f;
+
+  if (active) {
+    for (int64_t j = j0 + phase; j < j1; j += kPhases) {
+      const uint8_t* w;
+      const float* s;
+      down_row<M>(src, j, w, s);
+      const float hj = __half2float(h[j]);
+      if constexpr (VEC == 4) {
+        const uint4 q = ldg_stream_u4(w + chunk * 16);
+        float c[5];
+        c[0] = hj * __ldg(s + grp);
+        c[1] = c[0] * 0.0625f;
+        c[2] = c[0] * 0.00390625f;
+        c[3] = c[0] * 0.000244140625f;
+        c[4] = c[0] * 0.0000152587890625f;
+        fma_word(q.x, c, acc + 0);
+        fma_word(q.y, c, acc + 8);
+        fma_word(q.z, c, acc + 16);
+        fma_word(q.w, c, acc + 24);
+      } else {
+        const uint32_t q = ldg_stream_u32(w + chunk * 4);
+        float c[5];
+        c[0] = hj * __ldg(s + col0 / gsz);
+        c[1] = c[0] * 0.0625f;
+        c[2] = c[0] * 0.00390625f;
+        c[3] = c[0] * 0.000244140625f;
+        c[4] = c[0] * 0.0000152587890625f;
+        fma_word(q, c, acc);
+      }
+    }
+  }
+
+  // fixed-order reduction over the CTA's row phases
+  constexpr int kSlabCols = kColChunks * kCols;
+#pragma unroll
+  for (int i = 0; i < kCols; ++i) red[phase * kSlabCols + cl * kCols + i] = acc[i];
+  __syncthreads();
+  const int64_t slab_col0 = col_slab * kSlabCols;
+  for (int c = threadIdx.x; c < kSlabCols; c += kThreads) {
+    float sum = 0.f;
+    for (int p = 0; p < kPhases; ++p) sum += red[p * kSlabCols + c];
+    if (slab_col0 + c < H) partials[row_slab * H + slab_col0 + c] = sum;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int ticket = atomicAdd(&tickets[col_slab], 1);
+    is_last = (ticket == (int)gridDim.y - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < kSlabCols; c += kThreads) {
+    const int64_t col = slab_col0 + c;
+    if (col >= H) continue;
+    float sum = 0.f;
+    const int64_t slabs = gridDim.y;
+#pragma unroll 8
+    for (int64_t r = 0; r < slabs; ++r) sum += __ldcg(partials + r * H + col);
+    y[col] = __float2half_rn(sum);
+  }
+  if (threadIdx.x == 0) tickets[col_slab] = 0;  // leave the workspace ready for the next call
+}
+
+template <RowMode M>
+cudaError_t launch_mode(const RowSource& src, const half* h, half* y, int64_t H, int64_t k, int64_t gsz,
+                        void* workspace, cudaStream_t stream, LaunchOpts opts) {
+  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool vec4 = (H % 32 == 0) && (gsz % 32 == 0) && src.row_bytes % 16 == 0 && aligned16(src.W) &&
+                    (M != RowMode::kDesc || aligned16(src.W2));
+  const DownShape s = down_shape(H, k, vec4);
+  int* tickets = reinterpret_cast<int*>(workspace);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterBytes);
+  const dim3 grid((unsigned)s.col_slabs, (unsigned)s.row_slabs);
+  if (vec4) {
+    const size_t smem = (size_t)kPhases * kColChunks * 32 * sizeof(float);
+    auto kernel = sparse_down_kernel<M, 4>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_ex(kernel, grid, dim3(kThreads), smem, stream, 1, opts.pdl, src, h, y, H, k, gsz, s.chunks,
+                     s.rows_per_slab, partials, tickets);
+  }
+  const size_t smem = (size_t)kPhases * kColChunks * 8 * sizeof(float);
+  return launch_ex(sparse_down_kernel<M, 1>, grid, dim3(kThreads), smem, stream, 1, opts.pdl, src, h, y, H, k, gsz,
+                   s.chunks, s.rows_per_slab, partials, tickets);
+}
+
+}  // namespace
+
+int64_t sparse_workspace_bytes(int64_t H, int64_t k) {
+  // the vector and scalar shapes differ; reserve the larger of the two
+  const DownShape a = down_shape(H, k, true);
+  const DownShape b = down_shape(H, k, false);
+  const int64_t slabs = a.row_slabs > b.row_slabs ? a.row_slabs : b.row_slabs;
+  return kCounterBytes + slabs * H * (int64_t)sizeof(float);
+}
+
+cudaError_t launch_sparse_down(RowMode mode, const RowSource& src, const half* h, half* y, int64_t H, int64_t k,
+                               int64_t group_size, void* workspace, cudaStream_t stream, LaunchOpts opts) {
+  switch (mode) {
+    case RowMode::kPlain:
+      return launch_mode<RowMode::kPlain>(src, h, y, H, k, group_size, workspace, stream, opts);
+    case RowMode::kIndexed:
+      return launch_mode<RowMode::kIndexed>(src, h, y, H, k, group_size, workspace, stream, opts);
+    case RowMode::kDesc:
+      return launch_mode<RowMode::kDesc>(src, h, y, H, k, group_size, workspace, stream, opts);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace soinfer

@@ -1,0 +1,530 @@
+"""Torch-tensor front end of the sm_100a C ABI (libsoinfer_b200.so).
+
+Mirrors the reference's pybind11 module ``soinfer._C`` (csrc/bindings.cpp:26-610
+of sparse-offload-infer): the same function names, argument order and
+preconditions, each failed precondition raised as ``RuntimeError`` (the
+reference's TORCH_CHECK), outputs freshly allocated, and every kernel launched
+on torch's *current* CUDA stream of the inputs' device.  The library is bound
+with ctypes over plain pointers; no torch type crosses the ABI.
+
+There is no CPU fallback: if the shared library is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_LIB_NAME = "libsoinfer_b200.so"
+_lib = None
+_lib_error: str | None = None
+_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_F32 = ctypes.c_float
+_INT = ctypes.c_int
+
+# name -> (restype, argtypes); kept in step with include/soinfer_b200.h
+_SIGNATURES = {
+    "soinfer_abi_version": (_INT, []),
+    "soinfer_last_error": (ctypes.c_char_p, []),
+    "soinfer_status_string": (ctypes.c_char_p, [_INT]),
+    "soinfer_gemv_w4a16_group": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "soinfer_gemv_w4a16_group_lop3": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "soinfer_gemv_w4a16_group_ex": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_uint32, _P]),
+    "soinfer_gemv_w4a16_rows": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
+    "soinfer_gemv_w8a16": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
+    "soinfer_topk_threshold_select": (_INT, [_P, _I64, _I64, _P, _P, _P]),
+    "soinfer_topk_select_exact": (_INT, [_P, _I64, _I64, _P, _P, _P]),
+    "soinfer_build_dip_descriptors": (_INT, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
+    "soinfer_gemv_dip_fused_up": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
+    "soinfer_sparse_workspace_bytes": (_I64, [_I64, _I64]),
+    "soinfer_gemv_w4a16_sparse_accumulate": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_gemv_w4a16_sparse_rows": (_INT, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_gemv_dip_fused_down": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64,
+                                           _P]),
+    "soinfer_gather_rows_staged": (_INT, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P]),
+    "soinfer_gather_rows_naive": (_INT, [_P, _I64, _I64, _P, _I64, _P, _I64, _P]),
+    "soinfer_gather_rows_device": (_INT, [_P, _I64, _I64, _P, _I64, _P, _P]),
+    "soinfer_rmsnorm": (_INT, [_P, _P, _P, _I64, _I64, _F32, _P]),
+    "soinfer_rope_apply": (_INT, [_P, _P, _P, _I64, _I64, _P]),
+    "soinfer_kv_cache_append": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "soinfer_decode_attention_workspace_bytes": (_I64, [_I64, _I64, _I64]),
+    "soinfer_decode_attention": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+}
+
+
+def lib_path() -> str:
+    return os.path.join(os.path.dirname(os.path.abspath(__file__)), _LIB_NAME)
+
+
+def lib():
+    """The loaded shared library; raises RuntimeError if it is not built."""
+    global _lib, _lib_error
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            try:
+                handle = ctypes.CDLL(path)
+            except OSError as exc:
+                _lib_error = f"soinfer CUDA library not available at {path}: {exc} (build it with __graft_entry__.build())"
+                raise RuntimeError(_lib_error) from exc
+            for name, (restype, argtypes) in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = handle
+    return _lib
+
+
+def is_available() -> bool:
+    try:
+        lib()
+        return True
+    except RuntimeError:
+        return False
+
+
+def last_error() -> str:
+    return lib().soinfer_last_error().decode()
+
+
+def _call(fn_name: str, *args) -> None:
+    status = getattr(lib(), fn_name)(*args)
+    if status != 0:
+        msg = lib().soinfer_last_error().decode()
+        kind = lib().soinfer_status_string(status).decode()
+        raise RuntimeError(f"{msg} [{kind}]")
+
+
+def _check(cond: bool, *msg) -> None:
+    if not cond:
+        raise RuntimeError("".join(str(m) for m in msg))
+
+
+def _check_cuda(t: torch.Tensor, name: str, dtype: torch.dtype, dtype_msg: str) -> None:
+    _check(t.is_cuda, name, ": input must be a CUDA tensor")
+    _check(t.dtype == dtype, name, dtype_msg)
+    _check(t.is_contiguous(), name, ": input must be contiguous")
+
+
+def _f16(t, name):
+    _check_cuda(t, name, torch.float16, ": only float16 is supported")
+
+
+def _f32(t, name):
+    _check_cuda(t, name, torch.float32, ": only float32 is supported")
+
+
+def _same_device(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts[1:]:
+        _check(t.device == dev, "all tensors must be on the same CUDA device, got ", dev, " and ", t.device)
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
+# ---------------------------------------------------------------- workspaces
+# One zero-initialised workspace per (kind, device, stream); the kernels leave
+# the sparse workspace zeroed again on exit, so it is reused across calls.
+_workspaces: dict[tuple, torch.Tensor] = {}
+
+
+def _workspace(kind: str, dev: torch.device, nbytes: int) -> torch.Tensor:
+    key = (kind, dev.index, _stream(dev))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
+        _workspaces[key] = ws
+    return ws
+
+
+# -------------------------------------------------------------------- GEMVs
+FLAG_PDL = 1
+
+
+def _gemv_w4a16_group_impl(fn: str, name: str, Wq_packed, scale, x, K: int, group_size: int,
+                           out: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    _check(Wq_packed.is_cuda, name, "(Wq_packed): must be a CUDA tensor")
+    _check(Wq_packed.dtype == torch.uint8, name, "(Wq_packed): must be uint8 (AWQ-packed int4)")
+    _check(Wq_packed.is_contiguous(), name, "(Wq_packed): must be contiguous")
+    _check(Wq_packed.dim() == 2, name, "(Wq_packed): must be 2D [N, ceil(K/8)*4]")
+    _f16(x, "x")
+    _check(x.dim() == 1 and x.size(0) == K, name, ": x must be 1D [K]")
+    _check(K >= 1, name, ": K must be >= 1")
+    _check(group_size >= 1 and group_size % 8 == 0, name, ": group_size must be a positive multiple of 8")
+    N = Wq_packed.size(0)
+    _check(Wq_packed.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
+    _check(scale.is_cuda, name, ": scale must be a CUDA tensor")
+    _check(scale.dtype == torch.float32, name, ": scale must be float32")
+    _check(scale.is_contiguous(), name, ": scale must be contiguous")
+    _check(scale.dim() == 2 and scale.size(0) == N, name,
+           ": scale must be 2D [N, num_groups] (grouped int4 has no per-tensor broadcast)")
+    num_groups = scale.size(1)
+    _check(num_groups == _cdiv(K, group_size), name, ": scale's num_groups must be ceil(K/group_size) for the given K "
+           "and group_size, got ", num_groups, " but expected ", _cdiv(K, group_size))
+    dev = _same_device(Wq_packed, scale, x)
+    y = out if out is not None else torch.empty(N, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        if pdl:
+            _call("soinfer_gemv_w4a16_group_ex", _ptr(Wq_packed), _ptr(scale), _ptr(x), _ptr(y), N, K, group_size,
+                  num_groups, FLAG_PDL, _stream(dev))
+        else:
+            _call(fn, _ptr(Wq_packed), _ptr(scale), _ptr(x), _ptr(y), N, K, group_size, num_groups, _stream(dev))
+    return y
+
+
+def gemv_w4a16_group(Wq_packed, scale, x, K: int, group_size: int, out=None, pdl: bool = False) -> torch.Tensor:
+    return _gemv_w4a16_group_impl("soinfer_gemv_w4a16_group", "gemv_w4a16_group", Wq_packed, scale, x, K, group_size,
+                                  out, pdl)
+
+
+def gemv_w4a16_group_lop3(Wq_packed, scale, x, K: int, group_size: int, out=None, pdl: bool = False) -> torch.Tensor:
+    """pdl=True: programmatic dependent launch (only when the weights are not
+    written by the kernel preceding this one on the stream)."""
+    return _gemv_w4a16_group_impl("soinfer_gemv_w4a16_group_lop3", "gemv_w4a16_group_lop3", Wq_packed, scale, x, K,
+                                  group_size, out, pdl)
+
+
+def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: torch.Tensor | None = None):
+    name = "gemv_w4a16_rows"
+    _check(Wq_packed.is_cuda and Wq_packed.dtype == torch.uint8 and Wq_packed.is_contiguous() and Wq_packed.dim() == 2,
+           name, "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
+    _check(Wq_packed.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
+    _f32(scale, name + "(scale)")
+    _check(scale.dim() == 2 and scale.size(0) == Wq_packed.size(0), name, ": scale must be 2D [N, num_groups]")
+    _check_cuda(rows, name + "(rows)", torch.int32, ": must be int32")
+    _check(rows.dim() == 1, name, ": rows must be 1D")
+    _f16(x, name + "(x)")
+    _check(x.dim() == 1 and x.size(0) == K, name, ": x must be 1D [K]")
+    dev = _same_device(Wq_packed, scale, rows, x)
+    y = out if out is not None else torch.empty(rows.numel(), dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_w4a16_rows", _ptr(Wq_packed), _ptr(scale), Wq_packed.size(0), _ptr(rows), rows.numel(),
+              _ptr(x), _ptr(y), K, group_size, scale.size(1), _stream(dev))
+    return y
+
+
+def gemv_w8a16(Wq, scale, x, group_size: int) -> torch.Tensor:
+    _check(Wq.is_cuda, "gemv_w8a16(Wq): must be a CUDA tensor")
+    _check(Wq.dtype == torch.int8, "gemv_w8a16(Wq): must be int8")
+    _check(Wq.is_contiguous(), "gemv_w8a16(Wq): must be contiguous")
+    _check(Wq.dim() == 2, "gemv_w8a16(Wq): must be 2D [N, K]")
+    _f16(x, "gemv_w8a16(x)")
+    _check(x.dim() == 1 and x.size(0) == Wq.size(1), "gemv_w8a16: x must be 1D [K] matching Wq's K")
+    _check(group_size >= 1, "gemv_w8a16: group_size must be >= 1")
+    N, K = Wq.size(0), Wq.size(1)
+    _check(scale.is_cuda, "gemv_w8a16: scale must be a CUDA tensor")
+    _check(scale.dtype == torch.float32, "gemv_w8a16: scale must be float32")
+    _check(scale.is_contiguous(), "gemv_w8a16: scale must be contiguous")
+    _check(scale.dim() == 2, "gemv_w8a16: scale must be 2D [N or 1, num_groups]")
+    _check(scale.size(0) == N or scale.size(0) == 1,
+           "gemv_w8a16: scale.size(0) must be N (per-channel/group) or 1 (per-tensor broadcast)")
+    num_groups = scale.size(1)
+    row_stride = 0 if scale.size(0) == 1 else num_groups
+    _check(num_groups == 1 or group_size % 4 == 0, "gemv_w8a16: group_size must be a multiple of 4 when num_groups > 1")
+    _check(num_groups == 1 or num_groups == _cdiv(K, group_size), "gemv_w8a16: scale's num_groups must be 1 or "
+           "ceil(K/group_size) for the given K and group_size, got ", num_groups, " but expected ",
+           _cdiv(K, group_size))
+    dev = _same_device(Wq, scale, x)
+    y = torch.empty(N, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_w8a16", _ptr(Wq), _ptr(scale), _ptr(x), _ptr(y), N, K, group_size, num_groups, row_stride,
+              _stream(dev))
+    return y
+
+
+# ------------------------------------------------------------- selection
+def _topk_impl(fn: str, name: str, abs_g, k: int):
+    _f32(abs_g, name + "(abs_g)")
+    _check(abs_g.dim() == 1, name, ": abs_g must be 1D [I]")
+    n = abs_g.size(0)
+    _check(1 <= k <= n, name, ": k must be in [1, I]")
+    dev = abs_g.device
+    idx = torch.empty(k, dtype=torch.int32, device=dev)
+    count = torch.empty(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _call(fn, _ptr(abs_g), n, k, _ptr(idx), _ptr(count), _stream(dev))
+    return idx, count
+
+
+def topk_threshold_select(abs_g, k: int):
+    return _topk_impl("soinfer_topk_threshold_select", "topk_threshold_select", abs_g, k)
+
+
+def topk_select_exact(abs_g, k: int):
+    return _topk_impl("soinfer_topk_select_exact", "topk_select_exact", abs_g, k)
+
+
+def build_dip_descriptors(selected_indices, slot_of):
+    name = "build_dip_descriptors"
+    _check(selected_indices.is_cuda and selected_indices.dtype == torch.int32 and selected_indices.dim() == 1
+           and selected_indices.is_contiguous(), name, "(selected_indices): must be a contiguous 1D int32 CUDA tensor")
+    _check(slot_of.is_cuda and slot_of.dtype == torch.int32 and slot_of.dim() == 1 and slot_of.is_contiguous(),
+           name, "(slot_of): must be a contiguous 1D int32 CUDA tensor")
+    dev = _same_device(selected_indices, slot_of)
+    k = selected_indices.size(0)
+    desc = torch.empty(k, dtype=torch.int32, device=dev)
+    miss = torch.empty(k, dtype=torch.int32, device=dev)
+    count = torch.empty(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_build_dip_descriptors", _ptr(selected_indices), k, _ptr(slot_of), slot_of.numel(), _ptr(desc),
+              _ptr(miss), count.data_ptr(), _stream(dev))
+    return desc, miss, count
+
+
+# ------------------------------------------------------- DIP fused GEMVs
+def _check_dip_common(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, row_dim: int, name: str):
+    expected = _cdiv(row_dim, 8) * 4
+    _check(cache_Wq.is_cuda and cache_Wq.dtype == torch.uint8 and cache_Wq.dim() == 2 and cache_Wq.is_contiguous()
+           and cache_Wq.size(1) == expected, name,
+           "(cache_Wq): must be a contiguous 2D uint8 CUDA tensor [C, ceil(row_dim/8)*4]")
+    _check(staging_Wq.is_cuda and staging_Wq.dtype == torch.uint8 and staging_Wq.dim() == 2
+           and staging_Wq.is_contiguous() and staging_Wq.size(1) == expected, name,
+           "(staging_Wq): must be a contiguous 2D uint8 CUDA tensor [M, ceil(row_dim/8)*4]")
+    _check(cache_scale.is_cuda and cache_scale.dtype == torch.float32 and cache_scale.dim() == 2
+           and cache_scale.is_contiguous(), name, "(cache_scale): must be a contiguous 2D float32 CUDA tensor")
+    _check(staging_scale.is_cuda and staging_scale.dtype == torch.float32 and staging_scale.dim() == 2
+           and staging_scale.is_contiguous(), name, "(staging_scale): must be a contiguous 2D float32 CUDA tensor")
+    _check(cache_scale.size(1) == staging_scale.size(1), name,
+           ": cache_scale and staging_scale must have the same num_groups")
+    _check(cache_scale.size(0) == cache_Wq.size(0) and staging_scale.size(0) == staging_Wq.size(0), name,
+           ": scale rows must match weight rows")
+    _check(descriptors.is_cuda and descriptors.dtype == torch.int32 and descriptors.dim() == 1
+           and descriptors.is_contiguous(), name, "(descriptors): must be a contiguous 1D int32 CUDA tensor")
+
+
+def gemv_dip_fused_up(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, x, K: int, group_size: int,
+                      out: torch.Tensor | None = None):
+    name = "gemv_dip_fused_up"
+    _check_dip_common(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, K, name)
+    _f16(x, "gemv_dip_fused_up(x)")
+    _check(x.dim() == 1 and x.size(0) == K, name, ": x must be 1D [K]")
+    _check(group_size >= 1 and group_size % 8 == 0, name, ": group_size must be a positive multiple of 8")
+    num_groups = cache_scale.size(1)
+    _check(num_groups == _cdiv(K, group_size), name, ": cache_scale/staging_scale's num_groups must be "
+           "ceil(K/group_size) for the given K and group_size, got ", num_groups, " but expected ",
+           _cdiv(K, group_size))
+    dev = _same_device(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, x)
+    k = descriptors.size(0)
+    y = out if out is not None else torch.empty(k, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_dip_fused_up", _ptr(cache_Wq), _ptr(cache_scale), cache_Wq.size(0), _ptr(staging_Wq),
+              _ptr(staging_scale), staging_Wq.size(0), _ptr(descriptors), k, _ptr(x), _ptr(y), K, group_size,
+              num_groups, _stream(dev))
+    return y
+
+
+def _sparse_ws(dev, H: int, k: int):
+    nbytes = lib().soinfer_sparse_workspace_bytes(H, max(k, 1))
+    ws = _workspace("sparse", dev, nbytes)
+    return ws.data_ptr(), ws.numel()
+
+
+def gemv_w4a16_sparse_accumulate(Wq_selected, scale_selected, h_selected, H: int, group_size: int,
+                                 out: torch.Tensor | None = None):
+    name = "gemv_w4a16_sparse_accumulate"
+    _check(Wq_selected.is_cuda and Wq_selected.dtype == torch.uint8 and Wq_selected.is_contiguous(), name,
+           "(Wq_selected): must be a contiguous CUDA uint8 tensor")
+    _check(Wq_selected.dim() == 2, name, "(Wq_selected): must be 2D [k, ceil(H/8)*4]")
+    _check(H >= 1, name, ": H must be >= 1")
+    _check(group_size >= 1 and group_size % 8 == 0, name, ": group_size must be a positive multiple of 8")
+    k = Wq_selected.size(0)
+    _check(Wq_selected.size(1) == _cdiv(H, 8) * 4, name, ": Wq_selected.size(1) must be ceil(H/8)*4 for the given H")
+    _check(scale_selected.is_cuda and scale_selected.dtype == torch.float32 and scale_selected.is_contiguous(), name,
+           "(scale_selected): must be a contiguous CUDA float32 tensor")
+    _check(scale_selected.dim() == 2 and scale_selected.size(0) == k, name,
+           ": scale_selected must be 2D [k, num_groups]")
+    _f16(h_selected, "gemv_w4a16_sparse_accumulate(h_selected)")
+    _check(h_selected.dim() == 1 and h_selected.size(0) == k, name, ": h_selected must be 1D [k]")
+    num_groups = scale_selected.size(1)
+    _check(num_groups == _cdiv(H, group_size), name, ": scale_selected's num_groups must be ceil(H/group_size) for "
+           "the given H and group_size, got ", num_groups, " but expected ", _cdiv(H, group_size))
+    dev = _same_device(Wq_selected, scale_selected, h_selected)
+    y = out if out is not None else torch.empty(H, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        ws, wsb = _sparse_ws(dev, H, k)
+        _call("soinfer_gemv_w4a16_sparse_accumulate", _ptr(Wq_selected), _ptr(scale_selected), _ptr(h_selected),
+              _ptr(y), H, k, group_size, num_groups, ws, wsb, _stream(dev))
+    return y
+
+
+def gemv_w4a16_sparse_rows(Wq_T, scale_T, rows, h_selected, H: int, group_size: int,
+                           out: torch.Tensor | None = None):
+    name = "gemv_w4a16_sparse_rows"
+    _check(Wq_T.is_cuda and Wq_T.dtype == torch.uint8 and Wq_T.is_contiguous() and Wq_T.dim() == 2, name,
+           "(Wq_T): must be a contiguous 2D uint8 CUDA tensor")
+    _check(Wq_T.size(1) == _cdiv(H, 8) * 4, name, ": Wq_T.size(1) must be ceil(H/8)*4 for the given H")
+    _f32(scale_T, name + "(scale_T)")
+    _check(scale_T.dim() == 2 and scale_T.size(0) == Wq_T.size(0), name, ": scale_T must be 2D [I, num_groups]")
+    _check_cuda(rows, name + "(rows)", torch.int32, ": must be int32")
+    _f16(h_selected, name + "(h_selected)")
+    k = rows.numel()
+    _check(h_selected.dim() == 1 and h_selected.size(0) == k, name, ": h_selected must be 1D [k]")
+    dev = _same_device(Wq_T, scale_T, rows, h_selected)
+    y = out if out is not None else torch.empty(H, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        ws, wsb = _sparse_ws(dev, H, k)
+        _call("soinfer_gemv_w4a16_sparse_rows", _ptr(Wq_T), _ptr(scale_T), Wq_T.size(0), _ptr(rows), _ptr(h_selected),
+              _ptr(y), H, k, group_size, scale_T.size(1), ws, wsb, _stream(dev))
+    return y
+
+
+def gemv_dip_fused_down(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, h_selected, H: int,
+                        group_size: int, out: torch.Tensor | None = None):
+    name = "gemv_dip_fused_down"
+    _check_dip_common(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, H, name)
+    _f16(h_selected, "gemv_dip_fused_down(h_selected)")
+    k = descriptors.size(0)
+    _check(h_selected.dim() == 1 and h_selected.size(0) == k, name, ": h_selected must be 1D [k]")
+    _check(H >= 1, name, ": H must be >= 1")
+    _check(group_size >= 1 and group_size % 8 == 0, name, ": group_size must be a positive multiple of 8")
+    num_groups = cache_scale.size(1)
+    _check(num_groups == _cdiv(H, group_size), name, ": cache_scale/staging_scale's num_groups must be "
+           "ceil(H/group_size) for the given H and group_size, got ", num_groups, " but expected ",
+           _cdiv(H, group_size))
+    dev = _same_device(cache_Wq, cache_scale, staging_Wq, staging_scale, descriptors, h_selected)
+    y = out if out is not None else torch.empty(H, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        ws, wsb = _sparse_ws(dev, H, k)
+        _call("soinfer_gemv_dip_fused_down", _ptr(cache_Wq), _ptr(cache_scale), cache_Wq.size(0), _ptr(staging_Wq),
+              _ptr(staging_scale), staging_Wq.size(0), _ptr(descriptors), _ptr(h_selected), _ptr(y), H, k, group_size,
+              num_groups, ws, wsb, _stream(dev))
+    return y
+
+
+# ------------------------------------------------------------------ gathers
+def _check_gather_common(matrix, indices, gpu_dst, name):
+    _check(matrix.device.type == "cpu" and matrix.is_pinned(), name, "(matrix): must be pinned host memory")
+    _check(matrix.dtype == torch.uint8 and matrix.dim() == 2 and matrix.is_contiguous(), name,
+           "(matrix): must be a contiguous 2D uint8 tensor [num_rows, row_nbytes]")
+    _check(indices.device.type == "cpu" and indices.dtype == torch.int64 and indices.dim() == 1, name,
+           "(indices): must be a 1D int64 CPU tensor")
+    _check(gpu_dst.is_cuda and gpu_dst.dtype == torch.uint8 and gpu_dst.is_contiguous(), name,
+           "(gpu_dst): must be a contiguous CUDA uint8 tensor")
+    k = indices.size(0)
+    _check(gpu_dst.numel() >= k * matrix.size(1), name, "(gpu_dst): too small for k * row_nbytes bytes")
+
+
+def gather_rows_staged(matrix, indices, staging, gpu_dst) -> None:
+    name = "gather_rows_staged"
+    _check_gather_common(matrix, indices, gpu_dst, name)
+    _check(staging.device.type == "cpu" and staging.is_pinned() and staging.dtype == torch.uint8,
+           "gather_rows_staged(staging): must be pinned host uint8 memory")
+    k, rb = indices.size(0), matrix.size(1)
+    _check(staging.numel() >= k * rb, "gather_rows_staged(staging): too small for k * row_nbytes bytes")
+    indices = indices.contiguous()
+    dev = gpu_dst.device
+    with torch.cuda.device(dev):
+        _call("soinfer_gather_rows_staged", _ptr(matrix), matrix.size(0), rb, _ptr(indices), k, _ptr(staging),
+              staging.numel(), _ptr(gpu_dst), gpu_dst.numel(), _stream(dev))
+
+
+def gather_rows_naive(matrix, indices, gpu_dst) -> None:
+    name = "gather_rows_naive"
+    _check_gather_common(matrix, indices, gpu_dst, name)
+    indices = indices.contiguous()
+    dev = gpu_dst.device
+    with torch.cuda.device(dev):
+        _call("soinfer_gather_rows_naive", _ptr(matrix), matrix.size(0), matrix.size(1), _ptr(indices),
+              indices.size(0), _ptr(gpu_dst), gpu_dst.numel(), _stream(dev))
+
+
+def gather_rows_device(matrix, rows, gpu_dst) -> None:
+    """Device-driven gather of rows `rows` (int32 CUDA) of `matrix` (CUDA, or
+    pinned host memory read zero-copy) into gpu_dst (CUDA uint8)."""
+    name = "gather_rows_device"
+    _check(matrix.dtype == torch.uint8 and matrix.dim() == 2 and matrix.is_contiguous(), name,
+           "(matrix): must be a contiguous 2D uint8 tensor")
+    _check(matrix.is_cuda or matrix.is_pinned(), name, "(matrix): must be CUDA or pinned host memory")
+    _check_cuda(rows, name + "(rows)", torch.int32, ": must be int32")
+    _check(gpu_dst.is_cuda and gpu_dst.dtype == torch.uint8 and gpu_dst.is_contiguous(), name,
+           "(gpu_dst): must be a contiguous CUDA uint8 tensor")
+    k, rb = rows.numel(), matrix.size(1)
+    _check(gpu_dst.numel() >= k * rb, name, "(gpu_dst): too small for k * row_nbytes bytes")
+    dev = gpu_dst.device
+    with torch.cuda.device(dev):
+        _call("soinfer_gather_rows_device", _ptr(matrix), matrix.size(0), rb, _ptr(rows), k, _ptr(gpu_dst),
+              _stream(dev))
+
+
+# ----------------------------------------------------- attention-side glue
+def rmsnorm(x, weight, eps: float = 1e-6) -> torch.Tensor:
+    _f16(x, "rmsnorm(x)")
+    _f16(weight, "rmsnorm(weight)")
+    _check(x.dim() == 2, "rmsnorm: x must be 2D [rows, hidden]")
+    _check(weight.dim() == 1 and weight.size(0) == x.size(1), "rmsnorm: weight shape must match x's hidden dim")
+    _check(x.size(1) % 2 == 0, "rmsnorm: hidden dim must be even (half2 vectorization)")
+    dev = _same_device(x, weight)
+    out = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        _call("soinfer_rmsnorm", _ptr(x), _ptr(weight), _ptr(out), x.size(0), x.size(1), float(eps), _stream(dev))
+    return out
+
+
+def rope_apply(x, cos_vals, sin_vals) -> None:
+    _f16(x, "rope_apply(x)")
+    _check(x.dim() == 2, "rope_apply: x must be 2D [num_heads, head_dim]")
+    _check(x.size(1) % 2 == 0, "rope_apply: head_dim must be even")
+    _check(cos_vals.is_cuda and cos_vals.dtype == torch.float32 and cos_vals.is_contiguous(),
+           "rope_apply: cos_vals must be a contiguous float32 CUDA tensor")
+    _check(sin_vals.shape == cos_vals.shape and sin_vals.is_cuda and sin_vals.dtype == torch.float32
+           and sin_vals.is_contiguous(), "rope_apply: sin_vals must match cos_vals (contiguous float32 CUDA, same shape)")
+    _check(cos_vals.dim() == 1 and cos_vals.size(0) == x.size(1) // 2,
+           "rope_apply: cos_vals/sin_vals must be 1D [head_dim / 2]")
+    dev = _same_device(x, cos_vals, sin_vals)
+    with torch.cuda.device(dev):
+        _call("soinfer_rope_apply", _ptr(x), _ptr(cos_vals), _ptr(sin_vals), x.size(0), x.size(1), _stream(dev))
+
+
+def kv_cache_append(k_cache, v_cache, k_new, v_new, pos: int) -> None:
+    for t, n in ((k_cache, "k_cache"), (v_cache, "v_cache"), (k_new, "k_new"), (v_new, "v_new")):
+        _f16(t, f"kv_cache_append({n})")
+    _check(k_cache.dim() == 3 and v_cache.shape == k_cache.shape,
+           "kv_cache_append: k_cache/v_cache must be 3D [num_kv_heads, max_seq_len, head_dim] and same shape")
+    _check(k_new.shape == v_new.shape, "kv_cache_append: k_new/v_new must have the same shape")
+    _check(k_new.dim() == 2 and k_new.size(0) == k_cache.size(0) and k_new.size(1) == k_cache.size(2),
+           "kv_cache_append: k_new/v_new must be 2D [num_kv_heads, head_dim] matching the cache")
+    nkv, max_seq, hd = k_cache.shape
+    _check(0 <= pos < max_seq, "kv_cache_append: pos out of range for max_seq_len")
+    dev = _same_device(k_cache, v_cache, k_new, v_new)
+    with torch.cuda.device(dev):
+        _call("soinfer_kv_cache_append", _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), nkv, max_seq, hd,
+              pos, _stream(dev))
+
+
+def decode_attention(q, k_cache, v_cache, cur_len: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    _f16(q, "decode_attention(q)")
+    _f16(k_cache, "decode_attention(k_cache)")
+    _f16(v_cache, "decode_attention(v_cache)")
+    _check(q.dim() == 2, "decode_attention: q must be 2D [num_q_heads, head_dim]")
+    _check(k_cache.dim() == 3 and v_cache.shape == k_cache.shape,
+           "decode_attention: k_cache/v_cache must be 3D [num_kv_heads, max_seq_len, head_dim] and same shape")
+    _check(q.size(1) == k_cache.size(2), "decode_attention: q's head_dim must match the cache's head_dim")
+    nq, (nkv, max_seq, hd) = q.size(0), k_cache.shape
+    _check(nq % nkv == 0, "decode_attention: num_q_heads must be a multiple of num_kv_heads")
+    _check(1 <= cur_len <= max_seq, "decode_attention: cur_len out of range for max_seq_len")
+    dev = _same_device(q, k_cache, v_cache)
+    y = out if out is not None else torch.empty(nq, hd, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        nbytes = lib().soinfer_decode_attention_workspace_bytes(nq, max_seq, hd)
+        ws = _workspace("attn", dev, nbytes)
+        _call("soinfer_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(y), nq, nkv, max_seq, hd,
+              cur_len, ws.data_ptr(), ws.numel(), _stream(dev))
+    return y
