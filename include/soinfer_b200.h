@@ -49,6 +49,13 @@ const char* soinfer_last_error(void);
 /* Static name of a status code. */
 const char* soinfer_status_string(int status);
 
+/* Reads and clears the device-side error bits set by kernels whose bounded
+ * waits gave up instead of hanging (bit 0: an asynchronous copy into shared
+ * memory did not complete within its time limit).  Synchronous; *flags = 0
+ * means no kernel reported a problem since the previous call.  No reference
+ * counterpart. */
+int soinfer_device_errors(int* flags);
+
 /* ---------------------------------------------------------------- GEMV --- */
 
 /* y[n] = fp16( sum_k scale[n, k/g] * q[n,k] * x[k] ), fp32 accumulation.
@@ -81,6 +88,35 @@ int soinfer_gemv_w4a16_group_lop3(const uint8_t* Wq, const float* scale, const s
 int soinfer_gemv_w4a16_group_ex(const uint8_t* Wq, const float* scale, const soinfer_half* x,
                                 soinfer_half* y, int64_t N, int64_t K, int64_t group_size,
                                 int64_t num_groups, uint32_t flags, void* stream);
+
+/* One INT4 GEMV of a batch: y = dequant(Wq, scale) @ x (shapes as in
+ * soinfer_gemv_w4a16_group).  dep = index of an earlier task of the same
+ * batch whose output this task's x depends on (x is read only after that
+ * task has finished), or -1 if x is ready when the batch starts. */
+typedef struct soinfer_gemv_task {
+  const uint8_t* Wq;
+  const float* scale;
+  const soinfer_half* x;
+  soinfer_half* y;
+  int64_t N, K, group_size, num_groups;
+  int64_t dep;
+} soinfer_gemv_task;
+
+/* Bytes of zero-initialised device workspace soinfer_gemv_w4a16_batch needs
+ * for num_tasks tasks (per-task completion counters; left zeroed on return). */
+int64_t soinfer_gemv_batch_workspace_bytes(int64_t num_tasks);
+
+/* Runs up to 256 INT4 GEMVs, in task order, as one persistent kernel: a
+ * producer warp per SM streams the weights of task after task through a deep
+ * shared-memory ring (weights never wait for activations) while consumer
+ * warps compute each task once its x is ready.  Dependencies are expressed
+ * with soinfer_gemv_task.dep.  Tasks outside the fast-path constraints (K and
+ * group_size multiples of 128, num_groups % 4 == 0, 16-byte aligned operands,
+ * N <= 128 * #SMs) make the whole batch run as ordered single-GEMV launches.
+ * No reference counterpart: the reference launches one GEMV per weight
+ * (runtime/generate.py:116-138). */
+int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,
+                             int64_t workspace_bytes, void* stream);
 
 /* Row-indirect INT4 GEMV over HBM-resident weights: y[r] = row rows[r] of
  * dequant(Wq, scale) dotted with x, for r in [0, num_sel).  Equivalent to

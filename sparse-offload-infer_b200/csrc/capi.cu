@@ -4,6 +4,7 @@
 // the thread's last-error message.
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/soinfer_b200.h"
@@ -78,6 +79,83 @@ const char* soinfer_status_string(int status) {
     case SOINFER_ERR_HOST: return "SOINFER_ERR_HOST";
   }
   return "SOINFER_ERR_UNKNOWN";
+}
+
+int soinfer_device_errors(int* flags) {
+  REQUIRE(flags, "device_errors: null flags");
+  *flags = 0;
+  int f = 0;
+  if (int st = cuda_result(read_and_clear_gemv_w4_error(&f), "device_errors")) return st;
+  *flags |= f;
+  if (int st = cuda_result(read_and_clear_gemv_batch_error(&f), "device_errors")) return st;
+  *flags |= f;
+  return SOINFER_OK;
+}
+
+int64_t soinfer_gemv_batch_workspace_bytes(int64_t num_tasks) {
+  if (num_tasks < 0 || num_tasks > kMaxBatchTasks) return 0;
+  return gemv_batch_workspace_bytes(num_tasks);
+}
+
+int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_w4a16_batch";
+  REQUIRE(num_tasks >= 0 && num_tasks <= kMaxBatchTasks, "%s: num_tasks must be in [0, %d]", name, kMaxBatchTasks);
+  if (num_tasks == 0) return SOINFER_OK;
+  REQUIRE(tasks, "%s: null task list", name);
+  bool fast = true;
+  for (int64_t i = 0; i < num_tasks; ++i) {
+    const soinfer_gemv_task& t = tasks[i];
+    char tn[64];
+    snprintf(tn, sizeof(tn), "%s[task %lld]", name, (long long)i);
+    if (int st = check_int4_layout(tn, t.K, t.group_size, t.num_groups)) return st;
+    REQUIRE(t.N >= 1, "%s: N must be >= 1", tn);
+    REQUIRE(t.Wq && t.scale && t.x && t.y, "%s: null pointer", tn);
+    REQUIRE(t.dep >= -1 && t.dep < i, "%s: dep must be -1 or an earlier task index", tn);
+    fast = fast && t.K % 128 == 0 && t.group_size % 128 == 0 && t.num_groups % 4 == 0 && aligned(t.Wq, 16) &&
+           aligned(t.scale, 16) && aligned(t.x, 16) && t.N < (1 << 30) && t.K < (1 << 30);
+  }
+  cudaStream_t st = as_stream(stream);
+  if (fast) {
+    static GemvBatchParams B;  // large: not on the stack
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    B.num = (int)num_tasks;
+    for (int64_t i = 0; i < num_tasks; ++i) {
+      const soinfer_gemv_task& t = tasks[i];
+      GemvBatchTask& d = B.tasks[i];
+      d.W = t.Wq;
+      d.S = t.scale;
+      d.x = as_half(t.x);
+      d.y = as_half(t.y);
+      d.N = (int)t.N;
+      d.K = (int)t.K;
+      d.G = (int)t.num_groups;
+      d.cpg = (int)(t.group_size / 128);
+      d.dep = (int)t.dep;
+    }
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (plan_gemv_batch(B, sms)) {
+      REQUIRE(workspace && workspace_bytes >= gemv_batch_workspace_bytes(num_tasks) && aligned(workspace, 4),
+              "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_batch_workspace_bytes(num_tasks));
+      return cuda_result(launch_gemv_batch(B, reinterpret_cast<int*>(workspace), st), name);
+    }
+  }
+  // fallback: ordered single-GEMV launches (stream order satisfies every dep)
+  for (int64_t i = 0; i < num_tasks; ++i) {
+    const soinfer_gemv_task& t = tasks[i];
+    RowSource src;
+    src.W = t.Wq;
+    src.S = t.scale;
+    src.rows1 = t.N;
+    src.row_bytes = int4_row_bytes(t.K);
+    src.num_groups = t.num_groups;
+    if (int rc = cuda_result(launch_gemv_w4(RowMode::kPlain, src, as_half(t.x), as_half(t.y), t.N, t.K, t.group_size, st),
+                             name))
+      return rc;
+  }
+  return SOINFER_OK;
 }
 
 static int gemv_w4_plain(const char* name, const uint8_t* Wq, const float* scale, const soinfer_half* x,

@@ -31,6 +31,29 @@ struct LaunchOpts {
 cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, half* y, int64_t nrows,
                            int64_t K, int64_t group_size, cudaStream_t stream, LaunchOpts opts = {});
 
+// Reads and clears the INT4 GEMV module's device error bits (DeviceError).
+cudaError_t read_and_clear_gemv_w4_error(int* out);
+
+// Persistent batched INT4 GEMV (gemv_batch.cu).  Tasks run in order; a task
+// with dep >= 0 reads x only after every CTA finished task `dep`.
+struct GemvBatchTask {
+  const uint8_t* W;
+  const float* S;
+  const half* x;
+  half* y;
+  int N, K, G, cpg, dep, rows_per_cta;
+};
+constexpr int kMaxBatchTasks = 256;
+struct GemvBatchParams {
+  int num, grid, x_bytes, xsum_bytes, slot_stride, scale_off, slot_bytes, smem_bytes, stages;
+  GemvBatchTask tasks[kMaxBatchTasks];
+};
+int64_t gemv_batch_workspace_bytes(int64_t num_tasks);
+// Fills the derived fields; false when the batch needs the per-task fallback.
+bool plan_gemv_batch(GemvBatchParams& B, int sms);
+cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream);
+cudaError_t read_and_clear_gemv_batch_error(int* out);
+
 // INT8 GEMV (per-tensor / per-channel / grouped scales).
 cudaError_t launch_gemv_w8(const int8_t* Wq, const float* scale, const half* x, half* y, int64_t N,
                            int64_t K, int64_t group_size, int64_t num_groups, int64_t scale_row_stride,

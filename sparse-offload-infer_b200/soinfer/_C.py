@@ -32,9 +32,12 @@ _SIGNATURES = {
     "soinfer_abi_version": (_INT, []),
     "soinfer_last_error": (ctypes.c_char_p, []),
     "soinfer_status_string": (ctypes.c_char_p, [_INT]),
+    "soinfer_device_errors": (_INT, [_P]),
     "soinfer_gemv_w4a16_group": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_group_lop3": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_group_ex": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_uint32, _P]),
+    "soinfer_gemv_batch_workspace_bytes": (_I64, [_I64]),
+    "soinfer_gemv_w4a16_batch": (_INT, [_P, _I64, _P, _I64, _P]),
     "soinfer_gemv_w4a16_rows": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w8a16": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "soinfer_topk_threshold_select": (_INT, [_P, _I64, _I64, _P, _P, _P]),
@@ -92,6 +95,13 @@ def is_available() -> bool:
 
 def last_error() -> str:
     return lib().soinfer_last_error().decode()
+
+
+def device_errors() -> int:
+    """Reads and clears the device-side error bits (bit 0: a bounded copy wait timed out)."""
+    flags = ctypes.c_int(0)
+    _call("soinfer_device_errors", ctypes.byref(flags))
+    return flags.value
 
 
 def _call(fn_name: str, *args) -> None:
@@ -200,6 +210,66 @@ def gemv_w4a16_group_lop3(Wq_packed, scale, x, K: int, group_size: int, out=None
     written by the kernel preceding this one on the stream)."""
     return _gemv_w4a16_group_impl("soinfer_gemv_w4a16_group_lop3", "gemv_w4a16_group_lop3", Wq_packed, scale, x, K,
                                   group_size, out, pdl)
+
+
+class _GemvTask(ctypes.Structure):
+    _fields_ = [("Wq", _P), ("scale", _P), ("x", _P), ("y", _P), ("N", _I64), ("K", _I64), ("group_size", _I64),
+                ("num_groups", _I64), ("dep", _I64)]
+
+
+MAX_BATCH_TASKS = 256
+
+
+class GemvBatch:
+    """A prepared list of INT4 GEMVs run as one persistent kernel
+    (soinfer_gemv_w4a16_batch).  tasks: sequence of
+    (Wq_packed, scale, x, y, K, group_size, dep) with dep = index of an
+    earlier task whose output feeds this task's x, or -1.  The tensors must
+    stay alive and keep their storage while the batch is used."""
+
+    def __init__(self, tasks):
+        n = len(tasks)
+        _check(0 < n <= MAX_BATCH_TASKS, "gemv_w4a16_batch: 1 ..", MAX_BATCH_TASKS, " tasks")
+        arr = (_GemvTask * n)()
+        dev = None
+        for i, (W, scale, x, y, K, group_size, dep) in enumerate(tasks):
+            name = f"gemv_w4a16_batch[task {i}]"
+            _check(W.is_cuda and W.dtype == torch.uint8 and W.is_contiguous() and W.dim() == 2, name,
+                   "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
+            _check(W.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
+            _f32(scale, name + "(scale)")
+            _check(scale.dim() == 2 and scale.size(0) == W.size(0), name, ": scale must be 2D [N, num_groups]")
+            _f16(x, name + "(x)")
+            _check(x.numel() == K, name, ": x must hold K values")
+            _f16(y, name + "(y)")
+            _check(y.numel() == W.size(0), name, ": y must hold N values")
+            _check(-1 <= dep < i, name, ": dep must be -1 or an earlier task index")
+            d = _same_device(W, scale, x, y)
+            _check(dev is None or d == dev, name, ": all tasks must be on one device")
+            dev = d
+            arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), y.data_ptr(), W.size(0), K, group_size,
+                               scale.size(1), dep)
+        self._arr, self.n, self.device = arr, n, dev
+        self._keep = [t[:4] for t in tasks]
+
+    def run(self) -> None:
+        dev = self.device
+        with torch.cuda.device(dev):
+            ws = _workspace("batch", dev, lib().soinfer_gemv_batch_workspace_bytes(self.n))
+            _call("soinfer_gemv_w4a16_batch", ctypes.addressof(self._arr), self.n, ws.data_ptr(), ws.numel(),
+                  _stream(dev))
+
+
+def gemv_w4a16_batch(tasks) -> None:
+    """Runs the tasks (see GemvBatch) as one persistent kernel on the current stream."""
+    GemvBatch(tasks).run()
+
+
+def reset_workspaces() -> None:
+    """Re-zero every cached workspace (needed after a device error left a
+    kernel's self-resetting counters dirty)."""
+    for ws in _workspaces.values():
+        ws.zero_()
 
 
 def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: torch.Tensor | None = None):

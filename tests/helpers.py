@@ -18,7 +18,10 @@ REL_L2 = 1e-3
 ELEM_ABS, ELEM_REL = 1e-2, 5e-3
 
 
-def assert_close(actual, expected, label: str, max_abs: float = MAX_ABS, rel_l2: float = REL_L2) -> None:
+def assert_close(actual, expected, label: str, max_abs: float | None = MAX_ABS, rel_l2: float = REL_L2) -> None:
+    """max_abs=None skips the absolute bound (for unit-variance test data whose
+    outputs are large enough that one fp16 ulp exceeds 1e-2; the reference
+    tests use only the magnitude-scaled bound there)."""
     a = (actual.detach().float().cpu().numpy() if isinstance(actual, torch.Tensor) else np.asarray(actual)).astype(
         np.float64)
     e = (expected.detach().float().cpu().numpy() if isinstance(expected, torch.Tensor) else np.asarray(expected)).astype(
@@ -28,7 +31,7 @@ def assert_close(actual, expected, label: str, max_abs: float = MAX_ABS, rel_l2:
     diff = np.abs(a - e)
     mx = float(diff.max()) if diff.size else 0.0
     rel = float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30)) if diff.size else 0.0
-    assert mx <= max_abs, f"{label}: max-abs {mx:.3e} > {max_abs}"
+    assert max_abs is None or mx <= max_abs, f"{label}: max-abs {mx:.3e} > {max_abs}"
     assert rel <= rel_l2, f"{label}: rel-L2 {rel:.3e} > {rel_l2}"
     bound = ELEM_ABS + ELEM_REL * np.abs(e)
     assert np.all(diff < bound), f"{label}: elementwise bound violated (worst {float((diff - bound).max()):.3e})"

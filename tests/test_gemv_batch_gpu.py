@@ -1,0 +1,114 @@
+"""Persistent batched INT4 GEMV (soinfer_gemv_w4a16_batch) parity on the GPU:
+independent and chained tasks at the BASELINE config shapes against the
+float64 oracle, exact basis-vector probes through the biased-MMA path,
+determinism across launches (the counters reset themselves), the per-task
+fallback for shapes outside the fast path, and argument checks."""
+import numpy as np
+import pytest
+import torch
+
+import soinfer.ops as ops
+from oracle import reference_port as port
+from soinfer import _C
+from soinfer.quant import formats, pack
+from tests.helpers import assert_close, fp16_randn, int4_weights
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _dev(w):
+    return w[0].to(DEV), w[1].to(DEV), w[2]
+
+
+@pytest.mark.parametrize("shapes", [
+    [(6144, 2048), (2048, 6144), (3072, 2048)],
+    [(17408, 5120), (5120, 17408), (1024, 5120)],
+    [(16, 128), (1, 256), (300, 1024), (6144, 2048)],
+])
+def test_independent_tasks_match_oracle(shapes):
+    tasks, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        p, s, pk = int4_weights(n, k, 128, seed=10 + i)
+        x = fp16_randn(pk, 20 + i)
+        y = torch.empty(n, dtype=torch.float16, device=DEV)
+        tasks.append((p.to(DEV), s.to(DEV), x.to(DEV), y, pk, 128, -1))
+        refs.append(port.gemv_w4a16(p.numpy(), s.numpy(), x.numpy(), pk, 128))
+    _C.gemv_w4a16_batch(tasks)
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    for i, t in enumerate(tasks):
+        assert_close(t[3], refs[i], f"batch task {i} {shapes[i]}")
+
+
+def test_chained_gate_down_layers():
+    H, I, L = 2048, 6144, 8
+    x0 = fp16_randn(H, 1).to(DEV)
+    layers = [(int4_weights(I, H, 128, seed=2 * l), int4_weights(H, I, 128, seed=2 * l + 1)) for l in range(L)]
+    ys = [torch.empty(I, dtype=torch.float16, device=DEV) for _ in range(L)]
+    outs = [torch.empty(H, dtype=torch.float16, device=DEV) for _ in range(L)]
+    tasks = []
+    x = x0
+    for l, (gw, dw) in enumerate(layers):
+        tasks.append((gw[0].to(DEV), gw[1].to(DEV), x, ys[l], H, 128, -1 if l == 0 else 2 * l - 1))
+        tasks.append((dw[0].to(DEV), dw[1].to(DEV), ys[l], outs[l], I, 128, 2 * l))
+        x = outs[l]
+    batch = _C.GemvBatch(tasks)
+    for rep in range(3):
+        batch.run()
+        torch.cuda.synchronize()
+        assert _C.device_errors() == 0
+        # every task against the oracle evaluated on the same (fp16) input the kernel read
+        for l, (gw, dw) in enumerate(layers):
+            xin = x0 if l == 0 else outs[l - 1]
+            # activations grow ~1.4x per layer; beyond unit scale one fp16 ulp
+            # exceeds 1e-2, so the magnitude-scaled bounds apply
+            assert_close(ys[l], port.gemv_w4a16(gw[0].numpy(), gw[1].numpy(), xin.cpu().numpy(), H, 128), f"gate {l}",
+                         max_abs=None)
+            assert_close(outs[l], port.gemv_w4a16(dw[0].numpy(), dw[1].numpy(), ys[l].cpu().numpy(), I, 128),
+                         f"down {l}", max_abs=None)
+        if rep == 0:
+            first = [o.clone() for o in outs]
+        else:
+            assert all(torch.equal(a, b) for a, b in zip(first, outs)), "batch results differ across launches"
+
+
+def test_basis_vectors_exact_through_batch():
+    torch.manual_seed(2)
+    N, K = 64, 1024
+    W = torch.randn(N, K) * 3.0
+    qt = formats.quantize(W, formats.QuantConfig(bits=4, granularity="group", group_size=128))
+    packed, _ = pack.pack_int4(qt.qweight)
+    deq = formats.dequantize(qt).half().to(DEV)
+    Wd, sd = packed.to(DEV), qt.scale.to(DEV)
+    eye = torch.eye(K, device=DEV, dtype=torch.float16)
+    cols = list(range(0, K, 37))
+    ys = [torch.empty(N, dtype=torch.float16, device=DEV) for _ in cols]
+    _C.gemv_w4a16_batch([(Wd, sd, eye[k].contiguous(), ys[i], K, 128, -1) for i, k in enumerate(cols)])
+    torch.cuda.synchronize()
+    for i, k in enumerate(cols):
+        assert torch.equal(ys[i], deq[:, k]), f"column {k}"
+
+
+def test_fallback_path_matches_single_op():
+    # K not a multiple of 128 -> ordered single-GEMV launches
+    p, s, pk = int4_weights(100, 200, 8, seed=3)
+    x = fp16_randn(pk, 4).to(DEV)
+    y = torch.empty(100, dtype=torch.float16, device=DEV)
+    _C.gemv_w4a16_batch([(p.to(DEV), s.to(DEV), x, y, pk, 8, -1)])
+    assert torch.equal(y, ops.gemv_w4a16_group_lop3(p.to(DEV), s.to(DEV), x, pk, 8))
+
+
+def test_batch_rejects_bad_tasks():
+    p, s, pk = int4_weights(16, 256, 128, seed=5)
+    Wd, sd = p.to(DEV), s.to(DEV)
+    x = torch.randn(256, device=DEV, dtype=torch.float16)
+    y = torch.empty(16, device=DEV, dtype=torch.float16)
+    with pytest.raises(RuntimeError):
+        _C.gemv_w4a16_batch([(Wd, sd, x, y, 256, 128, 0)])  # self dependency
+    with pytest.raises(RuntimeError):
+        _C.gemv_w4a16_batch([(Wd, sd, x[:128], y, 256, 128, -1)])
+    with pytest.raises(RuntimeError):
+        _C.gemv_w4a16_batch([(Wd, sd[:, :1].contiguous(), x, y, 256, 128, -1)])
+    with pytest.raises(RuntimeError):
+        _C.gemv_w4a16_batch([])
