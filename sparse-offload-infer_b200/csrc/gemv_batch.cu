@@ -2,35 +2,54 @@
 // (y_i = dequant(W_i, S_i) x_i), optionally chained (x_i = y_j of an earlier
 // task j) -- a decode layer's or a whole token's weight stream in one kernel.
 //
-// Why: a batch-1 decode GEMV moves ~6.7 MB, i.e. ~42 KB per SM, while an SM
-// needs ~100 KB of copies in flight to run HBM at full rate; a single GEMV
-// launch is therefore latency-bound no matter how it is written.  Weights do
-// not depend on activations, so here a producer warp per CTA streams the
-// weight pieces of task after task through a deep shared-memory ring
-// (cp.async.bulk + full/empty mbarriers) without ever waiting for x; a loader
-// warp double-buffers each task's x (bulk copy), waiting first for the task it
-// depends on (a per-task completion counter in global memory reaching the grid
-// size); consumer warps compute as weights and x land.
+// Why: a batch-1 decode GEMV moves a few MB, i.e. tens of KB per SM, while an
+// SM needs well over 100 KB of copies in flight to run HBM at full rate; a
+// single GEMV launch is latency-bound however it is written.  Weights do not
+// depend on activations, so here one producer thread per CTA streams the
+// weight slabs of task after task into a shared-memory byte ring and never
+// waits for x.
 //
-// Per task each CTA owns a contiguous, equal slab of output rows (no
-// cross-CTA reduction).  Dot products: each packed word is turned into fp16
-// values biased by a constant with a single LOP3 per half2 -- (n^8)+1024 for
-// the low nibble of each byte pair, 16(n^8)+1024 for the high nibble -- and
-// fed to mma.sync.m16n8k16 (exact products, fp32 accumulation) in two chains
-// (low / high nibbles); the bias is removed per 128-K chunk with the chunk's
-// x sums: sum q x = (E - 1032 XL) + (O - 1152 XH) / 16.  That leaves ~0.6
-// SIMT instructions per INT4 value.
+// Work split: per task every CTA owns a contiguous, equal slab of output rows
+// (rows_per_cta = ceil(N / grid)), so a CTA's weights for a task are one
+// contiguous byte range of the packed matrix and its scales another.  The
+// slab is cut into items of whole 16-row tiles (as many as fit in
+// kMaxItemBytes); each item is exactly two bulk copies (cp.async.bulk, one
+// for the packed rows, one for their scale rows) completing on one mbarrier.
+// Items of any size share a circular byte ring, so the bytes in flight stay
+// near the ring size whatever the matrix shape.
 //
-// Every wait is bounded (%globaltimer); a timeout sets a device error bit and
-// the CTA drains its in-flight copies and exits.  The completion counters
-// (workspace) are reset to zero by the last CTA to finish, so a zeroed
-// workspace stays reusable across launches and CUDA-graph replays.
+// Roles (one CTA per SM, 19 warps):
+//   warps 0..15  consumers in two groups of 8 that take alternate tasks; a
+//                group splits K across its warps (chunk c of every tile goes
+//                to group warp c mod 8), tensor-core dot products, per-warp
+//                partial row sums into a double-buffered reduction area;
+//   warp 16      producer: ring allocation + the item copies;
+//   warp 17      x loader: waits for the task's dependency (a completion
+//                counter in global memory reaching the grid size), then loads
+//                x (L2) into a double-buffered x slot;
+//   warp 18      epilogue: sums the 8 partials per row, frees the partial
+//                buffer, writes y and -- only for a task that a later task
+//                depends on -- fences and publishes its completion counter.
+// All lanes of a warp wait on an mbarrier together: a lane-0 poll with the
+// rest of the warp parked in __syncwarp delays the hand-offs measurably.
+//
+// Dot products: each packed word becomes fp16 values biased by a constant
+// with one LOP3 per half2 -- (n^8)+1024 for the low nibble of each byte pair,
+// 16(n^8)+1024 for the high nibble -- fed to mma.sync.m16n8k16 (exact
+// products, fp32 accumulation) in two chains; the bias is removed per 128-K
+// chunk with the chunk's x sums: sum q x = (E - 1032 XL) + (O - 1152 XH) / 16.
+//
+// Every wait is bounded (%globaltimer) and also gives up once another warp of
+// the CTA has raised the abort flag; a timeout sets a device error bit, the
+// producer waits (bounded) for its copies in flight, and the CTA
+// exits.  The completion counters (workspace) are reset to zero by the last
+// CTA to finish, so a zeroed workspace stays reusable across launches and
+// CUDA-graph replays; after a reported error the caller re-zeroes it.
 //
 // Reference semantics per task: csrc/kernels/gemv_w4a16_group.cu:77-127 of
 // sparse-offload-infer.
 #include "common.cuh"
 #include "kernels.h"
-#include "launch.cuh"
 
 namespace soinfer {
 
@@ -38,33 +57,22 @@ namespace {
 
 __device__ int g_gemv_batch_error;
 
-constexpr int kCWarps = 16;                   // consumer warps (0..15)
-constexpr int kCThreads = kCWarps * 32;
-constexpr int kPWarps = 4;                    // producer warps (16..19): one warp issues copies serially,
-                                              // so the 16 row copies of a stage are spread over 4 warps
-constexpr int kLoaderWarp = kCWarps + kPWarps;
-constexpr int kThreads = (kCWarps + kPWarps + 1) * 32;
-constexpr int kMaxStages = 10;
-constexpr int kPieceChunks = 16;              // 128-K chunks per stage row piece: one per consumer warp
-constexpr int kMaxPieces = 16;                // K <= 32768
-constexpr int kSlotPad = 64;
-constexpr int kMaxTilesPerTask = 8;           // 16-row tiles per CTA per task
+constexpr int kCWarps = 16;
+constexpr int kGroupWarps = 8;                // consumer warps per task (two groups alternate tasks)
+constexpr int kProducerWarp = kCWarps;
+constexpr int kLoaderWarp = kCWarps + 1;
+constexpr int kEpilogueWarp = kCWarps + 2;
+constexpr int kThreads = (kCWarps + 3) * 32;
+constexpr int kMaxItems = 16;                 // item descriptors (mbarrier pairs) in flight
+constexpr int kMaxTiles = 8;                  // 16-row tiles per CTA per task
+constexpr int kRedRows = kMaxTiles * 16;
+constexpr int kRedBytes = 2 * kGroupWarps * kRedRows * 4;
+constexpr int kMaxItemBytes = 52 * 1024;
+constexpr int kMaxChunksPerWarp = 8;          // K <= kGroupWarps * kMaxChunksPerWarp * 128 = 8192
+constexpr int kSmemLimit = 227 * 1024;
 constexpr uint64_t kWaitNs = 1000000000ull;   // 1 s
-constexpr int kSmemBudget = 220 * 1024;
 
-__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-
-// Named barrier over `n` threads that also ORs `pred` across them: every
-// participant gets the same answer (uniform control flow after the barrier).
-__device__ __forceinline__ bool named_sync_or(int id, int n, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(out)
-      : "r"((uint32_t)pred), "r"(id), "r"(n)
-      : "memory");
-  return out != 0;
-}
+__host__ __device__ __forceinline__ int round128(int v) { return (v + 127) & ~127; }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
   int v;
@@ -72,293 +80,431 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy through L2 (x may have been
+// written by other SMs during this kernel), and the arrive-on that signals
+// an mbarrier once all of this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Row sums of one 128-K chunk for the thread's two MMA rows (see file comment).
-__device__ __forceinline__ void chunk_dot_biased(const uint4 wa, const uint4 wb, const uint4 xf[4], float xl,
-                                                 float xh, float& s0, float& s1) {
+// Bounded wait for the phase of `bar` with the given parity, giving up early
+// once the CTA's abort flag is raised.  Called by every lane of a warp; the
+// result is made warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+  bool ok = mbar_try_wait(bar, parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      if (mbar_try_wait(bar, parity)) {
+        ok = true;
+        break;
+      }
+      if (*abort_flag || globaltimer_ns() - t0 > kWaitNs) break;
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ void raise_abort(volatile int* abort_flag) {
+  if ((threadIdx.x & 31) == 0) {
+    *abort_flag = 1;
+    atomicOr(&g_gemv_batch_error, kErrCopyTimeout);
+  }
+}
+
+// Bias of one 128-K chunk of x as seen by chunk_dot: the MMAs there multiply
+// x by 1024 + (s + 8) (low-nibble positions: x0 x1 x4 x5 of each 8-group) and
+// 1024 + 16 (s + 8) (high positions x2 x3 x6 x7, later scaled by 1/16), so
+// sum q x = chunk_dot - bias with bias = 1032 XL + 72 XH.  One MMA computes it:
+// A = 1032 in k-columns 0..7 and 72 in 8..15 (every row), and column n of B
+// holds the 16 values of x groups 2n and 2n + 1 (low pairs in k 0..7, high
+// pairs in k 8..15), so D[*][n] is the bias share of 16 of the chunk's 128
+// values; the 8 columns are summed across the 4 lanes of a row group.
+// `xc` is the chunk's 256 bytes of x in shared memory; every lane gets the value.
+__device__ __forceinline__ float chunk_bias(const uint8_t* xc, int g, int t) {
+  const uint32_t* xw = reinterpret_cast<const uint32_t*>(xc + (2 * g + (t >> 1)) * 16 + (t & 1) * 8);
+  const uint32_t a[4] = {0x64086408u, 0x64086408u, 0x54805480u, 0x54805480u};  // 1032 1032 | 72 72
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_16816(d, a, xw[0], xw[1]);  // b0 = (x0, x1) or (x4, x5), b1 = (x2, x3) or (x6, x7)
+  float bias = d[0] + d[1];
+  bias += __shfl_xor_sync(0xffffffffu, bias, 1);
+  bias += __shfl_xor_sync(0xffffffffu, bias, 2);
+  return bias;
+}
+
+// Biased row sums of one 128-K chunk for the thread's two MMA rows (see file
+// comment): returns E + O / 16 for rows g and g + 8, in four independent MMA
+// chains of depth two.
+__device__ __forceinline__ void chunk_dot(const uint4 wa, const uint4 wb, const uint4 xf[4], float& s0, float& s1) {
   const uint32_t r0[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t r1[4] = {wb.x, wb.y, wb.z, wb.w};
-  float e[4] = {0.f, 0.f, 0.f, 0.f}, o[4] = {0.f, 0.f, 0.f, 0.f};
+  float e[2][4] = {}, o[2][4] = {};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t t0 = r0[j] >> 8, t1 = r1[j] >> 8;
     const uint32_t ae[4] = {lop3_and_xor(r0[j], 0x000f000fu, 0x64086408u), lop3_and_xor(r1[j], 0x000f000fu, 0x64086408u),
                             lop3_and_xor(t0, 0x000f000fu, 0x64086408u), lop3_and_xor(t1, 0x000f000fu, 0x64086408u)};
-    mma_16816(e, ae, xf[j].x, xf[j].z);  // (v0,v1) with x0x1, (v4,v5) with x4x5
+    mma_16816(e[j & 1], ae, xf[j].x, xf[j].z);  // (v0,v1) with x0x1, (v4,v5) with x4x5
     const uint32_t ao[4] = {lop3_and_xor(r0[j], 0x00f000f0u, 0x64806480u), lop3_and_xor(r1[j], 0x00f000f0u, 0x64806480u),
                             lop3_and_xor(t0, 0x00f000f0u, 0x64806480u), lop3_and_xor(t1, 0x00f000f0u, 0x64806480u)};
-    mma_16816(o, ao, xf[j].y, xf[j].w);  // (v2,v3) with x2x3, (v6,v7) with x6x7
+    mma_16816(o[j & 1], ao, xf[j].y, xf[j].w);  // (v2,v3) with x2x3, (v6,v7) with x6x7
   }
-  const float bl = 1032.f * xl, bh = 1152.f * xh;
-  s0 = (e[0] - bl) + (o[0] - bh) * 0.0625f;
-  s1 = (e[2] - bl) + (o[2] - bh) * 0.0625f;
+  s0 = fmaf(o[0][0] + o[1][0], 0.0625f, e[0][0] + e[1][0]);
+  s1 = fmaf(o[0][2] + o[1][2], 0.0625f, e[0][2] + e[1][2]);
 }
 
 struct TaskView {
-  int rows, tiles, chunks, pieces;
+  int rows, tiles, chunks;
   int64_t row0;
 };
 
 __device__ __forceinline__ TaskView task_view(const GemvBatchTask& tk, int cta) {
   TaskView v;
   v.row0 = (int64_t)cta * tk.rows_per_cta;
-  int rows = tk.N - (int)v.row0;
+  const int rows = tk.N - (int)v.row0;
   v.rows = rows < 0 ? 0 : (rows > tk.rows_per_cta ? tk.rows_per_cta : rows);
   v.tiles = (v.rows + 15) / 16;
   v.chunks = tk.K / 128;
-  v.pieces = (v.chunks + kPieceChunks - 1) / kPieceChunks;
   return v;
 }
 
-// Lane 0 polls the barrier (with back-off) while the other lanes park in
-// __syncwarp; the result is broadcast so the warp decides uniformly.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) {
-    if (!mbar_try_wait(bar, parity)) {
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > timeout_ns) {
-          ok = 0;
-          break;
-        }
-        __nanosleep(20);
+// Rows of the item covering tiles [tile0, tile0 + nt) of the CTA's slab.
+__device__ __forceinline__ int item_rows(const TaskView& v, int tile0, int nt) {
+  const int r = v.rows - tile0 * 16;
+  return r < nt * 16 ? r : nt * 16;
+}
+
+// Per-task state of one consumer warp (everything that depends only on the
+// task is computed once; the kernel is issue-bound).
+struct ConsumerTask {
+  const uint4* xq;        // this lane's 64 x bytes of its first chunk
+  const float* sbias;     // chunk_bias of each owned chunk (shared memory)
+  float* rr;              // this warp's partial rows
+  int row_bytes, G, g, cpg, c_first;
+  uint32_t tmask;         // tiles this warp works on
+};
+
+// One unit: 16 rows x one 128-K chunk (chunk c_first + i * kGroupWarps);
+// w0 / w1 point at rows g / g + 8 of the tile at the first owned chunk.
+__device__ __forceinline__ void consume_unit(const uint4 xf[4], const uint8_t* w0, const uint8_t* w1, float sc0,
+                                             float sc1, float bias, int i, float& acc0, float& acc1) {
+  const uint4 wa = *reinterpret_cast<const uint4*>(w0 + i * (kGroupWarps * 64));
+  const uint4 wb = *reinterpret_cast<const uint4*>(w1 + i * (kGroupWarps * 64));
+  float d0, d1;
+  chunk_dot(wa, wb, xf, d0, d1);
+  acc0 = fmaf(sc0, d0 - bias, acc0);
+  acc1 = fmaf(sc1, d1 - bias, acc1);
+}
+
+// The warp's units of one item: for each owned tile of the item, nm chunks
+// (stride kGroupWarps); the tile's partial rows go to the reduction buffer
+// (the 4 lanes of a row group hold the same value and all store it).  NM is
+// the chunk count when it is 1 or 2 (x fragments and biases stay in
+// registers, every offset is an immediate); NM == 0 is the rolled loop over
+// nm chunks.  G128: group size 128, one scale column per chunk.
+template <int NM, bool G128>
+__device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint8_t* wbase, const float* sbase,
+                                              int rows, int tile0, int nt, int nm) {
+  uint4 xr[2][4];
+  float br[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < NM; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xr[i][j] = ct.xq[i * (kGroupWarps * 16) + j];
+    br[i] = ct.sbias[i];
+  }
+  const int rstep = 16 * ct.row_bytes, sstep = 16 * ct.G;
+  const uint8_t* w0 = wbase + ct.g * ct.row_bytes;
+  const float* s0p = sbase + ct.g * ct.G + (G128 ? ct.c_first : 0);
+  for (int tt = tile0; tt < tile0 + nt; ++tt, w0 += rstep, s0p += sstep) {
+    if (!((ct.tmask >> tt) & 1u)) continue;
+    const uint8_t* w1 = w0 + 8 * ct.row_bytes;
+    const float* s1p = s0p + 8 * ct.G;
+    const int last = rows - 1 - (tt - tile0) * 16;  // last valid row of this tile (ragged tile: repeat it)
+    const uint8_t* wa = w0;
+    const float* sa = s0p;
+    if (ct.g > last) wa -= (ct.g - last) * ct.row_bytes, sa -= (ct.g - last) * ct.G;
+    if (ct.g + 8 > last) w1 -= (ct.g + 8 - last) * ct.row_bytes, s1p -= (ct.g + 8 - last) * ct.G;
+    float acc0 = 0.f, acc1 = 0.f;
+    if (NM > 0) {
+#pragma unroll
+      for (int i = 0; i < NM; ++i) consume_unit(xr[i], wa, w1, sa[i * kGroupWarps], s1p[i * kGroupWarps], br[i], i, acc0, acc1);
+    } else {
+#pragma unroll 1
+      for (int i = 0; i < nm; ++i) {
+        uint4 xf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xf[j] = ct.xq[i * (kGroupWarps * 16) + j];
+        const int sc = G128 ? i * kGroupWarps : (ct.c_first + i * kGroupWarps) / ct.cpg;
+        consume_unit(xf, wa, w1, sa[sc], s1p[sc], ct.sbias[i], i, acc0, acc1);
       }
     }
+    ct.rr[tt * 16 + ct.g] = acc0;
+    ct.rr[tt * 16 + ct.g + 8] = acc1;
   }
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
 }
 
-__device__ __forceinline__ void red_release_add(int* p, int v) {
-  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-
-// Low- / high-nibble-position sums of one 128-K chunk of x: each thread sums
-// its 32-value slice, then the 4 lanes of a groupID (t = 0..3) combine.
-__device__ __forceinline__ void chunk_xsums(const uint4 xf[4], float& xl, float& xh) {
-  float lo = 0.f, hi = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 a = __half22float2(u32_as_h2(xf[j].x)), b = __half22float2(u32_as_h2(xf[j].y));
-    const float2 c = __half22float2(u32_as_h2(xf[j].z)), d = __half22float2(u32_as_h2(xf[j].w));
-    lo += (a.x + a.y) + (c.x + c.y);
-    hi += (b.x + b.y) + (d.x + d.y);
-  }
-  lo += __shfl_xor_sync(0xffffffffu, lo, 1);
-  hi += __shfl_xor_sync(0xffffffffu, hi, 1);
-  lo += __shfl_xor_sync(0xffffffffu, lo, 2);
-  hi += __shfl_xor_sync(0xffffffffu, hi, 2);
-  xl = lo;
-  xh = hi;
-}
-
+// 19 warps put 5 warps on some of the SM's four 16K-register partitions:
+// at most 96 registers per thread.
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_batch_kernel(const __grid_constant__ GemvBatchParams B, int* __restrict__ counters) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* xbuf = smem;                                     // [2][x_bytes]
-  uint8_t* slots = smem + 2 * B.x_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(slots + B.stages * B.slot_bytes);
-  uint64_t* empty = full + kMaxStages;
-  uint64_t* xfull = empty + kMaxStages;
-  uint64_t* xempty = xfull + 2;
-  float* red = reinterpret_cast<float*>(xempty + 2);        // [kCWarps][kMaxTilesPerTask*16]
+  uint8_t* ring = smem;                                                  // [ring_bytes]
+  uint8_t* xbuf = smem + B.ring_bytes;                                   // [2][x_bytes]
+  float* red = reinterpret_cast<float*>(xbuf + 2 * B.x_bytes);          // [2][kGroupWarps][kRedRows]
+  __shared__ uint64_t full[kMaxItems], empty[kMaxItems];
+  __shared__ uint64_t xfull[2], xempty[2], rfull[2], rempty[2];
+  __shared__ int item_off[kMaxItems];
+  __shared__ float s_bias[kCWarps][kMaxChunksPerWarp];
   __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x;
   const int grid = gridDim.x;
-  const int S = B.stages;
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < kMaxItems; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCWarps);
+      mbar_init(&empty[s], kGroupWarps);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], kCWarps);
+      mbar_init(&xfull[s], 32);  // one cp.async arrive-on per loader lane
+      mbar_init(&xempty[s], kGroupWarps);
+      mbar_init(&rfull[s], kGroupWarps);
+      mbar_init(&rempty[s], 1);
     }
     fence_mbar_init();
     s_abort = 0;
   }
   __syncthreads();
 
-  if (warp >= kCWarps && warp < kLoaderWarp) {
-    // ------------------------------------------------------------ producers
-    // Items are ordered piece-major within a task (piece p of every tile,
-    // then piece p + 1), matching the consumers.  Producer warp pw issues the
-    // row copies of rows pw, pw + 4, ... (lanes 0..3); warp 0 also posts the
-    // stage's expected byte count and copies the tile's scale rows.
-    const int pw = warp - kCWarps;
-    int item = 0;
+  if (warp == kProducerWarp) {
+    // ------------------------------------------------------------ producer
+    // Ring allocation is FIFO: items are consumed in issue order, so the
+    // occupied bytes are [item_off[oldest], head) circularly.
+    int head = 0, issued = 0, oldest = 0;
     bool stop = false;
     for (int ti = 0; ti < B.num && !stop; ++ti) {
       const GemvBatchTask& tk = B.tasks[ti];
       const TaskView v = task_view(tk, cta);
-      const int64_t row_bytes = tk.K / 2;
-      const uint32_t srow = (uint32_t)tk.G * 4u;
-      for (int piece = 0; piece < v.pieces && !stop; ++piece) {
-        const int c0 = piece * kPieceChunks;
-        const int pc = min(kPieceChunks, v.chunks - c0);
-        for (int tile = 0; tile < v.tiles; ++tile, ++item) {
-          const int slot = item % S;
-          if (item >= S && !mbar_wait_bounded(&empty[slot], (uint32_t)(((item / S) - 1) & 1), kWaitNs)) {
+      const int row_bytes = tk.K / 2;
+      const int srow = tk.G * 4;
+      for (int tile0 = 0; tile0 < v.tiles && !stop; tile0 += tk.tiles_per_item) {
+        const int nt = min(tk.tiles_per_item, v.tiles - tile0);
+        const int rows = item_rows(v, tile0, nt);
+        const int wb = rows * row_bytes, sb = rows * srow;
+        const int bytes = round128(wb) + round128(sb);
+        if (head + bytes > B.ring_bytes) head = 0;
+        while (issued > oldest) {
+          const int start = item_off[oldest % kMaxItems];
+          const bool overlap = head <= start && head + bytes > start;
+          if (issued - oldest < kMaxItems && !overlap) break;
+          if (!warp_wait(&empty[oldest % kMaxItems], (uint32_t)((oldest / kMaxItems) & 1), abort_flag)) {
             stop = true;
             break;
           }
-          if (s_abort) {
-            stop = true;
-            break;
-          }
-          const int valid = min(16, v.rows - tile * 16);
-          const int64_t r = v.row0 + tile * 16;
-          uint8_t* sb = slots + slot * B.slot_bytes;
-          if (pw == 0 && lane == 0)
-            mbar_arrive_expect_tx(&full[slot], (uint32_t)(valid * pc * 64) + (uint32_t)valid * srow);
-          const int row = lane * kPWarps + pw;
-          if (lane < 4 && row < valid)
-            bulk_g2s(sb + row * B.slot_stride, tk.W + (r + row) * row_bytes + (int64_t)c0 * 64, (uint32_t)(pc * 64),
-                     &full[slot]);
-          if (pw == 0 && lane == 4) bulk_g2s(sb + B.scale_off, tk.S + r * tk.G, (uint32_t)valid * srow, &full[slot]);
+          ++oldest;
         }
+        if (stop) break;
+        const int d = issued % kMaxItems;
+        __syncwarp();  // every lane has read item_off[] before lane 0 rewrites a slot
+        if (lane == 0) {
+          item_off[d] = head;
+          const int64_t r = v.row0 + tile0 * 16;
+          mbar_arrive_expect_tx(&full[d], (uint32_t)(wb + sb));
+          bulk_g2s(ring + head, tk.W + r * row_bytes, (uint32_t)wb, &full[d]);
+          bulk_g2s(ring + head + round128(wb), tk.S + r * tk.G, (uint32_t)sb, &full[d]);
+        }
+        __syncwarp();
+        head += bytes;
+        ++issued;
       }
     }
-    if (stop && lane == 0) {
-      s_abort = 1;
-      atomicOr(&g_gemv_batch_error, kErrCopyTimeout);
-    }
-    // drain: every issued stage must land before this CTA's shared memory is released
-    for (int q = item - S; q < item; ++q)
-      if (q >= 0) (void)mbar_wait_bounded(&full[q % S], (uint32_t)((q / S) & 1), kWaitNs / 4);
+    if (stop) raise_abort(abort_flag);
+    // every issued copy must land before this CTA's shared memory is released
+    for (int q = max(oldest, issued - kMaxItems); q < issued; ++q)
+      (void)mbar_wait_bounded(&full[q % kMaxItems], (uint32_t)((q / kMaxItems) & 1), kWaitNs / 4);
   } else if (warp == kLoaderWarp) {
     // ------------------------------------------------------------ x loader
-    int issued = 0;
+    int a = 0;  // index among this CTA's active (rows > 0) tasks
     bool stop = false;
     for (int ti = 0; ti < B.num && !stop; ++ti) {
       const GemvBatchTask& tk = B.tasks[ti];
-      const int xs = ti & 1;
-      int ok = 1;
-      if (lane == 0) {
-        if (ti >= 2 && !mbar_wait_bounded(&xempty[xs], (uint32_t)(((ti >> 1) - 1) & 1), kWaitNs)) ok = 0;
-        if (ok && tk.dep >= 0) {
-          const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire(counters + tk.dep) < grid) {
-            if (s_abort || globaltimer_ns() - t0 > kWaitNs) {
-              ok = 0;
-              break;
-            }
-            __nanosleep(32);
-          }
-          fence_proxy_async_global();  // x was written by other SMs through the generic proxy
-        }
-        if (s_abort) ok = 0;
-        if (ok) mbar_arrive_expect_tx(&xfull[xs], (uint32_t)tk.K * 2u);
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
+      if (task_view(tk, cta).rows == 0) continue;
+      const int xs = a & 1;
+      if (a >= 2 && !warp_wait(&xempty[xs], (uint32_t)(((a >> 1) - 1) & 1), abort_flag)) {
         stop = true;
         break;
       }
-      if (lane == 0) bulk_g2s(xbuf + xs * B.x_bytes, tk.x, (uint32_t)tk.K * 2u, &xfull[xs]);
-      __syncwarp();
-      issued = ti + 1;
+      if (tk.dep >= 0) {
+        // every lane polls the same word (one request); the exit is uniform
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+          const bool done = ld_acquire(counters + tk.dep) >= grid;
+          if (__all_sync(0xffffffffu, done)) break;
+          const bool give_up = *abort_flag || globaltimer_ns() - t0 > kWaitNs;
+          if (__any_sync(0xffffffffu, give_up)) {
+            stop = true;
+            break;
+          }
+        }
+        if (stop) break;
+      }
+      // x through cp.async (all 16-byte pieces in flight at once), not a bulk
+      // copy: a bulk copy would queue behind the producer's weight copies in
+      // this SM's copy engine.  Each lane's arrive-on fires when its copies land.
+      const uint4* src = reinterpret_cast<const uint4*>(tk.x);
+      uint4* dst = reinterpret_cast<uint4*>(xbuf + xs * B.x_bytes);
+      const int n16 = tk.K / 8;
+      for (int u = lane; u < n16; u += 32) cp_async_16(dst + u, src + u);
+      cp_async_arrive_noinc(&xfull[xs]);
+      ++a;
     }
-    if (stop && lane == 0) {
-      s_abort = 1;
-      atomicOr(&g_gemv_batch_error, kErrCopyTimeout);
-    }
-    if (lane == 0)
-      for (int q = issued - 2; q < issued; ++q)
-        if (q >= 0) (void)mbar_wait_bounded(&xfull[q & 1], (uint32_t)((q >> 1) & 1), kWaitNs / 4);
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ consumers
-    // Abort decisions are made only through named_sync_or, so all consumer
-    // threads leave the task loop together; a failed wait marks the thread
-    // `bad`, after which it stops waiting and skips work until that barrier.
-    const int g = lane >> 2, t = lane & 3;
-    const int lr0 = g, lr1 = g + 8;
-    int item = 0;
-    bool bad = false;
-    for (int ti = 0; ti < B.num; ++ti) {
+    if (stop) raise_abort(abort_flag);
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into this CTA's shared memory outlives it
+  } else if (warp == kEpilogueWarp) {
+    // ------------------------------------------------------------ epilogue
+    int a = 0;
+    bool stop = false;
+    for (int ti = 0; ti < B.num && !stop; ++ti) {
       const GemvBatchTask& tk = B.tasks[ti];
       const TaskView v = task_view(tk, cta);
-      const int xsl = ti & 1;
-      if (!bad && !warp_wait(&xfull[xsl], (uint32_t)((ti >> 1) & 1), kWaitNs)) bad = true;
-      const uint4* xs = reinterpret_cast<const uint4*>(xbuf + xsl * B.x_bytes);
-      float acc0[kMaxTilesPerTask], acc1[kMaxTilesPerTask];
-#pragma unroll
-      for (int i = 0; i < kMaxTilesPerTask; ++i) acc0[i] = acc1[i] = 0.f;
-      for (int piece = 0; piece < v.pieces; ++piece) {
-        const int cg = piece * kPieceChunks + warp;  // the one chunk of this piece this warp owns
-        const bool mine = cg < v.chunks;
-        uint4 xf[4];
-        float xl = 0.f, xh = 0.f;
-        if (!bad && mine) {
-          const uint4* xc = xs + cg * 16 + t * 4;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) xf[j] = xc[j];
-          chunk_xsums(xf, xl, xh);
+      if (v.rows > 0) {
+        const int rb = a & 1;
+        if (!warp_wait(&rfull[rb], (uint32_t)((a >> 1) & 1), abort_flag)) {
+          stop = true;
+          break;
         }
-        const int grp = cg / tk.cpg;
+        const float* rr = red + rb * (kGroupWarps * kRedRows);
+        // warps holding partials of a row: the whole group, or -- with fewer chunks
+        // than group warps -- the `chunks` warps that own the row's tile
+        const int nsplit = v.chunks >= kGroupWarps ? 1 : kGroupWarps / v.chunks;
+        const int nw = v.chunks >= kGroupWarps ? kGroupWarps : v.chunks;
+        float sums[kRedRows / 32];
 #pragma unroll
-        for (int tile = 0; tile < kMaxTilesPerTask; ++tile) {
-          if (tile < v.tiles) {
-            const int slot = item % S;
-            if (!bad && !warp_wait(&full[slot], (uint32_t)((item / S) & 1), kWaitNs)) bad = true;
-            if (!bad && mine) {
-              const uint8_t* sb = slots + slot * B.slot_bytes;
-              const float* sc = reinterpret_cast<const float*>(sb + B.scale_off);
-              const uint4 wa = *reinterpret_cast<const uint4*>(sb + lr0 * B.slot_stride + warp * 64 + t * 16);
-              const uint4 wb = *reinterpret_cast<const uint4*>(sb + lr1 * B.slot_stride + warp * 64 + t * 16);
-              const int sr0 = min(tile * 16 + lr0, v.rows - 1) - tile * 16;
-              const int sr1 = min(tile * 16 + lr1, v.rows - 1) - tile * 16;
-              float d0, d1;
-              chunk_dot_biased(wa, wb, xf, xl, xh, d0, d1);
-              acc0[tile] = fmaf(sc[sr0 * tk.G + grp], d0, acc0[tile]);
-              acc1[tile] = fmaf(sc[sr1 * tk.G + grp], d1, acc1[tile]);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            ++item;
+        for (int i = 0; i < kRedRows / 32; ++i) {
+          const int r = lane + 32 * i;
+          sums[i] = 0.f;
+          if (r < v.rows) {
+            const int w0 = ((r >> 4) % nsplit) * nw;
+            for (int w = w0; w < w0 + nw; ++w) sums[i] += rr[w * kRedRows + r];
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[rb]);  // partials consumed: the consumers may refill the buffer
+#pragma unroll
+        for (int i = 0; i < kRedRows / 32; ++i) {
+          const int r = lane + 32 * i;
+          if (r < v.rows) tk.y[v.row0 + r] = __float2half_rn(sums[i]);
+        }
+        ++a;
+      }
+      if (tk.publish) {  // a later task reads this y: make it visible GPU-wide, then count this CTA in
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) red_release_add(counters + ti, 1);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&xempty[xsl]);  // this warp is done with the task's x
-      if (t == 0) {
-#pragma unroll
-        for (int tile = 0; tile < kMaxTilesPerTask; ++tile) {
-          if (tile < v.tiles) {
-            red[warp * (kMaxTilesPerTask * 16) + tile * 16 + lr0] = acc0[tile];
-            red[warp * (kMaxTilesPerTask * 16) + tile * 16 + lr1] = acc1[tile];
-          }
-        }
+    }
+    if (stop) raise_abort(abort_flag);
+  } else {
+    // ------------------------------------------------------------ consumers
+    // Two groups of kGroupWarps warps alternate over this CTA's active tasks
+    // (group = active index & 1, matching the x and partial double buffers),
+    // so each warp works on every other task with twice the chunks: the
+    // per-task overhead is paid by half the warps.
+    const int group = warp / kGroupWarps, gw = warp % kGroupWarps;
+    const int g = lane >> 2, t = lane & 3;
+    int item = 0, a = 0;
+    bool stop = false;
+    for (int ti = 0; ti < B.num && !stop; ++ti) {
+      const GemvBatchTask& tk = B.tasks[ti];
+      const TaskView v = task_view(tk, cta);
+      if (v.rows == 0) continue;
+      const int tpi = tk.tiles_per_item;
+      const int nitems = (v.tiles + tpi - 1) / tpi;
+      if ((a & 1) != group) {  // the other group's task
+        item += nitems;
+        ++a;
+        continue;
       }
-      if (named_sync_or(1, kCThreads, bad || s_abort)) {
-        bad = true;
+      const int row_bytes = tk.K / 2;
+      int c_first, nmine;
+      uint32_t tmask = 0xffu;
+      if (v.chunks >= kGroupWarps) {
+        c_first = gw, nmine = (v.chunks - gw + kGroupWarps - 1) / kGroupWarps;
+      } else {  // fewer chunks than group warps: warps also split the tiles
+        const int nsplit = kGroupWarps / v.chunks, tsel = gw / v.chunks;
+        c_first = gw % v.chunks, nmine = tsel < nsplit ? 1 : 0;
+        tmask = 0;
+        for (int tt = tsel; tt < kMaxTiles; tt += nsplit) tmask |= 1u << tt;
+      }
+      const int xs = a & 1, rb = a & 1;
+      if (!warp_wait(&xfull[xs], (uint32_t)((a >> 1) & 1), abort_flag)) {
+        stop = true;
         break;
       }
-      for (int r = tid; r < v.rows; r += kCThreads) {
-        float sum = 0.f;
-#pragma unroll
-        for (int w = 0; w < kCWarps; ++w) sum += red[w * (kMaxTilesPerTask * 16) + r];
-        tk.y[v.row0 + r] = __float2half_rn(sum);
+      ConsumerTask ct;
+      ct.xq = reinterpret_cast<const uint4*>(xbuf + xs * B.x_bytes) + c_first * 16 + t * 4;
+      ct.sbias = s_bias[warp];
+      ct.rr = red + rb * (kGroupWarps * kRedRows) + gw * kRedRows;
+      ct.row_bytes = row_bytes;
+      ct.G = tk.G;
+      ct.g = g;
+      ct.cpg = tk.cpg;
+      ct.c_first = c_first;
+      ct.tmask = tmask;
+      for (int i = 0; i < nmine; ++i) {
+        const float bias = chunk_bias(xbuf + xs * B.x_bytes + (c_first + i * kGroupWarps) * 256, g, t);
+        if (lane == 0) s_bias[warp][i] = bias;
       }
-      named_sync(1, kCThreads);  // all y rows of this CTA written; red free again
-      if (tid == 0) red_release_add(counters + ti, 1);  // release: cumulative over the barrier
+      __syncwarp();
+      if (a >= 2 && !warp_wait(&rempty[rb], (uint32_t)(((a >> 1) - 1) & 1), abort_flag)) {
+        stop = true;
+        break;
+      }
+      // 1, 2: unrolled (group size 128); 3: rolled, group size 128; 4: rolled, general; 0: idle
+      const int kind = nmine == 0 ? 0 : (tk.cpg == 1 ? (nmine <= 2 ? nmine : 3) : 4);
+      for (int tile0 = 0; tile0 < v.tiles; tile0 += tpi) {
+        const int nt = min(tpi, v.tiles - tile0);
+        const int rows = item_rows(v, tile0, nt);
+        const int d = item % kMaxItems;
+        if (!warp_wait(&full[d], (uint32_t)((item / kMaxItems) & 1), abort_flag)) {
+          stop = true;
+          break;
+        }
+        const uint8_t* ib = ring + item_off[d];
+        const uint8_t* wbase = ib + c_first * 64 + t * 16;
+        const float* sbase = reinterpret_cast<const float*>(ib + round128(rows * row_bytes));
+        if (kind == 1) consume_tiles<1, true>(ct, wbase, sbase, rows, tile0, nt, 1);
+        else if (kind == 2) consume_tiles<2, true>(ct, wbase, sbase, rows, tile0, nt, 2);
+        else if (kind == 3) consume_tiles<0, true>(ct, wbase, sbase, rows, tile0, nt, nmine);
+        else if (kind == 4) consume_tiles<0, false>(ct, wbase, sbase, rows, tile0, nt, nmine);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[d]);
+        ++item;
+      }
+      if (stop) break;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&xempty[xs]);  // this warp is done with the task's x
+        mbar_arrive(&rfull[rb]);   // and has written its partials
+      }
+      ++a;
     }
-    if (bad && tid == 0) {
-      s_abort = 1;
-      atomicOr(&g_gemv_batch_error, kErrCopyTimeout);
-    }
+    if (stop) raise_abort(abort_flag);
   }
   __syncthreads();
   if (tid == 0 && !s_abort) {
@@ -376,36 +522,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 int64_t gemv_batch_workspace_bytes(int64_t num_tasks) { return ((num_tasks + 1) * 4 + 255) / 256 * 256; }
 
 bool plan_gemv_batch(GemvBatchParams& B, int sms) {
-  int max_k = 0, max_g = 0;
+  int max_k = 0;
+  for (int i = 0; i < B.num; ++i) B.tasks[i].publish = 0;
+  for (int i = 0; i < B.num; ++i)
+    if (B.tasks[i].dep >= 0) B.tasks[B.tasks[i].dep].publish = 1;
   for (int i = 0; i < B.num; ++i) {
     GemvBatchTask& tk = B.tasks[i];
     tk.rows_per_cta = (tk.N + sms - 1) / sms;
-    if (tk.rows_per_cta > kMaxTilesPerTask * 16) return false;
+    if (tk.rows_per_cta > kMaxTiles * 16) return false;
+    if (tk.K % 128 != 0 || (tk.G * 4) % 16 != 0 || tk.K / 128 > kGroupWarps * kMaxChunksPerWarp) return false;
+    const int tile_bytes = round128(16 * (tk.K / 2)) + round128(16 * tk.G * 4);
+    if (tile_bytes > kMaxItemBytes) return false;  // rows too long for whole-row items
+    tk.tiles_per_item = kMaxItemBytes / tile_bytes;
     max_k = tk.K > max_k ? tk.K : max_k;
-    max_g = tk.G > max_g ? tk.G : max_g;
   }
   B.grid = sms;
-  if (max_k / 128 > kMaxPieces * kPieceChunks) return false;
-  B.x_bytes = (max_k * 2 + 127) / 128 * 128;
-  B.xsum_bytes = 0;
-  B.slot_stride = kPieceChunks * 64 + kSlotPad;
-  B.scale_off = 16 * B.slot_stride;
-  B.slot_bytes = B.scale_off + ((16 * max_g * 4 + 127) / 128) * 128;
-  const int fixed = 2 * B.x_bytes + (2 * kMaxStages + 4) * 8 + kCWarps * kMaxTilesPerTask * 16 * 4 + B.xsum_bytes;
-  int stages = (kSmemBudget - fixed) / B.slot_bytes;
-  if (stages > kMaxStages) stages = kMaxStages;
-  if (stages < 2) return false;
-  B.stages = stages;
-  B.smem_bytes = fixed + stages * B.slot_bytes;
+  B.x_bytes = round128(max_k * 2);
+  const int static_smem = 2048;  // mbarriers, item offsets, per-warp biases, flags (1 KB used)
+  B.ring_bytes = ((kSmemLimit - static_smem - 2 * B.x_bytes - kRedBytes - 256) / 128) * 128;
+  if (B.ring_bytes < kMaxItemBytes + 128) return false;
+  B.smem_bytes = B.ring_bytes + 2 * B.x_bytes + kRedBytes;
   return true;
 }
 
 cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+  static int attr_bytes = 0;  // callers serialise launches (the C ABI holds a mutex)
+  if (B.smem_bytes > attr_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B.smem_bytes);
     if (e != cudaSuccess) return e;
-    attr = true;
+    attr_bytes = B.smem_bytes;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(B.grid);

@@ -41,11 +41,12 @@ struct GemvBatchTask {
   const float* S;
   const half* x;
   half* y;
-  int N, K, G, cpg, dep, rows_per_cta;
+  int N, K, G, cpg, dep;
+  int rows_per_cta, tiles_per_item, publish;  // filled by plan_gemv_batch (publish: a later task depends on it)
 };
 constexpr int kMaxBatchTasks = 256;
 struct GemvBatchParams {
-  int num, grid, x_bytes, xsum_bytes, slot_stride, scale_off, slot_bytes, smem_bytes, stages;
+  int num, grid, x_bytes, ring_bytes, smem_bytes;
   GemvBatchTask tasks[kMaxBatchTasks];
 };
 int64_t gemv_batch_workspace_bytes(int64_t num_tasks);
