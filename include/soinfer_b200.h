@@ -199,6 +199,23 @@ int soinfer_gemv_w4a16_sparse_accumulate(const uint8_t* Wq_sel, const float* sca
                                          int64_t group_size, int64_t num_groups, void* workspace,
                                          int64_t workspace_bytes, void* stream);
 
+/* No-allocation form of soinfer_gemv_w4a16_sparse_accumulate (no reference
+ * counterpart: the reference allocates its output and has no workspace).
+ * Same arguments, results bit-identical, but the scratch is a per-device
+ * static device array of 512 KiB instead of a caller workspace, for callers
+ * that cannot hand over memory (e.g. a decode loop with no allocator at
+ * hand).  Limits: soinfer_sparse_workspace_bytes(H, k) must fit in 512 KiB
+ * (every shape up to H = 16384 needs ~0.3 MiB; larger ones return
+ * SOINFER_ERR_INVALID_ARGUMENT); the scratch is shared, so two calls on one
+ * device that overlap in time (different streams, or host threads) race on
+ * it -- serialise them; the first call on each device does a one-time set-up
+ * (symbol lookup and an async clear of the scratch's tickets on `stream`),
+ * so make that call before capturing a stream into a CUDA graph. */
+int soinfer_gemv_w4a16_sparse_accumulate_noalloc(const uint8_t* Wq_sel, const float* scale_sel,
+                                                 const soinfer_half* h, soinfer_half* y, int64_t H,
+                                                 int64_t k, int64_t group_size, int64_t num_groups,
+                                                 void* stream);
+
 /* Row-indirect form of the sparse 'down' GEMV over a resident transposed
  * matrix: row j of the sum is Wq_T[rows[j]] with scale_T[rows[j]].
  * Bit-identical to gathering those rows and calling

@@ -327,6 +327,33 @@ int soinfer_gemv_w4a16_sparse_accumulate(const uint8_t* Wq_sel, const float* sca
                        stream);
 }
 
+int soinfer_gemv_w4a16_sparse_accumulate_noalloc(const uint8_t* Wq_sel, const float* scale_sel, const soinfer_half* h,
+                                                 soinfer_half* y, int64_t H, int64_t k, int64_t group_size,
+                                                 int64_t num_groups, void* stream) {
+  const char* name = "gemv_w4a16_sparse_accumulate_noalloc";
+  REQUIRE(k == 0 || (Wq_sel && scale_sel), "%s: null pointer", name);
+  REQUIRE(aligned(Wq_sel, 4), "%s: misaligned weights", name);
+  if (int st = check_int4_layout(name, H, group_size, num_groups)) return st;
+  REQUIRE(k >= 0, "%s: k must be >= 0", name);
+  REQUIRE(y, "%s: null output", name);
+  if (k == 0) return cuda_result(cudaMemsetAsync(y, 0, (size_t)H * 2, as_stream(stream)), name);
+  REQUIRE(h, "%s: null h", name);
+  REQUIRE(sparse_workspace_bytes(H, k) <= sparse_static_scratch_bytes(),
+          "%s: H=%lld, k=%lld needs %lld scratch bytes, above the static %lld", name, (long long)H, (long long)k,
+          (long long)sparse_workspace_bytes(H, k), (long long)sparse_static_scratch_bytes());
+  void* scratch = nullptr;
+  if (int st = cuda_result(sparse_static_scratch(&scratch, as_stream(stream)), name)) return st;
+  RowSource src;
+  src.W = Wq_sel;
+  src.S = scale_sel;
+  src.rows1 = k;
+  src.row_bytes = int4_row_bytes(H);
+  src.num_groups = num_groups;
+  return cuda_result(launch_sparse_down(RowMode::kPlain, src, as_half(h), as_half(y), H, k, group_size, scratch,
+                                        as_stream(stream)),
+                     name);
+}
+
 int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, int64_t I, const int32_t* rows,
                                    const soinfer_half* h, soinfer_half* y, int64_t H, int64_t k, int64_t group_size,
                                    int64_t num_groups, void* workspace, int64_t workspace_bytes, void* stream) {

@@ -62,6 +62,11 @@ cudaError_t launch_gemv_w8(const int8_t* Wq, const float* scale, const half* x, 
 
 // Sparse 'down' accumulate: y[c] = sum_j h[j] * scale(j, c/g) * q(j, c).
 int64_t sparse_workspace_bytes(int64_t H, int64_t k);
+// Per-device static scratch usable as the sparse workspace (no allocation):
+// its size, and its address on the current device (first call per device
+// resolves the symbol and clears the tickets on `stream`).
+int64_t sparse_static_scratch_bytes();
+cudaError_t sparse_static_scratch(void** scratch, cudaStream_t stream);
 cudaError_t launch_sparse_down(RowMode mode, const RowSource& src, const half* h, half* y, int64_t H,
                                int64_t k, int64_t group_size, void* workspace, cudaStream_t stream,
                                LaunchOpts opts = {});

@@ -18,6 +18,8 @@
 // the slab partials in row-slab order.  The reduction order depends only on
 // (H, k), never on which buffer a row came from, so cache / staging /
 // indexed / plain sources give bit-identical outputs.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -30,6 +32,16 @@ constexpr int kColChunks = 8;            // 16-byte column chunks per column sla
 constexpr int kPhases = kThreads / kColChunks;
 constexpr int kTargetCtas = 296;
 constexpr int64_t kCounterBytes = 4096;  // room for 1024 column-slab tickets
+constexpr int64_t kStaticScratchBytes = 512 * 1024;
+constexpr int kMaxDevices = 64;
+
+// Scratch of the no-alloc entry point, one copy per device (file-scope device
+// memory: no allocation at call time).  Same layout as a caller workspace:
+// kCounterBytes of column-slab tickets, which must start at zero and which
+// every call leaves at zero, then the fp32 partial rows (overwritten by each
+// call).  Workspaces of up to kStaticScratchBytes fit: every shape from H =
+// 2048 to H = 16384 needs about 0.3 MiB.
+static __device__ __align__(256) unsigned char g_sparse_scratch[kStaticScratchBytes];
 
 struct DownShape {
   int64_t H, k;
@@ -219,6 +231,28 @@ int64_t sparse_workspace_bytes(int64_t H, int64_t k) {
   const DownShape b = down_shape(H, k, false);
   const int64_t slabs = a.row_slabs > b.row_slabs ? a.row_slabs : b.row_slabs;
   return kCounterBytes + slabs * H * (int64_t)sizeof(float);
+}
+
+int64_t sparse_static_scratch_bytes() { return kStaticScratchBytes; }
+
+cudaError_t sparse_static_scratch(void** scratch, cudaStream_t stream) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {  // first use on this device: resolve the symbol, clear the tickets
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_sparse_scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p, 0, (size_t)kCounterBytes, stream);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *scratch = addr[dev];
+  return cudaSuccess;
 }
 
 cudaError_t launch_sparse_down(RowMode mode, const RowSource& src, const half* h, half* y, int64_t H, int64_t k,

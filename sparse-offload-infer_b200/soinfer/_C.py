@@ -46,6 +46,7 @@ _SIGNATURES = {
     "soinfer_gemv_dip_fused_up": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
     "soinfer_sparse_workspace_bytes": (_I64, [_I64, _I64]),
     "soinfer_gemv_w4a16_sparse_accumulate": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_gemv_w4a16_sparse_accumulate_noalloc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_sparse_rows": (_INT, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "soinfer_gemv_dip_fused_down": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64,
                                            _P]),
@@ -407,9 +408,8 @@ def _sparse_ws(dev, H: int, k: int):
     return ws.data_ptr(), ws.numel()
 
 
-def gemv_w4a16_sparse_accumulate(Wq_selected, scale_selected, h_selected, H: int, group_size: int,
-                                 out: torch.Tensor | None = None):
-    name = "gemv_w4a16_sparse_accumulate"
+def _sparse_accumulate_args(name, Wq_selected, scale_selected, h_selected, H, group_size, out):
+    """Reference-style argument checks of the sparse accumulate ops; returns (k, num_groups, device, y)."""
     _check(Wq_selected.is_cuda and Wq_selected.dtype == torch.uint8 and Wq_selected.is_contiguous(), name,
            "(Wq_selected): must be a contiguous CUDA uint8 tensor")
     _check(Wq_selected.dim() == 2, name, "(Wq_selected): must be 2D [k, ceil(H/8)*4]")
@@ -428,10 +428,31 @@ def gemv_w4a16_sparse_accumulate(Wq_selected, scale_selected, h_selected, H: int
            "the given H and group_size, got ", num_groups, " but expected ", _cdiv(H, group_size))
     dev = _same_device(Wq_selected, scale_selected, h_selected)
     y = out if out is not None else torch.empty(H, dtype=torch.float16, device=dev)
+    return k, num_groups, dev, y
+
+
+def gemv_w4a16_sparse_accumulate(Wq_selected, scale_selected, h_selected, H: int, group_size: int,
+                                 out: torch.Tensor | None = None):
+    name = "gemv_w4a16_sparse_accumulate"
+    k, num_groups, dev, y = _sparse_accumulate_args(name, Wq_selected, scale_selected, h_selected, H, group_size, out)
     with torch.cuda.device(dev):
         ws, wsb = _sparse_ws(dev, H, k)
         _call("soinfer_gemv_w4a16_sparse_accumulate", _ptr(Wq_selected), _ptr(scale_selected), _ptr(h_selected),
               _ptr(y), H, k, group_size, num_groups, ws, wsb, _stream(dev))
+    return y
+
+
+def gemv_w4a16_sparse_accumulate_noalloc(Wq_selected, scale_selected, h_selected, H: int, group_size: int,
+                                         out: torch.Tensor | None = None):
+    """gemv_w4a16_sparse_accumulate with the kernel's scratch in a per-device
+    static device array instead of a workspace (no reference counterpart).
+    Calls that overlap in time on one device race on that scratch; make the
+    first call on a device before capturing a CUDA graph."""
+    name = "gemv_w4a16_sparse_accumulate_noalloc"
+    k, num_groups, dev, y = _sparse_accumulate_args(name, Wq_selected, scale_selected, h_selected, H, group_size, out)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_w4a16_sparse_accumulate_noalloc", _ptr(Wq_selected), _ptr(scale_selected),
+              _ptr(h_selected), _ptr(y), H, k, group_size, num_groups, _stream(dev))
     return y
 
 
