@@ -183,6 +183,26 @@ int soinfer_gemv_dip_fused_up(const uint8_t* cache_Wq, const float* cache_scale,
                               const int32_t* desc, int64_t k, const soinfer_half* x, soinfer_half* y,
                               int64_t K, int64_t group_size, int64_t num_groups, void* stream);
 
+/* fp16 GEMV: y[n] = fp16( sum_k W[n, k] * x[k] ), fp32 accumulation.  The
+ * decode LM head.  W: fp16 [N, K] row-major (16-byte aligned), x: fp16 [K],
+ * y: fp16 [N]; K % 8 == 0.
+ * Replaces: csrc/bindings.cpp:201-208 (gemv_fp16_v3), csrc/kernels/gemv_fp16.cu:60-95. */
+int soinfer_gemv_fp16(const soinfer_half* W, const soinfer_half* x, soinfer_half* y, int64_t N,
+                      int64_t K, void* stream);
+
+/* Bytes of zero-initialised workspace soinfer_gemv_fp16_argmax needs (left
+ * zeroed on return). */
+int64_t soinfer_lm_head_argmax_workspace_bytes(void);
+
+/* soinfer_gemv_fp16 fused with the greedy token choice: *out_idx = the
+ * argmax of the fp16 logits (lowest index among equal maxima, as
+ * torch.argmax).  y may be NULL when the logits are not needed.
+ * Replaces the reference's gemv_fp16_v3 + torch.argmax pair
+ * (python/soinfer/runtime/generate.py:452-454). */
+int soinfer_gemv_fp16_argmax(const soinfer_half* W, const soinfer_half* x, soinfer_half* y, int64_t N,
+                             int64_t K, int32_t* out_idx, void* workspace, int64_t workspace_bytes,
+                             void* stream);
+
 /* Bytes of zero-initialised device workspace the sparse 'down' GEMVs need for
  * an output width H over k selected rows.  The kernels leave the workspace
  * zeroed again on return, so a caller allocates (and clears) it once and

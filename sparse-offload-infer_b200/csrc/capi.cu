@@ -291,6 +291,33 @@ int soinfer_gemv_dip_fused_up(const uint8_t* cache_Wq, const float* cache_scale,
                      name);
 }
 
+int soinfer_gemv_fp16(const soinfer_half* W, const soinfer_half* x, soinfer_half* y, int64_t N, int64_t K,
+                      void* stream) {
+  const char* name = "gemv_fp16_v3";
+  REQUIRE(N >= 0 && K >= 1, "%s: N must be >= 0 and K >= 1", name);
+  REQUIRE(K % 8 == 0, "%s: K must be a multiple of 8 (float4-vectorized loads)", name);
+  if (N == 0) return SOINFER_OK;
+  REQUIRE(W && x && y, "%s: null pointer", name);
+  REQUIRE(aligned(W, 16) && aligned(x, 16) && aligned(y, 2), "%s: W and x must be 16-byte aligned", name);
+  return cuda_result(launch_gemv_fp16(as_half(W), as_half(x), as_half(y), N, K, as_stream(stream)), name);
+}
+
+int64_t soinfer_lm_head_argmax_workspace_bytes(void) { return lm_head_argmax_workspace_bytes(); }
+
+int soinfer_gemv_fp16_argmax(const soinfer_half* W, const soinfer_half* x, soinfer_half* y, int64_t N, int64_t K,
+                             int32_t* out_idx, void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_fp16_argmax";
+  REQUIRE(N >= 1 && N < (int64_t)1 << 31 && K >= 1, "%s: N must be in [1, 2^31) and K >= 1", name);
+  REQUIRE(K % 8 == 0, "%s: K must be a multiple of 8 (float4-vectorized loads)", name);
+  REQUIRE(W && x && out_idx, "%s: null pointer", name);
+  REQUIRE(aligned(W, 16) && aligned(x, 16) && aligned(y, 2), "%s: W and x must be 16-byte aligned", name);
+  REQUIRE(workspace && workspace_bytes >= lm_head_argmax_workspace_bytes() && aligned(workspace, 8),
+          "%s: workspace too small (need %lld zeroed bytes)", name, (long long)lm_head_argmax_workspace_bytes());
+  return cuda_result(launch_gemv_fp16_argmax(as_half(W), as_half(x), as_half(y), N, K, workspace, out_idx,
+                                             as_stream(stream)),
+                     name);
+}
+
 int64_t soinfer_sparse_workspace_bytes(int64_t H, int64_t k) {
   if (H < 1 || k < 0) return 0;
   return sparse_workspace_bytes(H, k > 0 ? k : 1);

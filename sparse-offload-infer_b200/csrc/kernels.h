@@ -81,6 +81,13 @@ cudaError_t launch_build_descriptors(const int32_t* sel, int64_t k, const int32_
 cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
                                       const int32_t* rows, int64_t k, uint8_t* dst, cudaStream_t stream);
 
+// fp16 GEMV (LM head) and the fused greedy argmax (lm_head.cu).  The argmax
+// workspace (lm_head_argmax_workspace_bytes, zero-initialised) is left zeroed.
+cudaError_t launch_gemv_fp16(const half* W, const half* x, half* y, int64_t N, int64_t K, cudaStream_t stream);
+int64_t lm_head_argmax_workspace_bytes();
+cudaError_t launch_gemv_fp16_argmax(const half* W, const half* x, half* y, int64_t N, int64_t K, void* workspace,
+                                    int32_t* out_idx, cudaStream_t stream);
+
 // Attention-side glue.
 cudaError_t launch_rmsnorm(const half* x, const half* w, half* out, int64_t rows, int64_t hidden, float eps,
                            cudaStream_t stream);

@@ -46,6 +46,9 @@ _SIGNATURES = {
     "soinfer_gemv_dip_fused_up": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
     "soinfer_sparse_workspace_bytes": (_I64, [_I64, _I64]),
     "soinfer_gemv_w4a16_sparse_accumulate": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_gemv_fp16": (_INT, [_P, _P, _P, _I64, _I64, _P]),
+    "soinfer_lm_head_argmax_workspace_bytes": (_I64, []),
+    "soinfer_gemv_fp16_argmax": (_INT, [_P, _P, _P, _I64, _I64, _P, _P, _I64, _P]),
     "soinfer_gemv_w4a16_sparse_accumulate_noalloc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_sparse_rows": (_INT, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
     "soinfer_gemv_dip_fused_down": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64,
@@ -211,6 +214,42 @@ def gemv_w4a16_group_lop3(Wq_packed, scale, x, K: int, group_size: int, out=None
     written by the kernel preceding this one on the stream)."""
     return _gemv_w4a16_group_impl("soinfer_gemv_w4a16_group_lop3", "gemv_w4a16_group_lop3", Wq_packed, scale, x, K,
                                   group_size, out, pdl)
+
+
+def _check_fp16_gemv(name, W, x):
+    """Reference check_gemv_shapes (csrc/bindings.cpp) + the 16-byte vector-load rule."""
+    _f16(W, name + "(W)")
+    _f16(x, name + "(x)")
+    _check(W.dim() == 2 and W.is_contiguous(), name, ": W must be a contiguous 2D [N, K] tensor")
+    _check(x.dim() == 1 and x.is_contiguous(), name, ": x must be a contiguous 1D [K] tensor")
+    _check(W.size(1) == x.size(0), name, ": W.size(1) must equal x.size(0)")
+    _check(W.size(1) % 8 == 0, name, ": K must be a multiple of 8 (float4-vectorized loads)")
+    return _same_device(W, x)
+
+
+def gemv_fp16_v3(W, x, out=None) -> torch.Tensor:
+    """fp16 GEMV, fp32 accumulation (the decode LM head)."""
+    dev = _check_fp16_gemv("gemv_fp16_v3", W, x)
+    y = out if out is not None else torch.empty(W.size(0), dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_fp16", _ptr(W), _ptr(x), _ptr(y), W.size(0), W.size(1), _stream(dev))
+    return y
+
+
+def gemv_fp16_argmax(W, x, logits: bool = False, out_idx=None):
+    """Greedy next token: argmax of the fp16 logits W x (lowest index among
+    equal maxima), fused into the LM head GEMV.  Returns (idx int32 [1] on the
+    device, logits fp16 [N] or None)."""
+    dev = _check_fp16_gemv("gemv_fp16_argmax", W, x)
+    _check(W.size(0) >= 1, "gemv_fp16_argmax: W must have at least one row")
+    idx = out_idx if out_idx is not None else torch.empty(1, dtype=torch.int32, device=dev)
+    y = torch.empty(W.size(0), dtype=torch.float16, device=dev) if logits else None
+    with torch.cuda.device(dev):
+        nbytes = lib().soinfer_lm_head_argmax_workspace_bytes()
+        ws = _workspace("argmax", dev, nbytes)
+        _call("soinfer_gemv_fp16_argmax", _ptr(W), _ptr(x), _ptr(y), W.size(0), W.size(1), _ptr(idx), ws.data_ptr(),
+              ws.numel(), _stream(dev))
+    return idx, y
 
 
 class _GemvTask(ctypes.Structure):

@@ -19,6 +19,19 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.T
     return _C.rmsnorm(x, weight, eps)
 
 
+def gemv_fp16_v3(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """fp16 GEMV y = W x with fp32 accumulation (the decode LM head). W: [N, K] half, x: [K] half, K % 8 == 0.
+    Reference: ops.py:82-84, csrc/kernels/gemv_fp16.cu:60-95."""
+    return _C.gemv_fp16_v3(W, x)
+
+
+def lm_head_argmax(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """B200 addition: the greedy next token, argmax over the fp16 logits of W x (lowest index among equal
+    maxima, like torch.argmax), fused into the LM head GEMV.  Returns an int32 [1] CUDA tensor.
+    Replaces gemv_fp16_v3 + torch.argmax (reference runtime/generate.py:452-454)."""
+    return _C.gemv_fp16_argmax(W, x)[0]
+
+
 def gemv_w8a16(Wq: torch.Tensor, scale: torch.Tensor, x: torch.Tensor, group_size: int) -> torch.Tensor:
     """y = dequant(Wq, scale) @ x. Wq: [N,K] int8 symmetric; scale: [N,num_groups] or [1,num_groups] fp32
     (per-tensor broadcast); num_groups == 1 means one scale per row.  Reference: ops.py:92-96."""

@@ -1,4 +1,4 @@
 """Decode loops over the soinfer ops (reference python/soinfer/runtime/)."""
-from . import generate  # noqa: F401
+from . import generate, loader  # noqa: F401
 
-__all__ = ["generate"]
+__all__ = ["generate", "loader"]

@@ -1,10 +1,20 @@
-"""Decode loop over weights streamed from the pinned arena (reference
-python/soinfer/runtime/generate.py:58-645).
+"""Batch-1 greedy decode over the soinfer ops (reference
+python/soinfer/runtime/generate.py:58-645): dense streaming, DIP (dynamic
+input pruning of the MLP) and cache-aware DIP decoder layers, the generate
+loops, teacher-forced NLL and channel-frequency calibration.
 
-`WeightPipeline` walks the fixed, cyclic per-token sequence of weight names
-one step ahead of compute: while the INT4 GEMV of weight i runs on the
-compute stream, the copy engine already streams weight i+1 into the other of
-two device buffers (side stream + events, write-after-read guarded).
+Weights live either in the pinned host arena, streamed to the GPU by
+`WeightPipeline` one matrix ahead of compute (the reference's offload mode),
+or resident in HBM (`StreamingModel.resident`, the natural B200 mode: 180 GB
+holds every config here); the layer functions are the same for both.
+
+Where the reference syncs with the host, this path stays on the device:
+DIP's selected up_proj / down_proj_T rows are read in place by row-indexed
+kernels (resident) or gathered by a device-driven zero-copy gather straight
+from the pinned arena (offload), so the selected indices never leave the
+GPU; the next token is chosen by the LM-head GEMV's fused argmax and its
+embedding row is selected on the device.  Cache-aware DIP keeps the
+reference's one sync per layer (the miss count sizes the staging rows).
 """
 from __future__ import annotations
 
@@ -12,14 +22,17 @@ import itertools
 from dataclasses import dataclass, field
 
 import torch
+import torch.nn.functional as F
 
 from .. import ops
+from ..offload.hot_cache import HotCache
 from ..offload.load_hf_checkpoint import DOWN_PROJ_T_SUFFIX, LINEAR_SUFFIXES, LoadedMatrix
 from ..offload.stream_manager import StreamManager
 from ..offload.weight_store import PinnedWeightStore
 
-# q/k/v/o/gate stay dense-streamed in DIP; up_proj and down_proj_T are fetched
-# per token as the selected rows only (reference generate.py:49-55).
+# q/k/v/o/gate stay dense in DIP (selection needs every |gate| value); up_proj
+# and down_proj_T are read per token as the selected rows only
+# (reference generate.py:49-55).
 DIP_DENSE_SUFFIXES = (
     "self_attn.q_proj.weight",
     "self_attn.k_proj.weight",
@@ -31,14 +44,17 @@ DIP_DENSE_SUFFIXES = (
 
 @dataclass
 class StreamingModel:
-    """Arena + handles, the small resident tensors, and the streaming machinery."""
+    """The arena and its per-matrix handles, the small resident tensors
+    (embeddings, LM head, norms), and the streaming machinery.  `resident`
+    (name -> packed uint8 CUDA tensor) switches a matrix from streamed to
+    HBM-resident."""
 
-    store: PinnedWeightStore
+    store: PinnedWeightStore | None
     matrices: dict[str, LoadedMatrix]
     num_layers: int
-    embed_tokens: torch.Tensor | None
-    lm_head: torch.Tensor | None
-    final_norm: torch.Tensor | None
+    embed_tokens: torch.Tensor | None   # [vocab, H] half, CUDA
+    lm_head: torch.Tensor | None        # [vocab, H] half, CUDA
+    final_norm: torch.Tensor | None     # [H] half, CUDA
     layer_norms: list[dict[str, torch.Tensor]]
     hidden_size: int
     num_attention_heads: int
@@ -47,22 +63,46 @@ class StreamingModel:
     rms_norm_eps: float
     rope_theta: float
     group_size: int = 128
+    resident: dict[str, torch.Tensor] | None = None
     stream_manager: StreamManager = field(init=False)
 
     def __post_init__(self) -> None:
-        self.stream_manager = StreamManager(num_buffers=2)
+        self.stream_manager = StreamManager(num_buffers=2, device=self.device)
+
+    @property
+    def device(self) -> torch.device:
+        for m in self.matrices.values():
+            return m.scale.device
+        return torch.device("cuda", torch.cuda.current_device())
+
+    def is_resident(self, name: str) -> bool:
+        return self.resident is not None and name in self.resident
+
+    def weight_source(self, m: LoadedMatrix) -> torch.Tensor:
+        """The packed rows of m: the resident CUDA tensor, else its arena view (pinned host)."""
+        if self.is_resident(m.handle.name):
+            return self.resident[m.handle.name]
+        return self.store.matrix_view(m.handle)
+
+    def matrix(self, layer_idx: int, suffix: str) -> LoadedMatrix:
+        return self.matrices[f"model.layers.{layer_idx}.{suffix}"]
 
 
 class WeightPipeline:
-    """Double-buffered, cyclic prefetch of per-token weights (reference generate.py:85-138)."""
+    """Cyclic per-token weight sequence (reference generate.py:85-138).
+    Streamed matrices: two device buffers, the copy of weight i+1 issued on a
+    side stream while weight i's GEMV runs (events, write-after-read guard).
+    Resident matrices are used in place."""
 
     def __init__(self, model: StreamingModel, suffixes: tuple[str, ...] = LINEAR_SUFFIXES):
         self.model = model
         self.sm = model.stream_manager
         seq = [f"model.layers.{i}.{s}" for i in range(model.num_layers) for s in suffixes]
-        max_bytes = max(model.matrices[n].n * model.matrices[n].handle.row_nbytes for n in seq)
-        dev = self.sm.device
-        self.bufs = [torch.empty(max_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+        streamed = [n for n in seq if not model.is_resident(n)]
+        self.bufs = []
+        if streamed:
+            max_bytes = max(model.matrices[n].n * model.matrices[n].handle.row_nbytes for n in streamed)
+            self.bufs = [torch.empty(max_bytes, dtype=torch.uint8, device=model.device) for _ in range(2)]
         self._names = itertools.cycle(seq)
         self.cur_buf = 0
         self.cur_name = next(self._names)
@@ -73,20 +113,305 @@ class WeightPipeline:
         return self.bufs[buf_idx][:nbytes].view(m.n, m.handle.row_nbytes)
 
     def _prefetch_into(self, buf_idx: int, name: str) -> None:
+        if self.model.is_resident(name):
+            return
         m = self.model.matrices[name]
         self.sm.prefetch(buf_idx, self._view(buf_idx, m), self.model.store.matrix_view(m.handle))
 
     def next_gemv(self, x_in: torch.Tensor) -> torch.Tensor:
-        """GEMV of the weight in flight (waits on its copy event), then start the next prefetch."""
-        m = self.model.matrices[self.cur_name]
-        self.sm.wait(self.cur_buf)
-        y = ops.gemv_w4a16_group_lop3(self._view(self.cur_buf, m), m.scale, x_in, m.packed_k, self.model.group_size)
-        self.sm.mark_read_done(self.cur_buf)
+        """GEMV of the weight in flight (its copy awaited on the GPU), then the next prefetch."""
+        name = self.cur_name
+        m = self.model.matrices[name]
+        if self.model.is_resident(name):
+            y = ops.gemv_w4a16_group_lop3(self.model.resident[name], m.scale, x_in, m.packed_k, self.model.group_size)
+        else:
+            self.sm.wait(self.cur_buf)
+            y = ops.gemv_w4a16_group_lop3(self._view(self.cur_buf, m), m.scale, x_in, m.packed_k,
+                                          self.model.group_size)
+            self.sm.mark_read_done(self.cur_buf)
         nxt = 1 - self.cur_buf
-        name = next(self._names)
-        self._prefetch_into(nxt, name)
-        self.cur_buf, self.cur_name = nxt, name
+        name_next = next(self._names)
+        self._prefetch_into(nxt, name_next)
+        self.cur_buf, self.cur_name = nxt, name_next
         return y
 
 
-__all__ = ["StreamingModel", "WeightPipeline", "DIP_DENSE_SUFFIXES", "DOWN_PROJ_T_SUFFIX", "LINEAR_SUFFIXES"]
+# --------------------------------------------------------------- attention
+def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
+                     k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """rmsnorm -> q/k/v GEMVs -> q/k norm -> RoPE -> KV append -> GQA decode
+    attention -> o GEMV -> residual.  Returns (h2, h3 = post-attention rmsnorm(h2))."""
+    NQ, NKV, HD = model.num_attention_heads, model.num_key_value_heads, model.head_dim
+    eps = model.rms_norm_eps
+    norms = model.layer_norms[layer_idx]
+    h = ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
+    q = pipeline.next_gemv(h).view(NQ, HD)
+    k = pipeline.next_gemv(h).view(NKV, HD)
+    v = pipeline.next_gemv(h).view(NKV, HD)
+    q = ops.qk_norm(q, norms["q_norm"], eps)
+    k = ops.qk_norm(k, norms["k_norm"], eps)
+    cos_vals, sin_vals = ops.precompute_rope_cos_sin(HD, model.rope_theta, pos, device=x_flat.device)
+    q = ops.apply_rope(q, cos_vals, sin_vals)
+    k = ops.apply_rope(k, cos_vals, sin_vals)
+    ops.kv_cache_append(k_cache, v_cache, k, v, pos)
+    attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
+    h2 = x_flat + pipeline.next_gemv(attn)
+    h3 = ops.rmsnorm(h2.unsqueeze(0), norms["post_attention_layernorm"], eps).squeeze(0)
+    return h2, h3
+
+
+def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
+                                x_flat: torch.Tensor, pos: int, k_cache: torch.Tensor,
+                                v_cache: torch.Tensor) -> torch.Tensor:
+    """Dense layer: all 7 linear weights through the pipeline (reference generate.py:141-182)."""
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
+    gate = pipeline.next_gemv(h3)
+    up = pipeline.next_gemv(h3)
+    mlp_h = (F.silu(gate.float()) * up.float()).half()
+    return h2 + pipeline.next_gemv(mlp_h)
+
+
+# --------------------------------------------------------------------- DIP
+@dataclass
+class DipBuffers:
+    """Device rows for the selected (DIP) or missed (cached DIP) up_proj /
+    down_proj_T rows, allocated once for the largest k (reference
+    generate.py:185-212; no pinned staging: the gather is device-driven)."""
+
+    gpu_up: torch.Tensor     # CUDA uint8 [max_k * up_row_nbytes]
+    gpu_down: torch.Tensor   # CUDA uint8 [max_k * downT_row_nbytes]
+    up_row_nbytes: int
+    down_row_nbytes: int
+
+    @staticmethod
+    def make(model: StreamingModel, max_k: int) -> "DipBuffers":
+        up_rb = model.matrix(0, "mlp.up_proj.weight").handle.row_nbytes
+        down_rb = model.matrix(0, DOWN_PROJ_T_SUFFIX).handle.row_nbytes
+        dev = model.device
+        return DipBuffers(gpu_up=torch.empty(max_k * up_rb, dtype=torch.uint8, device=dev),
+                          gpu_down=torch.empty(max_k * down_rb, dtype=torch.uint8, device=dev),
+                          up_row_nbytes=up_rb, down_row_nbytes=down_rb)
+
+    def up_rows(self, k: int) -> torch.Tensor:
+        return self.gpu_up[: k * self.up_row_nbytes].view(k, self.up_row_nbytes)
+
+    def down_rows(self, k: int) -> torch.Tensor:
+        return self.gpu_down[: k * self.down_row_nbytes].view(k, self.down_row_nbytes)
+
+
+def _select(gate: torch.Tensor, dip_k: int) -> torch.Tensor:
+    """The reference's DIP selector on |gate| (fp32): int32 [dip_k] ascending channel indices."""
+    return ops.topk_threshold_select(gate.float().abs(), dip_k)
+
+
+def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor,
+                          pos: int, k_cache: torch.Tensor, v_cache: torch.Tensor, dip_k: int, bufs: DipBuffers,
+                          channel_counts: list[torch.Tensor] | None = None,
+                          selected_out: list[list] | None = None) -> torch.Tensor:
+    """DIP layer (reference generate.py:215-310): dense gate, top-dip_k |gate|
+    channels, up_proj on the selected rows, h = fp16(silu(g) * u), down_proj_T
+    sparse accumulate over the same rows.  channel_counts[layer] (int64 [I]
+    CUDA) accumulates selections; selected_out[layer] collects the index lists
+    (this one syncs)."""
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
+    gate = pipeline.next_gemv(h3)
+    idx = _select(gate, dip_k)
+    idx_long = idx.long()
+    if channel_counts is not None:
+        channel_counts[layer_idx].scatter_add_(0, idx_long, torch.ones_like(idx_long))
+    if selected_out is not None:
+        selected_out[layer_idx].append(idx_long.cpu().tolist())
+    up = model.matrix(layer_idx, "mlp.up_proj.weight")
+    down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
+    g = model.group_size
+    if model.is_resident(up.handle.name):
+        u_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, idx, h3, up.packed_k, g)
+    else:
+        rows = bufs.up_rows(dip_k)
+        ops.gather_rows_device(model.weight_source(up), idx, rows)
+        u_sel = ops.gemv_w4a16_group_lop3(rows, up.scale.index_select(0, idx_long), h3, up.packed_k, g)
+    h_sel = (F.silu(gate.index_select(0, idx_long).float()) * u_sel.float()).half()
+    if model.is_resident(down_t.handle.name):
+        down = ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, idx, h_sel,
+                                          model.hidden_size, g)
+    else:
+        rows = bufs.down_rows(dip_k)
+        ops.gather_rows_device(model.weight_source(down_t), idx, rows)
+        down = ops.gemv_w4a16_sparse_accumulate(rows, down_t.scale.index_select(0, idx_long), h_sel,
+                                                model.hidden_size, g)
+    return h2 + down
+
+
+def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
+                                 x_flat: torch.Tensor, pos: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                                 dip_k: int, bufs: DipBuffers, caches: list[HotCache],
+                                 miss_bytes: list[int] | None = None) -> torch.Tensor:
+    """Cache-aware DIP layer (reference generate.py:313-404): the selected
+    channels resolve to hot-cache slots or staging rows (the misses, gathered
+    from the arena); one fused GEMV per direction reads both.  Bit-identical
+    to run_decoder_layer_dip on the same inputs.  miss_bytes[layer] counts
+    the streamed bytes."""
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
+    gate = pipeline.next_gemv(h3)
+    idx = _select(gate, dip_k)
+    cache = caches[layer_idx]
+    up = model.matrix(layer_idx, "mlp.up_proj.weight")
+    down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
+    g = model.group_size
+    desc, miss, miss_count = ops.build_dip_descriptors(idx, cache.slot_of)
+    mc = int(miss_count.item())  # sizes the staging rows (the reference's sync)
+    miss = miss[:mc]
+    miss_long = miss.long()
+    up_rows, down_rows = bufs.up_rows(mc), bufs.down_rows(mc)
+    if mc:
+        ops.gather_rows_device(model.weight_source(up), miss, up_rows)
+        ops.gather_rows_device(model.weight_source(down_t), miss, down_rows)
+    if miss_bytes is not None:
+        miss_bytes[layer_idx] += mc * (bufs.up_row_nbytes + bufs.down_row_nbytes)
+    u_sel = ops.gemv_dip_fused_up(cache.up_Wq, cache.up_scale, up_rows, up.scale.index_select(0, miss_long), desc,
+                                  h3, up.packed_k, g)
+    h_sel = (F.silu(gate.index_select(0, idx.long()).float()) * u_sel.float()).half()
+    down = ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows,
+                                   down_t.scale.index_select(0, miss_long), desc, h_sel, model.hidden_size, g)
+    return h2 + down
+
+
+def dip_bytes_per_token(model: StreamingModel, dip_k: int, dense: bool = False) -> int:
+    """Per-token weight bytes of the decode path (reference generate.py:407-426):
+    q/k/v/o/gate in full, up_proj / down_proj_T in full (dense) or dip_k rows."""
+    total = 0
+    for layer in range(model.num_layers):
+        for suffix in DIP_DENSE_SUFFIXES:
+            m = model.matrix(layer, suffix)
+            total += m.n * m.handle.row_nbytes
+        up = model.matrix(layer, "mlp.up_proj.weight")
+        down_t = model.matrix(layer, DOWN_PROJ_T_SUFFIX)
+        total += (up.n if dense else dip_k) * up.handle.row_nbytes
+        total += (down_t.n if dense else dip_k) * down_t.handle.row_nbytes
+    return total
+
+
+# ------------------------------------------------------------------- loops
+def _kv_caches(model: StreamingModel, max_seq_len: int):
+    shape = (model.num_key_value_heads, max_seq_len, model.head_dim)
+    dev = model.device
+    return ([torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(model.num_layers)],
+            [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(model.num_layers)])
+
+
+def _greedy(model: StreamingModel, prompt_ids: list[int], n_new: int, run_layer, eos_token_id: int | None,
+            max_seq_len: int) -> list[int]:
+    """Prefill the prompt one token at a time, then greedy-decode n_new tokens.
+    run_layer(layer_idx, x, pos, k_cache, v_cache) -> x.  Token ids stay on
+    the device until the end (a host sync per token only with an EOS id)."""
+    if len(prompt_ids) + n_new > max_seq_len:
+        raise ValueError(f"prompt ({len(prompt_ids)}) + n_new ({n_new}) exceeds max_seq_len ({max_seq_len})")
+    k_caches, v_caches = _kv_caches(model, max_seq_len)
+    dev = model.device
+
+    def forward(x, pos):
+        for li in range(model.num_layers):
+            x = run_layer(li, x, pos, k_caches[li], v_caches[li])
+        return x
+
+    x = None
+    for pos, tok in enumerate(prompt_ids):
+        x = forward(model.embed_tokens[tok], pos)
+    new_ids = []
+    pos = len(prompt_ids)
+    for _ in range(n_new):
+        xn = ops.rmsnorm(x.unsqueeze(0), model.final_norm, model.rms_norm_eps).squeeze(0)
+        idx = ops.lm_head_argmax(model.lm_head, xn)  # int32 [1] on the device
+        new_ids.append(idx)
+        if eos_token_id is not None and int(idx.item()) == eos_token_id:
+            break
+        x = forward(model.embed_tokens.index_select(0, idx.long()).view(-1), pos)
+        pos += 1
+    out = list(prompt_ids)
+    if new_ids:
+        out += torch.cat(new_ids).cpu().tolist()
+    return out
+
+
+def generate_streaming(model: StreamingModel, prompt_ids: list[int], n_new: int, eos_token_id: int | None = None,
+                       max_seq_len: int = 512) -> list[int]:
+    """Greedy decode, dense layers (reference generate.py:429-463)."""
+    pipeline = WeightPipeline(model)
+    return _greedy(model, prompt_ids, n_new,
+                   lambda li, x, p, kc, vc: run_decoder_layer_streaming(pipeline, model, li, x, p, kc, vc),
+                   eos_token_id, max_seq_len)
+
+
+def generate_dip(model: StreamingModel, prompt_ids: list[int], n_new: int, dip_k: int,
+                 eos_token_id: int | None = None, max_seq_len: int = 512) -> list[int]:
+    """Greedy decode, DIP MLPs (reference generate.py:466-500)."""
+    pipeline = WeightPipeline(model, suffixes=DIP_DENSE_SUFFIXES)
+    bufs = DipBuffers.make(model, dip_k)
+    return _greedy(model, prompt_ids, n_new,
+                   lambda li, x, p, kc, vc: run_decoder_layer_dip(pipeline, model, li, x, p, kc, vc, dip_k, bufs),
+                   eos_token_id, max_seq_len)
+
+
+def generate_cached_dip(model: StreamingModel, prompt_ids: list[int], n_new: int, dip_k: int,
+                        caches: list[HotCache], eos_token_id: int | None = None, max_seq_len: int = 512,
+                        miss_bytes: list[int] | None = None) -> list[int]:
+    """Greedy decode, cache-aware DIP MLPs (reference generate.py:503-542)."""
+    pipeline = WeightPipeline(model, suffixes=DIP_DENSE_SUFFIXES)
+    bufs = DipBuffers.make(model, dip_k)
+    return _greedy(model, prompt_ids, n_new,
+                   lambda li, x, p, kc, vc: run_decoder_layer_cached_dip(pipeline, model, li, x, p, kc, vc, dip_k,
+                                                                         bufs, caches, miss_bytes),
+                   eos_token_id, max_seq_len)
+
+
+def teacher_forced_nll(model: StreamingModel, layer_fn, token_ids: list[int], max_seq_len: int = 512) -> float:
+    """Mean NLL of each real next token with the true prefix fed
+    (reference generate.py:545-582).  layer_fn(model, layer_idx, x, pos,
+    k_cache, v_cache) -> x selects the decode path."""
+    k_caches, v_caches = _kv_caches(model, max_seq_len)
+    total, count = 0.0, 0
+    for pos, tok in enumerate(token_ids[:-1]):
+        x = model.embed_tokens[tok]
+        for li in range(model.num_layers):
+            x = layer_fn(model, li, x, pos, k_caches[li], v_caches[li])
+        xn = ops.rmsnorm(x.unsqueeze(0), model.final_norm, model.rms_norm_eps).squeeze(0)
+        logp = F.log_softmax(ops.gemv_fp16_v3(model.lm_head, xn).float(), dim=-1)
+        total += -float(logp[token_ids[pos + 1]].item())
+        count += 1
+    return total / count
+
+
+def _calibrate(model: StreamingModel, token_ids: list[int], dip_k: int, max_seq_len: int, trace: bool):
+    I = model.matrix(0, "mlp.up_proj.weight").n
+    counts = [torch.zeros(I, dtype=torch.int64, device=model.device) for _ in range(model.num_layers)]
+    selected = [[] for _ in range(model.num_layers)] if trace else None
+    k_caches, v_caches = _kv_caches(model, max_seq_len)
+    pipeline = WeightPipeline(model, suffixes=DIP_DENSE_SUFFIXES)
+    bufs = DipBuffers.make(model, dip_k)
+    for pos, tok in enumerate(token_ids):
+        x = model.embed_tokens[tok]
+        for li in range(model.num_layers):
+            x = run_decoder_layer_dip(pipeline, model, li, x, pos, k_caches[li], v_caches[li], dip_k, bufs,
+                                      channel_counts=counts, selected_out=selected)
+    return counts, selected
+
+
+def calibrate_channel_frequencies(model: StreamingModel, token_ids: list[int], dip_k: int,
+                                  max_seq_len: int = 512) -> list[torch.Tensor]:
+    """Per layer, how many of the tokens selected each channel, teacher-forced
+    through the DIP path (reference generate.py:585-614)."""
+    return _calibrate(model, token_ids, dip_k, max_seq_len, trace=False)[0]
+
+
+def calibrate_with_trace(model: StreamingModel, token_ids: list[int], dip_k: int, max_seq_len: int = 512):
+    """As calibrate_channel_frequencies, plus the per-token, per-layer selected
+    index lists the adaptive cache policies replay (reference generate.py:617-645)."""
+    return _calibrate(model, token_ids, dip_k, max_seq_len, trace=True)
+
+
+__all__ = [
+    "StreamingModel", "WeightPipeline", "DipBuffers", "DIP_DENSE_SUFFIXES", "DOWN_PROJ_T_SUFFIX", "LINEAR_SUFFIXES",
+    "run_decoder_layer_streaming", "run_decoder_layer_dip", "run_decoder_layer_cached_dip", "dip_bytes_per_token",
+    "generate_streaming", "generate_dip", "generate_cached_dip", "teacher_forced_nll",
+    "calibrate_channel_frequencies", "calibrate_with_trace",
+]
