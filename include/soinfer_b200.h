@@ -315,6 +315,26 @@ int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
                              int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim, int64_t cur_len,
                              void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Device-position forms (no reference counterpart): the same kernels with the
+ * token position read from device memory when they run (*pos_dev), so a whole
+ * decode step -- its position advanced by a device op -- can be captured in a
+ * CUDA graph and replayed.  rope: cos_table / sin_table fp32
+ * [table_rows, head_dim/2], row *pos_dev (positions outside the table: no
+ * change).  kv append: written at *pos_dev (outside [0, max_seq_len): no
+ * write).  attention: over positions [0, *pos_dev + 1), clamped to
+ * [1, max_seq_len]; the launch is planned for max_seq_len. */
+int soinfer_rope_apply_at(soinfer_half* x, const float* cos_table, const float* sin_table,
+                          int64_t table_rows, int64_t num_heads, int64_t head_dim,
+                          const int32_t* pos_dev, void* stream);
+int soinfer_kv_cache_append_at(soinfer_half* k_cache, soinfer_half* v_cache, const soinfer_half* k_new,
+                               const soinfer_half* v_new, int64_t num_kv_heads, int64_t max_seq_len,
+                               int64_t head_dim, const int32_t* pos_dev, void* stream);
+int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cache,
+                                const soinfer_half* v_cache, soinfer_half* out, int64_t num_q_heads,
+                                int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim,
+                                const int32_t* pos_dev, void* workspace, int64_t workspace_bytes,
+                                void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

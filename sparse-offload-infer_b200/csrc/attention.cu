@@ -26,12 +26,18 @@ constexpr int kMaxSplits = 64;
 constexpr int kTargetCtas = 296;
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Attended length of the device-position form: *pos_dev + 1, clamped to [1, max_seq].
+__device__ __forceinline__ int device_cur_len(const int32_t* pos_dev, int64_t max_seq) {
+  const int64_t len = (int64_t)*pos_dev + 1;
+  return (int)(len < 1 ? 1 : (len > max_seq ? max_seq : len));
+}
+
 template <int TEAM, int REP>
 __global__ void __launch_bounds__(kThreads)
     attn_split_kernel(const half* __restrict__ q, const half* __restrict__ kc, const half* __restrict__ vc,
                       half* __restrict__ out, float* __restrict__ ws_acc, float* __restrict__ ws_ml, const int nq,
-                      const int nkv, const int64_t max_seq, const int hd, const int cur_len, const int L,
-                      const float scale_log2) {
+                      const int nkv, const int64_t max_seq, const int hd, const int cur_len_host, const int L,
+                      const float scale_log2, const int32_t* __restrict__ pos_dev) {
   constexpr int kTeams = kThreads / TEAM;
   extern __shared__ float smem[];
   float* s_p = smem;                        // [REP][L] scores, then probabilities
@@ -44,7 +50,6 @@ __global__ void __launch_bounds__(kThreads)
   const int n_rep = nq / nkv;
   const int qh0 = kvh * n_rep + blockIdx.z * REP;
   const int t0 = split * L;
-  const int t1 = (t0 + L < cur_len) ? t0 + L : cur_len;
   const int team = threadIdx.x / TEAM;
   const int tl = threadIdx.x % TEAM;
   const int d0 = tl * 8;
@@ -54,6 +59,12 @@ __global__ void __launch_bounds__(kThreads)
 
   pdl_launch_dependents();
   pdl_wait();
+  // device-position form: cur_len = *pos_dev + 1, read after the producer of
+  // pos_dev has finished; the launch was planned for max_seq, so splits past
+  // the live length have nothing to do
+  const int cur_len = pos_dev ? device_cur_len(pos_dev, max_seq) : cur_len_host;
+  if (t0 >= cur_len) return;
+  const int t1 = (t0 + L < cur_len) ? t0 + L : cur_len;
 
   float qf[REP][8];
 #pragma unroll
@@ -174,9 +185,15 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
-                                    half* __restrict__ out, const int hd, const int nsplit) {
+                                    half* __restrict__ out, const int hd, const int nsplit_launched, const int L,
+                                    const int64_t max_seq, const int32_t* __restrict__ pos_dev) {
   pdl_launch_dependents();
   pdl_wait();
+  int nsplit = nsplit_launched;
+  if (pos_dev) {  // only the splits the live length reached wrote partials
+    const int active = (device_cur_len(pos_dev, max_seq) + L - 1) / L;
+    nsplit = active < nsplit ? active : nsplit;
+  }
   const int qh = blockIdx.x;
   const float* ml = ws_ml + (int64_t)qh * kMaxSplits * 2;
   float M = -INFINITY;
@@ -195,7 +212,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_acc, const floa
 template <int TEAM, int REP>
 cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* out, float* ws_acc, float* ws_ml,
                          int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L, float scale_log2,
-                         int groups, cudaStream_t stream) {
+                         int groups, const int32_t* pos_dev, cudaStream_t stream) {
   constexpr int kTeams = kThreads / TEAM;
   const size_t smem = (size_t)(REP * L + kTeams * REP * hd) * sizeof(float);
   auto kernel = attn_split_kernel<TEAM, REP>;
@@ -204,19 +221,19 @@ cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* ou
     if (e != cudaSuccess) return e;
   }
   return launch_ex(kernel, dim3(nkv, nsplit, groups), dim3(kThreads), smem, stream, 1, false, q, kc, vc, out, ws_acc,
-                   ws_ml, nq, nkv, max_seq, hd, cur_len, L, scale_log2);
+                   ws_ml, nq, nkv, max_seq, hd, cur_len, L, scale_log2, pos_dev);
 }
 
 template <int TEAM>
 cudaError_t dispatch_rep(int rep, const half* q, const half* kc, const half* vc, half* out, float* ws_acc,
                          float* ws_ml, int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L,
-                         float sl2, int groups, cudaStream_t st) {
+                         float sl2, int groups, const int32_t* pd, cudaStream_t st) {
   switch (rep) {
-    case 1: return launch_split<TEAM, 1>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
-    case 2: return launch_split<TEAM, 2>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
-    case 4: return launch_split<TEAM, 4>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
-    case 5: return launch_split<TEAM, 5>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
-    case 8: return launch_split<TEAM, 8>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, st);
+    case 1: return launch_split<TEAM, 1>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
+    case 2: return launch_split<TEAM, 2>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
+    case 4: return launch_split<TEAM, 4>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
+    case 5: return launch_split<TEAM, 5>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
+    case 8: return launch_split<TEAM, 8>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -228,9 +245,11 @@ int64_t attention_workspace_bytes(int64_t nq, int64_t max_seq, int64_t hd) {
   return nq * kMaxSplits * (hd + 2) * (int64_t)sizeof(float);
 }
 
-cudaError_t launch_decode_attention(const half* q, const half* kc, const half* vc, half* out, int64_t nq, int64_t nkv,
-                                    int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
-                                    cudaStream_t stream) {
+namespace {
+
+cudaError_t decode_attention_impl(const half* q, const half* kc, const half* vc, half* out, int64_t nq, int64_t nkv,
+                                  int64_t max_seq, int64_t hd, int64_t plan_len, const int32_t* pos_dev,
+                                  void* workspace, cudaStream_t stream) {
   const int n_rep = (int)(nq / nkv);
   int rep;
   if (n_rep == 1 || n_rep == 2 || n_rep == 4 || n_rep == 5 || n_rep == 8)
@@ -244,11 +263,11 @@ cudaError_t launch_decode_attention(const half* q, const half* kc, const half* v
   const int groups = n_rep / rep;
   int64_t want = (kTargetCtas + nkv * groups - 1) / (nkv * groups);
   if (want > kMaxSplits) want = kMaxSplits;
-  const int64_t by_len = (cur_len + 15) / 16;
+  const int64_t by_len = (plan_len + 15) / 16;
   if (want > by_len) want = by_len;
   if (want < 1) want = 1;
-  const int L = (int)((cur_len + want - 1) / want);
-  const int nsplit = (int)((cur_len + L - 1) / L);
+  const int L = (int)((plan_len + want - 1) / want);
+  const int nsplit = (int)((plan_len + L - 1) / L);
   float* ws_acc = reinterpret_cast<float*>(workspace);
   float* ws_ml = ws_acc + nq * kMaxSplits * hd;
   const float sl2 = (1.0f / sqrtf((float)hd)) * kLog2e;
@@ -256,17 +275,32 @@ cudaError_t launch_decode_attention(const half* q, const half* kc, const half* v
   int team = 4;
   while (team < chunks) team <<= 1;
   cudaError_t e;
-  const int inq = (int)nq, inkv = (int)nkv, ihd = (int)hd, icl = (int)cur_len;
+  const int inq = (int)nq, inkv = (int)nkv, ihd = (int)hd, icl = (int)plan_len;
   switch (team) {
-    case 4: e = dispatch_rep<4>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
-    case 8: e = dispatch_rep<8>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
-    case 16: e = dispatch_rep<16>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
-    case 32: e = dispatch_rep<32>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, stream); break;
+    case 4: e = dispatch_rep<4>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
+    case 8: e = dispatch_rep<8>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
+    case 16: e = dispatch_rep<16>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
+    case 32: e = dispatch_rep<32>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess || nsplit == 1) return e;
   const int threads = ihd < 32 ? 32 : (ihd > 256 ? 256 : ihd);
-  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, false, ws_acc, ws_ml, out, ihd, nsplit);
+  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, false, ws_acc, ws_ml, out, ihd, nsplit,
+                   L, max_seq, pos_dev);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_attention(const half* q, const half* kc, const half* vc, half* out, int64_t nq, int64_t nkv,
+                                    int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
+                                    cudaStream_t stream) {
+  return decode_attention_impl(q, kc, vc, out, nq, nkv, max_seq, hd, cur_len, nullptr, workspace, stream);
+}
+
+cudaError_t launch_decode_attention_at(const half* q, const half* kc, const half* vc, half* out, int64_t nq,
+                                       int64_t nkv, int64_t max_seq, int64_t hd, const int32_t* pos_dev,
+                                       void* workspace, cudaStream_t stream) {
+  return decode_attention_impl(q, kc, vc, out, nq, nkv, max_seq, hd, max_seq, pos_dev, workspace, stream);
 }
 
 }  // namespace soinfer

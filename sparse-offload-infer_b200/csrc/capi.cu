@@ -494,4 +494,49 @@ int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
                      name);
 }
 
+int soinfer_rope_apply_at(soinfer_half* x, const float* cos_table, const float* sin_table, int64_t table_rows,
+                          int64_t num_heads, int64_t head_dim, const int32_t* pos_dev, void* stream) {
+  const char* name = "rope_apply_at";
+  REQUIRE(num_heads >= 0 && num_heads < (1ll << 31) && table_rows >= 1, "%s: invalid num_heads / table_rows", name);
+  REQUIRE(head_dim >= 2 && head_dim % 2 == 0, "%s: head_dim must be even", name);
+  if (num_heads == 0) return SOINFER_OK;
+  REQUIRE(x && cos_table && sin_table && pos_dev, "%s: null pointer", name);
+  return cuda_result(launch_rope_at(as_half(x), cos_table, sin_table, table_rows, num_heads, head_dim, pos_dev,
+                                    as_stream(stream)),
+                     name);
+}
+
+int soinfer_kv_cache_append_at(soinfer_half* k_cache, soinfer_half* v_cache, const soinfer_half* k_new,
+                               const soinfer_half* v_new, int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim,
+                               const int32_t* pos_dev, void* stream) {
+  const char* name = "kv_cache_append_at";
+  REQUIRE(num_kv_heads >= 0 && max_seq_len >= 1 && head_dim >= 1, "%s: invalid cache shape", name);
+  if (num_kv_heads == 0) return SOINFER_OK;
+  REQUIRE(k_cache && v_cache && k_new && v_new && pos_dev, "%s: null pointer", name);
+  return cuda_result(launch_kv_append_at(as_half(k_cache), as_half(v_cache), as_half(k_new), as_half(v_new),
+                                         num_kv_heads, max_seq_len, head_dim, pos_dev, as_stream(stream)),
+                     name);
+}
+
+int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cache, const soinfer_half* v_cache,
+                                soinfer_half* out, int64_t num_q_heads, int64_t num_kv_heads, int64_t max_seq_len,
+                                int64_t head_dim, const int32_t* pos_dev, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
+  const char* name = "decode_attention_at";
+  REQUIRE(num_kv_heads >= 1 && num_q_heads >= 1, "%s: head counts must be >= 1", name);
+  REQUIRE(num_q_heads % num_kv_heads == 0, "%s: num_q_heads must be a multiple of num_kv_heads", name);
+  REQUIRE(head_dim >= 8 && head_dim % 8 == 0 && head_dim <= 256, "%s: head_dim must be a multiple of 8 in [8, 256]",
+          name);
+  REQUIRE(max_seq_len >= 1 && num_q_heads < (1 << 20) && max_seq_len < (1ll << 31), "%s: sizes out of range", name);
+  REQUIRE(q && k_cache && v_cache && out && pos_dev, "%s: null pointer", name);
+  REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16), "%s: q and caches must be 16-byte aligned",
+          name);
+  REQUIRE(workspace && workspace_bytes >= attention_workspace_bytes(num_q_heads, max_seq_len, head_dim),
+          "%s: workspace too small", name);
+  return cuda_result(launch_decode_attention_at(as_half(q), as_half(k_cache), as_half(v_cache), as_half(out),
+                                                num_q_heads, num_kv_heads, max_seq_len, head_dim, pos_dev, workspace,
+                                                as_stream(stream)),
+                     name);
+}
+
 }  // extern "C"

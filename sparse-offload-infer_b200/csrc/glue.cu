@@ -48,11 +48,19 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// cv / sv: the position's cos / sin [head_dim / 2], or -- with pos_dev -- tables
+// [table_rows, head_dim / 2] indexed by *pos_dev (out-of-range positions: no-op).
 __global__ void rope_kernel(half* __restrict__ x, const float* __restrict__ cv, const float* __restrict__ sv,
-                            const int64_t head_dim) {
+                            const int64_t head_dim, const int32_t* __restrict__ pos_dev, const int64_t table_rows) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t half_dim = head_dim / 2;
+  if (pos_dev) {
+    const int64_t pos = *pos_dev;
+    if (pos < 0 || pos >= table_rows) return;
+    cv += pos * half_dim;
+    sv += pos * half_dim;
+  }
   half* row = x + (int64_t)blockIdx.x * head_dim;
   for (int64_t i = threadIdx.x; i < half_dim; i += blockDim.x) {
     const float c = cv[i], s = sv[i];
@@ -65,9 +73,13 @@ __global__ void rope_kernel(half* __restrict__ x, const float* __restrict__ cv, 
 
 __global__ void kv_append_kernel(half* __restrict__ kc, half* __restrict__ vc, const half* __restrict__ kn,
                                  const half* __restrict__ vn, const int64_t max_seq, const int64_t hd,
-                                 const int64_t pos) {
+                                 int64_t pos, const int32_t* __restrict__ pos_dev) {
   pdl_launch_dependents();
   pdl_wait();
+  if (pos_dev) {  // device-position form: out-of-range positions write nothing
+    pos = *pos_dev;
+    if (pos < 0 || pos >= max_seq) return;
+  }
   const int64_t h = blockIdx.x;
   half* kd = kc + (h * max_seq + pos) * hd;
   half* vd = vc + (h * max_seq + pos) * hd;
@@ -114,14 +126,30 @@ cudaError_t launch_rope(half* x, const float* cv, const float* sv, int64_t heads
                         cudaStream_t stream) {
   int threads = (int)(head_dim / 2);
   threads = threads < 32 ? 32 : (threads > 1024 ? 1024 : threads);
-  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, false, x, cv, sv, head_dim);
+  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, false, x, cv, sv, head_dim,
+                   (const int32_t*)nullptr, (int64_t)0);
+}
+
+cudaError_t launch_rope_at(half* x, const float* cos_table, const float* sin_table, int64_t table_rows, int64_t heads,
+                           int64_t head_dim, const int32_t* pos_dev, cudaStream_t stream) {
+  int threads = (int)(head_dim / 2);
+  threads = threads < 32 ? 32 : (threads > 1024 ? 1024 : threads);
+  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, false, x, cos_table, sin_table,
+                   head_dim, pos_dev, table_rows);
 }
 
 cudaError_t launch_kv_append(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                              int64_t hd, int64_t pos, cudaStream_t stream) {
   int threads = hd < 32 ? 32 : (hd > 256 ? 256 : (int)hd);
   return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, false, kc, vc, kn, vn, max_seq,
-                   hd, pos);
+                   hd, pos, (const int32_t*)nullptr);
+}
+
+cudaError_t launch_kv_append_at(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
+                                int64_t hd, const int32_t* pos_dev, cudaStream_t stream) {
+  int threads = hd < 32 ? 32 : (hd > 256 ? 256 : (int)hd);
+  return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, false, kc, vc, kn, vn, max_seq,
+                   hd, (int64_t)0, pos_dev);
 }
 
 cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,

@@ -95,7 +95,16 @@ cudaError_t launch_rope(half* x, const float* cos_v, const float* sin_v, int64_t
                         cudaStream_t stream);
 cudaError_t launch_kv_append(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                              int64_t hd, int64_t pos, cudaStream_t stream);
+// Device-position forms (CUDA-graph capturable decode step): the position is
+// read from device memory when the kernel runs.
+cudaError_t launch_rope_at(half* x, const float* cos_table, const float* sin_table, int64_t table_rows, int64_t heads,
+                           int64_t head_dim, const int32_t* pos_dev, cudaStream_t stream);
+cudaError_t launch_kv_append_at(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
+                                int64_t hd, const int32_t* pos_dev, cudaStream_t stream);
 int64_t attention_workspace_bytes(int64_t nq, int64_t max_seq, int64_t hd);
+cudaError_t launch_decode_attention_at(const half* q, const half* kc, const half* vc, half* out, int64_t nq,
+                                       int64_t nkv, int64_t max_seq, int64_t hd, const int32_t* pos_dev,
+                                       void* workspace, cudaStream_t stream);
 cudaError_t launch_decode_attention(const half* q, const half* kc, const half* vc, half* out, int64_t nq,
                                     int64_t nkv, int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
                                     cudaStream_t stream);

@@ -61,6 +61,9 @@ _SIGNATURES = {
     "soinfer_kv_cache_append": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_decode_attention_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "soinfer_decode_attention": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_rope_apply_at": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
 }
 
 
@@ -637,6 +640,67 @@ def kv_cache_append(k_cache, v_cache, k_new, v_new, pos: int) -> None:
     with torch.cuda.device(dev):
         _call("soinfer_kv_cache_append", _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), nkv, max_seq, hd,
               pos, _stream(dev))
+
+
+def _check_pos_dev(pos_dev, name):
+    _check(pos_dev.is_cuda and pos_dev.dtype == torch.int32 and pos_dev.numel() == 1, name,
+           "(pos_dev): must be a one-element int32 CUDA tensor")
+
+
+def rope_apply_at(x, cos_table, sin_table, pos_dev) -> None:
+    """rope_apply with the position read on the device: row *pos_dev of the
+    fp32 tables [max_pos, head_dim / 2] (capturable in a CUDA graph)."""
+    name = "rope_apply_at"
+    _f16(x, name + "(x)")
+    _check(x.dim() == 2 and x.size(1) % 2 == 0, name, ": x must be 2D [num_heads, even head_dim]")
+    for t, n in ((cos_table, "cos_table"), (sin_table, "sin_table")):
+        _f32(t, f"{name}({n})")
+        _check(t.dim() == 2 and t.size(1) == x.size(1) // 2 and t.is_contiguous(), name,
+               f"({n}): must be contiguous 2D [max_pos, head_dim / 2]")
+    _check(sin_table.shape == cos_table.shape, name, ": cos_table and sin_table must have the same shape")
+    _check_pos_dev(pos_dev, name)
+    dev = _same_device(x, cos_table, sin_table, pos_dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_rope_apply_at", _ptr(x), _ptr(cos_table), _ptr(sin_table), cos_table.size(0), x.size(0),
+              x.size(1), _ptr(pos_dev), _stream(dev))
+
+
+def kv_cache_append_at(k_cache, v_cache, k_new, v_new, pos_dev) -> None:
+    """kv_cache_append at position *pos_dev (read on the device)."""
+    name = "kv_cache_append_at"
+    for t, n in ((k_cache, "k_cache"), (v_cache, "v_cache"), (k_new, "k_new"), (v_new, "v_new")):
+        _f16(t, f"{name}({n})")
+    _check(k_cache.dim() == 3 and v_cache.shape == k_cache.shape, name,
+           ": k_cache/v_cache must be 3D [num_kv_heads, max_seq_len, head_dim] and same shape")
+    _check(k_new.shape == v_new.shape and k_new.dim() == 2 and k_new.size(0) == k_cache.size(0)
+           and k_new.size(1) == k_cache.size(2), name, ": k_new/v_new must be 2D [num_kv_heads, head_dim]")
+    _check_pos_dev(pos_dev, name)
+    nkv, max_seq, hd = k_cache.shape
+    dev = _same_device(k_cache, v_cache, k_new, v_new, pos_dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_kv_cache_append_at", _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), nkv, max_seq, hd,
+              _ptr(pos_dev), _stream(dev))
+
+
+def decode_attention_at(q, k_cache, v_cache, pos_dev, out: torch.Tensor | None = None) -> torch.Tensor:
+    """decode_attention over positions [0, *pos_dev + 1) (read on the device)."""
+    name = "decode_attention_at"
+    _f16(q, name + "(q)")
+    _f16(k_cache, name + "(k_cache)")
+    _f16(v_cache, name + "(v_cache)")
+    _check(q.dim() == 2 and k_cache.dim() == 3 and v_cache.shape == k_cache.shape and q.size(1) == k_cache.size(2),
+           name, ": q [num_q_heads, head_dim], caches [num_kv_heads, max_seq_len, head_dim]")
+    _check_pos_dev(pos_dev, name)
+    nq, (nkv, max_seq, hd) = q.size(0), k_cache.shape
+    _check(nq % nkv == 0, name, ": num_q_heads must be a multiple of num_kv_heads")
+    dev = _same_device(q, k_cache, v_cache, pos_dev)
+    y = out if out is not None else torch.empty(nq, hd, dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        nbytes = lib().soinfer_decode_attention_workspace_bytes(nq, max_seq, hd)
+        ws = _workspace("attn", dev, nbytes)
+        _call("soinfer_decode_attention_at", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(y), nq, nkv, max_seq, hd,
+              _ptr(pos_dev), ws.data_ptr(), ws.numel(), _stream(dev))
+    return y
 
 
 def decode_attention(q, k_cache, v_cache, cur_len: int, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -163,3 +163,31 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     qh // (NQ // NKV).  q: [NQ, hd] half (already RoPE'd); caches [NKV, max_seq, hd] half.
     Reference: ops.py:253-260."""
     return _C.decode_attention(q, k_cache, v_cache, cur_len)
+
+
+# ------------------------------------------------------------------ B200 additions: device-position forms
+def precompute_rope_table(head_dim: int, theta: float, max_pos: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """B200 addition: cos / sin tables [max_pos, head_dim / 2] whose row p equals
+    precompute_rope_cos_sin(head_dim, theta, p) element for element (same fp32 ops)."""
+    exponents = torch.arange(0, head_dim, 2, dtype=torch.float32, device=device) / head_dim
+    inv_freq = 1.0 / (theta ** exponents)
+    angles = torch.arange(max_pos, dtype=torch.float32, device=device)[:, None] * inv_freq[None, :]
+    return angles.cos().contiguous(), angles.sin().contiguous()
+
+
+def apply_rope_at(x: torch.Tensor, cos_table: torch.Tensor, sin_table: torch.Tensor, pos_dev: torch.Tensor) -> torch.Tensor:
+    """B200 addition: apply_rope (in place on x, returns x) with the position read on the device (rows of the
+    tables); graph-capturable."""
+    _C.rope_apply_at(x, cos_table, sin_table, pos_dev)
+    return x
+
+
+def kv_cache_append_at(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                       pos_dev: torch.Tensor) -> None:
+    """B200 addition: kv_cache_append at the device position *pos_dev; graph-capturable."""
+    _C.kv_cache_append_at(k_cache, v_cache, k_new.contiguous(), v_new.contiguous(), pos_dev)
+
+
+def decode_attention_at(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos_dev: torch.Tensor) -> torch.Tensor:
+    """B200 addition: decode_attention over [0, *pos_dev + 1), the length read on the device; graph-capturable."""
+    return _C.decode_attention_at(q.contiguous(), k_cache, v_cache, pos_dev)

@@ -137,6 +137,18 @@ class WeightPipeline:
 
 
 # --------------------------------------------------------------- attention
+@dataclass
+class DevicePosition:
+    """A token position held on the device (int32 [1]) with RoPE tables
+    [max_seq, head_dim/2]: passed as `pos` to the layer functions it makes a
+    decode step independent of host values, so it can be captured in a CUDA
+    graph and replayed while the position advances on the device."""
+
+    pos: torch.Tensor
+    cos_table: torch.Tensor
+    sin_table: torch.Tensor
+
+
 def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
                      k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """rmsnorm -> q/k/v GEMVs -> q/k norm -> RoPE -> KV append -> GQA decode
@@ -150,11 +162,17 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
     v = pipeline.next_gemv(h).view(NKV, HD)
     q = ops.qk_norm(q, norms["q_norm"], eps)
     k = ops.qk_norm(k, norms["k_norm"], eps)
-    cos_vals, sin_vals = ops.precompute_rope_cos_sin(HD, model.rope_theta, pos, device=x_flat.device)
-    q = ops.apply_rope(q, cos_vals, sin_vals)
-    k = ops.apply_rope(k, cos_vals, sin_vals)
-    ops.kv_cache_append(k_cache, v_cache, k, v, pos)
-    attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
+    if isinstance(pos, DevicePosition):
+        q = ops.apply_rope_at(q, pos.cos_table, pos.sin_table, pos.pos)
+        k = ops.apply_rope_at(k, pos.cos_table, pos.sin_table, pos.pos)
+        ops.kv_cache_append_at(k_cache, v_cache, k, v, pos.pos)
+        attn = ops.decode_attention_at(q, k_cache, v_cache, pos.pos).reshape(NQ * HD)
+    else:
+        cos_vals, sin_vals = ops.precompute_rope_cos_sin(HD, model.rope_theta, pos, device=x_flat.device)
+        q = ops.apply_rope(q, cos_vals, sin_vals)
+        k = ops.apply_rope(k, cos_vals, sin_vals)
+        ops.kv_cache_append(k_cache, v_cache, k, v, pos)
+        attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
     h2 = x_flat + pipeline.next_gemv(attn)
     h3 = ops.rmsnorm(h2.unsqueeze(0), norms["post_attention_layernorm"], eps).squeeze(0)
     return h2, h3
@@ -364,6 +382,83 @@ def generate_cached_dip(model: StreamingModel, prompt_ids: list[int], n_new: int
                    eos_token_id, max_seq_len)
 
 
+class GraphDecoder:
+    """Greedy decode with one CUDA graph per step (B200 addition).
+
+    The step -- embedding of ids[pos], every decoder layer (dense or DIP),
+    final norm, the LM head with its fused argmax, then ids[pos + 1] =
+    next token unless it is still a prompt token, pos += 1 -- reads and writes
+    only device state, so it is captured once and replayed; generating n
+    tokens after a P-token prompt is P + n - 1 replays with no host work in
+    between.  Weights must be HBM-resident.  Tokens equal generate_streaming /
+    generate_dip on the same model (same kernels, same order)."""
+
+    def __init__(self, model: StreamingModel, dip_k: int | None = None, max_seq_len: int = 2048):
+        names = [f"model.layers.{i}.{s}" for i in range(model.num_layers) for s in LINEAR_SUFFIXES]
+        if dip_k is not None:
+            names.append(f"model.layers.0.{DOWN_PROJ_T_SUFFIX}")
+        if not all(model.is_resident(n) for n in names):
+            raise ValueError("GraphDecoder needs every decoder weight resident in HBM (StreamingModel.resident)")
+        self.model, self.dip_k, self.max_seq_len = model, dip_k, max_seq_len
+        dev = model.device
+        self.stream = torch.cuda.Stream(dev)
+        self.ids = torch.zeros(max_seq_len + 1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.prompt_len = torch.zeros(1, dtype=torch.int32, device=dev)
+        cos_t, sin_t = ops.precompute_rope_table(model.head_dim, model.rope_theta, max_seq_len, dev)
+        self.where = DevicePosition(self.pos, cos_t, sin_t)
+        self.k_caches, self.v_caches = _kv_caches(model, max_seq_len)
+        suffixes = LINEAR_SUFFIXES if dip_k is None else DIP_DENSE_SUFFIXES
+        self.pipeline = WeightPipeline(model, suffixes=suffixes)
+        self.bufs = DipBuffers.make(model, dip_k) if dip_k is not None else None
+        self.graph = None
+
+    def _step(self) -> None:
+        m, where = self.model, self.where
+        x = m.embed_tokens.index_select(0, self.ids.index_select(0, self.pos.long()).long()).view(-1)
+        for li in range(m.num_layers):
+            if self.dip_k is None:
+                x = run_decoder_layer_streaming(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
+            else:
+                x = run_decoder_layer_dip(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li],
+                                          self.dip_k, self.bufs)
+        xn = ops.rmsnorm(x.unsqueeze(0), m.final_norm, m.rms_norm_eps).squeeze(0)
+        nxt = ops.lm_head_argmax(m.lm_head, xn)
+        at = (self.pos + 1).long()
+        keep = (self.pos + 1) < self.prompt_len  # still inside the prompt: keep its token
+        self.ids.index_copy_(0, at, torch.where(keep, self.ids.index_select(0, at), nxt))
+        self.pos.add_(1)
+
+    def _capture(self) -> None:
+        with torch.cuda.stream(self.stream):
+            self.pos.zero_()
+            self._step()  # warm-up: workspaces and lazy initialisation outside the capture
+            self.stream.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=self.stream):
+                self._step()
+        torch.cuda.synchronize(self.model.device)
+
+    def generate(self, prompt_ids: list[int], n_new: int) -> list[int]:
+        P = len(prompt_ids)
+        if P < 1 or P + n_new > self.max_seq_len:
+            raise ValueError(f"need 1 <= prompt length and prompt + n_new <= max_seq_len ({self.max_seq_len})")
+        if self.graph is None:
+            self._capture()
+        with torch.cuda.stream(self.stream):
+            self.ids.zero_()
+            self.ids[:P].copy_(torch.tensor(prompt_ids, dtype=torch.int32), non_blocking=False)
+            self.prompt_len.fill_(P)
+            self.pos.zero_()
+            for kc, vc in zip(self.k_caches, self.v_caches):
+                kc.zero_()
+                vc.zero_()
+            for _ in range(P + n_new - 1):
+                self.graph.replay()
+        self.stream.synchronize()
+        return self.ids[: P + n_new].cpu().tolist()
+
+
 def teacher_forced_nll(model: StreamingModel, layer_fn, token_ids: list[int], max_seq_len: int = 512) -> float:
     """Mean NLL of each real next token with the true prefix fed
     (reference generate.py:545-582).  layer_fn(model, layer_idx, x, pos,
@@ -413,5 +508,5 @@ __all__ = [
     "StreamingModel", "WeightPipeline", "DipBuffers", "DIP_DENSE_SUFFIXES", "DOWN_PROJ_T_SUFFIX", "LINEAR_SUFFIXES",
     "run_decoder_layer_streaming", "run_decoder_layer_dip", "run_decoder_layer_cached_dip", "dip_bytes_per_token",
     "generate_streaming", "generate_dip", "generate_cached_dip", "teacher_forced_nll",
-    "calibrate_channel_frequencies", "calibrate_with_trace",
+    "calibrate_channel_frequencies", "calibrate_with_trace", "DevicePosition", "GraphDecoder",
 ]
