@@ -144,24 +144,24 @@ __device__ __forceinline__ float chunk_bias(const uint8_t* xc, int g, int t) {
 }
 
 // Biased row sums of one 128-K chunk for the thread's two MMA rows (see file
-// comment): returns E + O / 16 for rows g and g + 8, in four independent MMA
-// chains of depth two.
+// comment): returns E + O / 16 for rows g and g + 8, in two MMA chains (one
+// per nibble position class) of depth four.
 __device__ __forceinline__ void chunk_dot(const uint4 wa, const uint4 wb, const uint4 xf[4], float& s0, float& s1) {
   const uint32_t r0[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t r1[4] = {wb.x, wb.y, wb.z, wb.w};
-  float e[2][4] = {}, o[2][4] = {};
+  float e[4] = {0.f, 0.f, 0.f, 0.f}, o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t t0 = r0[j] >> 8, t1 = r1[j] >> 8;
     const uint32_t ae[4] = {lop3_and_xor(r0[j], 0x000f000fu, 0x64086408u), lop3_and_xor(r1[j], 0x000f000fu, 0x64086408u),
                             lop3_and_xor(t0, 0x000f000fu, 0x64086408u), lop3_and_xor(t1, 0x000f000fu, 0x64086408u)};
-    mma_16816(e[j & 1], ae, xf[j].x, xf[j].z);  // (v0,v1) with x0x1, (v4,v5) with x4x5
+    mma_16816(e, ae, xf[j].x, xf[j].z);  // (v0,v1) with x0x1, (v4,v5) with x4x5
     const uint32_t ao[4] = {lop3_and_xor(r0[j], 0x00f000f0u, 0x64806480u), lop3_and_xor(r1[j], 0x00f000f0u, 0x64806480u),
                             lop3_and_xor(t0, 0x00f000f0u, 0x64806480u), lop3_and_xor(t1, 0x00f000f0u, 0x64806480u)};
-    mma_16816(o[j & 1], ao, xf[j].y, xf[j].w);  // (v2,v3) with x2x3, (v6,v7) with x6x7
+    mma_16816(o, ao, xf[j].y, xf[j].w);  // (v2,v3) with x2x3, (v6,v7) with x6x7
   }
-  s0 = fmaf(o[0][0] + o[1][0], 0.0625f, e[0][0] + e[1][0]);
-  s1 = fmaf(o[0][2] + o[1][2], 0.0625f, e[0][2] + e[1][2]);
+  s0 = fmaf(o[0], 0.0625f, e[0]);
+  s1 = fmaf(o[2], 0.0625f, e[2]);
 }
 
 struct TaskView {

@@ -439,7 +439,9 @@ class GraphDecoder:
                 self._step()
         torch.cuda.synchronize(self.model.device)
 
-    def generate(self, prompt_ids: list[int], n_new: int) -> list[int]:
+    def generate(self, prompt_ids: list[int], n_new: int, timings: dict | None = None) -> list[int]:
+        """timings (optional): filled with CUDA-event milliseconds of the prompt
+        replays ("prefill_ms") and of the n_new - 1 generating replays ("decode_ms")."""
         P = len(prompt_ids)
         if P < 1 or P + n_new > self.max_seq_len:
             raise ValueError(f"need 1 <= prompt length and prompt + n_new <= max_seq_len ({self.max_seq_len})")
@@ -453,9 +455,18 @@ class GraphDecoder:
             for kc, vc in zip(self.k_caches, self.v_caches):
                 kc.zero_()
                 vc.zero_()
-            for _ in range(P + n_new - 1):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(self.stream)
+            for _ in range(P):
                 self.graph.replay()
+            ev[1].record(self.stream)
+            for _ in range(n_new - 1):
+                self.graph.replay()
+            ev[2].record(self.stream)
         self.stream.synchronize()
+        if timings is not None:
+            timings["prefill_ms"] = ev[0].elapsed_time(ev[1])
+            timings["decode_ms"] = ev[1].elapsed_time(ev[2])
         return self.ids[: P + n_new].cpu().tolist()
 
 
