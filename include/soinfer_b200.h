@@ -153,6 +153,13 @@ int soinfer_gemv_w8a16(const int8_t* Wq, const float* scale, const soinfer_half*
 int soinfer_topk_threshold_select(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx,
                                   int32_t* out_count, void* stream);
 
+/* soinfer_topk_threshold_select on |gate| of an fp16 gate vector: the values
+ * selected on are exactly the fp32 |float(gate[i])| the reference computes
+ * with gate.float().abs() before selecting (runtime/generate.py:276-278).
+ * No reference counterpart (fuses that conversion into the selector). */
+int soinfer_topk_threshold_select_abs_f16(const soinfer_half* gate, int64_t n, int64_t k,
+                                          int32_t* out_idx, int32_t* out_count, void* stream);
+
 /* Exact top-k ("exact mode"): the k largest values, ties at the k-th value
  * broken by the lower index, written in ascending index order; *out_count = k.
  * NaN ranks below every number.  Same buffers as the ref-mode selector.
@@ -314,6 +321,34 @@ int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
                              const soinfer_half* v_cache, soinfer_half* out, int64_t num_q_heads,
                              int64_t num_kv_heads, int64_t max_seq_len, int64_t head_dim, int64_t cur_len,
                              void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Fused decode-layer glue (no reference counterpart; each equals the
+ * reference's unfused composition).
+ * add_rmsnorm: sum_out = fp16(x + x2) (fp32 add, one rounding: the fp16
+ * residual add), out = rmsnorm(sum_out, weight) as soinfer_rmsnorm;
+ * bit-identical to the two ops.  x, x2, out, sum_out: fp16 [rows, hidden].
+ * swiglu: out[i] = fp16(silu(float(g_i)) * float(up[i])) with g_i = gate[idx[i]]
+ * (idx may be NULL: gate[i]); silu(x) = x / (1 + exp(-x)) in fp32 -- the
+ * reference's (F.silu(g.float()) * u.float()).half(), generate.py:300-302.
+ * head_norm_rope: after the q / k / v GEMVs of one token: RMSNorm of every q
+ * and k head (q_norm / k_norm weights, fp16 [head_dim]), rotate-half RoPE of
+ * the normalised values (q rewritten in place), k and v appended to the
+ * caches at pos -- or, when pos_dev is not NULL, at *pos_dev with cos / sin
+ * tables [table_rows, head_dim/2] indexed by it (out-of-range: nothing
+ * written).  q: fp16 [num_q_heads, head_dim]; k, v: [num_kv_heads, head_dim];
+ * head_dim even and <= 256.  Replaces the reference's qk_norm x2, rope x2 and
+ * kv_cache_append sequence (generate.py:243-252). */
+int soinfer_add_rmsnorm(const soinfer_half* x, const soinfer_half* x2, const soinfer_half* weight,
+                        soinfer_half* out, soinfer_half* sum_out, int64_t rows, int64_t hidden,
+                        float eps, void* stream);
+int soinfer_swiglu(const soinfer_half* gate, const soinfer_half* up, const int32_t* idx,
+                   soinfer_half* out, int64_t n, void* stream);
+int soinfer_head_norm_rope(soinfer_half* q, const soinfer_half* k, const soinfer_half* v,
+                           const soinfer_half* q_norm, const soinfer_half* k_norm,
+                           const float* cos_vals, const float* sin_vals, int64_t table_rows,
+                           soinfer_half* k_cache, soinfer_half* v_cache, int64_t num_q_heads,
+                           int64_t num_kv_heads, int64_t head_dim, int64_t max_seq_len, int64_t pos,
+                           const int32_t* pos_dev, float eps, void* stream);
 
 /* Device-position forms (no reference counterpart): the same kernels with the
  * token position read from device memory when they run (*pos_dev), so a whole

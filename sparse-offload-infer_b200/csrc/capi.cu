@@ -250,6 +250,15 @@ int soinfer_topk_threshold_select(const float* abs_g, int64_t n, int64_t k, int3
   return topk_common("topk_threshold_select", false, abs_g, n, k, out_idx, out_count, stream);
 }
 
+int soinfer_topk_threshold_select_abs_f16(const soinfer_half* gate, int64_t n, int64_t k, int32_t* out_idx,
+                                          int32_t* out_count, void* stream) {
+  const char* name = "topk_threshold_select_abs_f16";
+  REQUIRE(n >= 1 && n < (1ll << 31), "%s: n must be in [1, 2^31)", name);
+  REQUIRE(k >= 1 && k <= n, "%s: k must be in [1, n]", name);
+  REQUIRE(gate && out_idx && out_count, "%s: null pointer", name);
+  return cuda_result(launch_topk_abs_half(false, as_half(gate), n, k, out_idx, out_count, as_stream(stream)), name);
+}
+
 int soinfer_topk_select_exact(const float* abs_g, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
                               void* stream) {
   return topk_common("topk_select_exact", true, abs_g, n, k, out_idx, out_count, stream);
@@ -491,6 +500,48 @@ int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
   return cuda_result(launch_decode_attention(as_half(q), as_half(k_cache), as_half(v_cache), as_half(out), num_q_heads,
                                              num_kv_heads, max_seq_len, head_dim, cur_len, workspace,
                                              as_stream(stream)),
+                     name);
+}
+
+int soinfer_add_rmsnorm(const soinfer_half* x, const soinfer_half* x2, const soinfer_half* weight, soinfer_half* out,
+                        soinfer_half* sum_out, int64_t rows, int64_t hidden, float eps, void* stream) {
+  const char* name = "add_rmsnorm";
+  REQUIRE(rows >= 0 && rows < (1ll << 31) && hidden >= 2 && hidden % 2 == 0, "%s: invalid shape (hidden even)", name);
+  if (rows == 0) return SOINFER_OK;
+  REQUIRE(x && x2 && weight && out && sum_out, "%s: null pointer", name);
+  REQUIRE(aligned(x, 4) && aligned(x2, 4) && aligned(weight, 4) && aligned(out, 4) && aligned(sum_out, 4),
+          "%s: misaligned pointer", name);
+  return cuda_result(launch_add_rmsnorm(as_half(x), as_half(x2), as_half(weight), as_half(out), as_half(sum_out), rows,
+                                        hidden, eps, as_stream(stream)),
+                     name);
+}
+
+int soinfer_swiglu(const soinfer_half* gate, const soinfer_half* up, const int32_t* idx, soinfer_half* out, int64_t n,
+                   void* stream) {
+  const char* name = "swiglu";
+  REQUIRE(n >= 0, "%s: n must be >= 0", name);
+  if (n == 0) return SOINFER_OK;
+  REQUIRE(gate && up && out, "%s: null pointer", name);
+  return cuda_result(launch_swiglu(as_half(gate), as_half(up), idx, as_half(out), n, as_stream(stream)), name);
+}
+
+int soinfer_head_norm_rope(soinfer_half* q, const soinfer_half* k, const soinfer_half* v, const soinfer_half* q_norm,
+                           const soinfer_half* k_norm, const float* cos_vals, const float* sin_vals, int64_t table_rows,
+                           soinfer_half* k_cache, soinfer_half* v_cache, int64_t num_q_heads, int64_t num_kv_heads,
+                           int64_t head_dim, int64_t max_seq_len, int64_t pos, const int32_t* pos_dev, float eps,
+                           void* stream) {
+  const char* name = "head_norm_rope";
+  REQUIRE(num_q_heads >= 1 && num_kv_heads >= 1 && num_q_heads + 2 * num_kv_heads < (1ll << 30),
+          "%s: invalid head counts", name);
+  REQUIRE(head_dim >= 2 && head_dim % 2 == 0 && head_dim <= 256, "%s: head_dim must be even and <= 256", name);
+  REQUIRE(max_seq_len >= 1, "%s: invalid max_seq_len", name);
+  REQUIRE(pos_dev || (pos >= 0 && pos < max_seq_len), "%s: pos out of range for max_seq_len", name);
+  REQUIRE(!pos_dev || table_rows >= 1, "%s: table_rows must be >= 1 with pos_dev", name);
+  REQUIRE(q && k && v && q_norm && k_norm && cos_vals && sin_vals && k_cache && v_cache, "%s: null pointer", name);
+  return cuda_result(launch_head_norm_rope(as_half(q), as_half(k), as_half(v), as_half(q_norm), as_half(k_norm),
+                                           cos_vals, sin_vals, as_half(k_cache), as_half(v_cache), num_q_heads,
+                                           num_kv_heads, head_dim, max_seq_len, pos, pos_dev, table_rows, eps,
+                                           as_stream(stream)),
                      name);
 }
 

@@ -14,21 +14,34 @@ namespace {
 
 constexpr int kNormThreads = 256;
 
+// ADD: the normalised row is v = fp16(x + x2) (fp32 add, one rounding -- the
+// fp16 tensor add of the reference's residual), also written to sum_out.
+template <bool ADD>
+__device__ __forceinline__ half2 norm_input(const half2* xr, const half2* x2r, int64_t i) {
+  if (!ADD) return xr[i];
+  const float2 a = __half22float2(xr[i]), b = __half22float2(x2r[i]);
+  return __floats2half2_rn(a.x + b.x, a.y + b.y);
+}
+
+template <bool ADD>
 __global__ void __launch_bounds__(kNormThreads)
-    rmsnorm_kernel(const half* __restrict__ x, const half* __restrict__ w, half* __restrict__ out, const int64_t hidden,
-                   const float eps) {
+    rmsnorm_kernel(const half* __restrict__ x, const half* __restrict__ x2, const half* __restrict__ w,
+                   half* __restrict__ out, half* __restrict__ sum_out, const int64_t hidden, const float eps) {
   __shared__ float s_part[kNormThreads / 32];
   __shared__ float s_inv;
   pdl_launch_dependents();
   pdl_wait();
   const int64_t row = blockIdx.x;
   const half2* xr = reinterpret_cast<const half2*>(x + row * hidden);
+  const half2* x2r = ADD ? reinterpret_cast<const half2*>(x2 + row * hidden) : nullptr;
   half2* orow = reinterpret_cast<half2*>(out + row * hidden);
   const half2* w2 = reinterpret_cast<const half2*>(w);
   const int64_t h2 = hidden / 2;
   float ss = 0.f;
   for (int64_t i = threadIdx.x; i < h2; i += kNormThreads) {
-    const float2 f = __half22float2(xr[i]);
+    const half2 hv = norm_input<ADD>(xr, x2r, i);
+    if (ADD) reinterpret_cast<half2*>(sum_out + row * hidden)[i] = hv;
+    const float2 f = __half22float2(hv);
     ss += f.x * f.x + f.y * f.y;
   }
   ss = warp_sum(ss);
@@ -42,9 +55,83 @@ __global__ void __launch_bounds__(kNormThreads)
   __syncthreads();
   const float inv = s_inv;
   for (int64_t i = threadIdx.x; i < h2; i += kNormThreads) {
-    const float2 f = __half22float2(xr[i]);
+    const float2 f = __half22float2(norm_input<ADD>(xr, x2r, i));
     const float2 g = __half22float2(w2[i]);
     orow[i] = __floats2half2_rn(f.x * inv * g.x, f.y * inv * g.y);
+  }
+}
+
+// out[i] = fp16( silu(float(g)) * float(up[i]) ), g = gate[idx[i]] (or gate[i]);
+// silu(x) = x / (1 + exp(-x)), the fp32 expression of torch's F.silu.
+__global__ void swiglu_kernel(const half* __restrict__ gate, const half* __restrict__ up,
+                              const int32_t* __restrict__ idx, half* __restrict__ out, const int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float g = __half2float(gate[idx ? idx[i] : i]);
+    const float s = g / (1.0f + expf(-g));
+    out[i] = __float2half_rn(s * __half2float(up[i]));
+  }
+}
+
+// After the q / k / v GEMVs of one decode token (rows: q heads, then k heads,
+// then v heads; one warp per row): q and k rows get RMSNorm over the head
+// (fp32 sum of squares, out = fp16((x * rsqrt(mean + eps)) * w)) followed by
+// rotate-half RoPE on the normalised fp16 values; q is rewritten in place,
+// the k and v rows are appended to the caches at `pos` (or *pos_dev).
+// cv / sv: the position's cos / sin, or with pos_dev tables indexed by it.
+constexpr int kHeadRowsPerBlock = 4;
+
+__global__ void __launch_bounds__(kHeadRowsPerBlock * 32)
+    head_norm_rope_kernel(half* __restrict__ q, const half* __restrict__ k, const half* __restrict__ v,
+                          const half* __restrict__ qw, const half* __restrict__ kw, const float* __restrict__ cv,
+                          const float* __restrict__ sv, half* __restrict__ kc, half* __restrict__ vc, const int nq,
+                          const int nkv, const int hd, const int64_t max_seq, int64_t pos,
+                          const int32_t* __restrict__ pos_dev, const int64_t table_rows, const float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x * kHeadRowsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= nq + 2 * nkv) return;
+  if (pos_dev) {
+    pos = *pos_dev;
+    if (pos < 0 || pos >= max_seq || pos >= table_rows) return;
+    cv += pos * (hd / 2);
+    sv += pos * (hd / 2);
+  }
+  const int half_dim = hd / 2;
+  if (row >= nq + nkv) {  // v: copy into the cache
+    const int h = row - nq - nkv;
+    const half* src = v + (int64_t)h * hd;
+    half* dst = vc + ((int64_t)h * max_seq + pos) * hd;
+    for (int i = lane; i < hd; i += 32) dst[i] = src[i];
+    return;
+  }
+  const bool is_q = row < nq;
+  const int h = is_q ? row : row - nq;
+  const half* src = is_q ? q + (int64_t)h * hd : k + (int64_t)h * hd;
+  const half* w = is_q ? qw : kw;
+  float ss = 0.f;
+  for (int i = lane; i < hd; i += 32) {
+    const float f = __half2float(src[i]);
+    ss = fmaf(f, f, ss);
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)hd + eps);
+  half* dst = is_q ? q + (int64_t)h * hd : kc + ((int64_t)h * max_seq + pos) * hd;
+  // pairs (i, i + hd/2): normalise both (rounded to fp16), then rotate
+  float x1[4], x2[4];
+  int n = 0;
+  for (int i = lane; i < half_dim; i += 32, ++n) {
+    x1[n] = __half2float(__float2half_rn(__half2float(src[i]) * inv * __half2float(w[i])));
+    x2[n] = __half2float(__float2half_rn(__half2float(src[i + half_dim]) * inv * __half2float(w[i + half_dim])));
+  }
+  __syncwarp();  // every lane has read its q values before any lane rewrites q in place
+  n = 0;
+  for (int i = lane; i < half_dim; i += 32, ++n) {
+    const float c = cv[i], s = sv[i];
+    dst[i] = __float2half_rn(x1[n] * c - x2[n] * s);
+    dst[i + half_dim] = __float2half_rn(x2[n] * c + x1[n] * s);
   }
 }
 
@@ -118,8 +205,33 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ matrix, const int
 
 cudaError_t launch_rmsnorm(const half* x, const half* w, half* out, int64_t rows, int64_t hidden, float eps,
                            cudaStream_t stream) {
-  return launch_ex(rmsnorm_kernel, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, false, x, w, out, hidden,
-                   eps);
+  return launch_ex(rmsnorm_kernel<false>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, false, x,
+                   (const half*)nullptr, w, out, (half*)nullptr, hidden, eps);
+}
+
+cudaError_t launch_add_rmsnorm(const half* x, const half* x2, const half* w, half* out, half* sum_out, int64_t rows,
+                               int64_t hidden, float eps, cudaStream_t stream) {
+  return launch_ex(rmsnorm_kernel<true>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, false, x, x2, w, out,
+                   sum_out, hidden, eps);
+}
+
+cudaError_t launch_swiglu(const half* gate, const half* up, const int32_t* idx, half* out, int64_t n,
+                          cudaStream_t stream) {
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  if (blocks > 1184) blocks = 1184;
+  if (blocks < 1) blocks = 1;
+  return launch_ex(swiglu_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, false, gate, up, idx, out, n);
+}
+
+cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const half* qw, const half* kw,
+                                  const float* cv, const float* sv, half* kc, half* vc, int64_t nq, int64_t nkv,
+                                  int64_t hd, int64_t max_seq, int64_t pos, const int32_t* pos_dev,
+                                  int64_t table_rows, float eps, cudaStream_t stream) {
+  const int64_t rows = nq + 2 * nkv;
+  const unsigned blocks = (unsigned)((rows + kHeadRowsPerBlock - 1) / kHeadRowsPerBlock);
+  return launch_ex(head_norm_rope_kernel, dim3(blocks), dim3(kHeadRowsPerBlock * 32), 0, stream, 1, false, q, k, v,
+                   qw, kw, cv, sv, kc, vc, (int)nq, (int)nkv, (int)hd, max_seq, pos, pos_dev, table_rows, eps);
 }
 
 cudaError_t launch_rope(half* x, const float* cv, const float* sv, int64_t heads, int64_t head_dim,

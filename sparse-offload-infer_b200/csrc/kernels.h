@@ -95,6 +95,20 @@ cudaError_t launch_rope(half* x, const float* cos_v, const float* sin_v, int64_t
                         cudaStream_t stream);
 cudaError_t launch_kv_append(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                              int64_t hd, int64_t pos, cudaStream_t stream);
+// Fused decode glue: residual add + RMSNorm (sum_out = fp16(x + x2), out =
+// rmsnorm(sum_out), bit-identical to the two ops); SwiGLU (optionally over
+// gate[idx[i]]); per-head q / k RMSNorm + RoPE + KV append (head_dim <= 256).
+cudaError_t launch_add_rmsnorm(const half* x, const half* x2, const half* w, half* out, half* sum_out, int64_t rows,
+                               int64_t hidden, float eps, cudaStream_t stream);
+cudaError_t launch_swiglu(const half* gate, const half* up, const int32_t* idx, half* out, int64_t n,
+                          cudaStream_t stream);
+cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const half* qw, const half* kw,
+                                  const float* cv, const float* sv, half* kc, half* vc, int64_t nq, int64_t nkv,
+                                  int64_t hd, int64_t max_seq, int64_t pos, const int32_t* pos_dev,
+                                  int64_t table_rows, float eps, cudaStream_t stream);
+cudaError_t launch_topk_abs_half(bool exact, const half* v, int64_t n, int64_t k, int32_t* out_idx,
+                                 int32_t* out_count, cudaStream_t stream);
+
 // Device-position forms (CUDA-graph capturable decode step): the position is
 // read from device memory when the kernel runs.
 cudaError_t launch_rope_at(half* x, const float* cos_table, const float* sin_table, int64_t table_rows, int64_t heads,

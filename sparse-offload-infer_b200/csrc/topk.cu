@@ -60,9 +60,17 @@ __device__ __forceinline__ int block_warp_scan(int warp_total, int* s_warp, int*
   return s_warp[warp];
 }
 
-template <bool EXACT, bool SMEM>
+// Selector input: fp32 values, or (HALF_ABS) |x| of fp16 values -- exactly
+// the fp32 tensor gate.float().abs() that the reference feeds the selector.
+template <bool HALF_ABS>
+__device__ __forceinline__ float sel_value(const void* v, int i) {
+  if (HALF_ABS) return fabsf(__half2float(static_cast<const half*>(v)[i]));
+  return static_cast<const float*>(v)[i];
+}
+
+template <bool EXACT, bool SMEM, bool HALF_ABS>
 __global__ void __launch_bounds__(kThreads)
-    topk_kernel(const float* __restrict__ v, const int n, const int k, int32_t* __restrict__ out_idx,
+    topk_kernel(const void* __restrict__ v, const int n, const int k, int32_t* __restrict__ out_idx,
                 int32_t* __restrict__ out_count) {
   extern __shared__ uint32_t skeys[];
   __shared__ uint32_t hist[256];
@@ -81,7 +89,7 @@ __global__ void __launch_bounds__(kThreads)
   // 1) keys (+ max for the reference's upper bisection bound)
   float lmax = 0.f;  // reference: local_max starts at 0 (topk_select.cu:19)
   for (int i = tid; i < n; i += kThreads) {
-    const float f = v[i];
+    const float f = sel_value<HALF_ABS>(v, i);
     lmax = fmaxf(lmax, f);
     if (SMEM) skeys[i] = float_key(f);
   }
@@ -102,7 +110,7 @@ __global__ void __launch_bounds__(kThreads)
       bool match = false;
       uint32_t bin = 0;
       if (i < n) {
-        const uint32_t key = SMEM ? skeys[i] : float_key(v[i]);
+        const uint32_t key = SMEM ? skeys[i] : float_key(sel_value<HALF_ABS>(v, i));
         match = (key & mask) == prefix;
         bin = (key >> shift) & 255u;
       }
@@ -168,7 +176,7 @@ __global__ void __launch_bounds__(kThreads)
   for (int tile = 0; tile < tiles && base < k; ++tile) {
     const int i = tile * kThreads + tid;
     const bool valid = i < n;
-    const uint32_t key = valid ? (SMEM ? skeys[i] : float_key(v[i])) : 0u;
+    const uint32_t key = valid ? (SMEM ? skeys[i] : float_key(sel_value<HALF_ABS>(v, i))) : 0u;
     const unsigned lt_mask = (1u << lane) - 1u;
     bool sel;
     if (EXACT) {
@@ -227,20 +235,35 @@ __global__ void __launch_bounds__(kThreads)
 
 }  // namespace
 
-cudaError_t launch_topk(bool exact, const float* v, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
-                        cudaStream_t stream) {
+namespace {
+
+template <bool HALF_ABS>
+cudaError_t launch_topk_impl(bool exact, const void* v, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
+                             cudaStream_t stream) {
   const bool smem = n <= kSmemKeysMax;
   const size_t bytes = smem ? (size_t)n * sizeof(uint32_t) : 0;
-  void (*kernel)(const float*, int, int, int32_t*, int32_t*);
+  void (*kernel)(const void*, int, int, int32_t*, int32_t*);
   if (exact)
-    kernel = smem ? topk_kernel<true, true> : topk_kernel<true, false>;
+    kernel = smem ? topk_kernel<true, true, HALF_ABS> : topk_kernel<true, false, HALF_ABS>;
   else
-    kernel = smem ? topk_kernel<false, true> : topk_kernel<false, false>;
+    kernel = smem ? topk_kernel<false, true, HALF_ABS> : topk_kernel<false, false, HALF_ABS>;
   if (bytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
   }
   return launch_ex(kernel, dim3(1), dim3(kThreads), bytes, stream, 1, false, v, (int)n, (int)k, out_idx, out_count);
+}
+
+}  // namespace
+
+cudaError_t launch_topk(bool exact, const float* v, int64_t n, int64_t k, int32_t* out_idx, int32_t* out_count,
+                        cudaStream_t stream) {
+  return launch_topk_impl<false>(exact, v, n, k, out_idx, out_count, stream);
+}
+
+cudaError_t launch_topk_abs_half(bool exact, const half* v, int64_t n, int64_t k, int32_t* out_idx,
+                                 int32_t* out_count, cudaStream_t stream) {
+  return launch_topk_impl<true>(exact, v, n, k, out_idx, out_count, stream);
 }
 
 cudaError_t launch_build_descriptors(const int32_t* sel, int64_t k, const int32_t* slot_of, int64_t I, int32_t* desc,

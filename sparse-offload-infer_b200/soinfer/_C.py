@@ -41,6 +41,7 @@ _SIGNATURES = {
     "soinfer_gemv_w4a16_rows": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w8a16": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "soinfer_topk_threshold_select": (_INT, [_P, _I64, _I64, _P, _P, _P]),
+    "soinfer_topk_threshold_select_abs_f16": (_INT, [_P, _I64, _I64, _P, _P, _P]),
     "soinfer_topk_select_exact": (_INT, [_P, _I64, _I64, _P, _P, _P]),
     "soinfer_build_dip_descriptors": (_INT, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
     "soinfer_gemv_dip_fused_up": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
@@ -61,6 +62,10 @@ _SIGNATURES = {
     "soinfer_kv_cache_append": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_decode_attention_workspace_bytes": (_I64, [_I64, _I64, _I64]),
     "soinfer_decode_attention": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _F32, _P]),
+    "soinfer_swiglu": (_INT, [_P, _P, _P, _P, _I64, _P]),
+    "soinfer_head_norm_rope": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P,
+                                      _F32, _P]),
     "soinfer_rope_apply_at": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
@@ -385,6 +390,21 @@ def topk_select_exact(abs_g, k: int):
     return _topk_impl("soinfer_topk_select_exact", "topk_select_exact", abs_g, k)
 
 
+def topk_threshold_select_abs_f16(gate, k: int):
+    """The reference selector on |gate| of an fp16 gate vector (no fp32 copy)."""
+    name = "topk_threshold_select_abs_f16"
+    _f16(gate, name + "(gate)")
+    _check(gate.dim() == 1 and gate.is_contiguous(), name, ": gate must be a contiguous 1D [I] tensor")
+    n = gate.size(0)
+    _check(1 <= k <= n, name, ": k must be in [1, I]")
+    dev = gate.device
+    idx = torch.empty(k, dtype=torch.int32, device=dev)
+    count = torch.empty(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _call("soinfer_topk_threshold_select_abs_f16", _ptr(gate), n, k, _ptr(idx), _ptr(count), _stream(dev))
+    return idx, count
+
+
 def build_dip_descriptors(selected_indices, slot_of):
     name = "build_dip_descriptors"
     _check(selected_indices.is_cuda and selected_indices.dtype == torch.int32 and selected_indices.dim() == 1
@@ -645,6 +665,74 @@ def kv_cache_append(k_cache, v_cache, k_new, v_new, pos: int) -> None:
 def _check_pos_dev(pos_dev, name):
     _check(pos_dev.is_cuda and pos_dev.dtype == torch.int32 and pos_dev.numel() == 1, name,
            "(pos_dev): must be a one-element int32 CUDA tensor")
+
+
+def add_rmsnorm(x, x2, weight, eps: float = 1e-6):
+    """(rmsnorm(fp16(x + x2)), fp16(x + x2)); x, x2: fp16 [rows, hidden]."""
+    name = "add_rmsnorm"
+    for t, n in ((x, "x"), (x2, "x2"), (weight, "weight")):
+        _f16(t, f"{name}({n})")
+    _check(x.dim() == 2 and x.is_contiguous() and x2.shape == x.shape and x2.is_contiguous(), name,
+           ": x and x2 must be contiguous 2D [rows, hidden] of the same shape")
+    _check(weight.dim() == 1 and weight.size(0) == x.size(1), name, ": weight shape must match x's hidden dim")
+    _check(x.size(1) % 2 == 0, name, ": hidden dim must be even")
+    dev = _same_device(x, x2, weight)
+    out, sum_out = torch.empty_like(x), torch.empty_like(x)
+    with torch.cuda.device(dev):
+        _call("soinfer_add_rmsnorm", _ptr(x), _ptr(x2), _ptr(weight), _ptr(out), _ptr(sum_out), x.size(0), x.size(1),
+              float(eps), _stream(dev))
+    return out, sum_out
+
+
+def swiglu(gate, up, idx=None) -> torch.Tensor:
+    """fp16(silu(float(gate[idx])) * float(up)); idx (int32) may be None (gate itself)."""
+    name = "swiglu"
+    _f16(gate, name + "(gate)")
+    _f16(up, name + "(up)")
+    _check(gate.is_contiguous() and up.is_contiguous() and up.dim() == 1 and gate.dim() == 1, name,
+           ": gate and up must be contiguous 1D tensors")
+    if idx is None:
+        _check(gate.numel() == up.numel(), name, ": gate and up must have the same length")
+    else:
+        _check_cuda(idx, name + "(idx)", torch.int32, ": must be int32")
+        _check(idx.numel() == up.numel(), name, ": idx and up must have the same length")
+    dev = _same_device(gate, up) if idx is None else _same_device(gate, up, idx)
+    out = torch.empty_like(up)
+    with torch.cuda.device(dev):
+        _call("soinfer_swiglu", _ptr(gate), _ptr(up), _ptr(idx), _ptr(out), up.numel(), _stream(dev))
+    return out
+
+
+def head_norm_rope(q, k, v, q_norm, k_norm, cos_vals, sin_vals, k_cache, v_cache, pos: int = 0, pos_dev=None,
+                   eps: float = 1e-6) -> None:
+    """Per-head RMSNorm + RoPE of q (in place) and k, then k / v appended to the
+    caches at pos (or *pos_dev with cos / sin tables [max_pos, head_dim/2])."""
+    name = "head_norm_rope"
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (q_norm, "q_norm"), (k_norm, "k_norm"), (k_cache, "k_cache"),
+                 (v_cache, "v_cache")):
+        _f16(t, f"{name}({n})")
+        _check(t.is_contiguous(), name, f"({n}): must be contiguous")
+    _check(q.dim() == 2 and k.dim() == 2 and v.shape == k.shape and k_cache.dim() == 3 and v_cache.shape == k_cache.shape,
+           name, ": q [NQ, hd], k / v [NKV, hd], caches [NKV, max_seq, hd]")
+    nq, hd = q.shape
+    nkv, max_seq, chd = k_cache.shape
+    _check(k.size(0) == nkv and k.size(1) == hd and chd == hd, name, ": head counts / head_dim disagree")
+    _check(q_norm.numel() == hd and k_norm.numel() == hd, name, ": q_norm / k_norm must be [head_dim]")
+    for t, n in ((cos_vals, "cos"), (sin_vals, "sin")):
+        _f32(t, f"{name}({n})")
+        _check(t.is_contiguous() and t.size(-1) == hd // 2, name, f"({n}): last dim must be head_dim / 2")
+    if pos_dev is None:
+        _check(0 <= pos < max_seq, name, ": pos out of range for max_seq_len")
+        table_rows = 1
+    else:
+        _check_pos_dev(pos_dev, name)
+        _check(cos_vals.dim() == 2, name, ": with pos_dev, cos / sin must be tables [max_pos, head_dim/2]")
+        table_rows = cos_vals.size(0)
+    dev = _same_device(q, k, v, k_cache)
+    with torch.cuda.device(dev):
+        _call("soinfer_head_norm_rope", _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm), _ptr(k_norm), _ptr(cos_vals),
+              _ptr(sin_vals), table_rows, _ptr(k_cache), _ptr(v_cache), nq, nkv, hd, max_seq, pos, _ptr(pos_dev),
+              float(eps), _stream(dev))
 
 
 def rope_apply_at(x, cos_table, sin_table, pos_dev) -> None:

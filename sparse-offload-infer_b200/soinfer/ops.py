@@ -191,3 +191,26 @@ def kv_cache_append_at(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torc
 def decode_attention_at(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos_dev: torch.Tensor) -> torch.Tensor:
     """B200 addition: decode_attention over [0, *pos_dev + 1), the length read on the device; graph-capturable."""
     return _C.decode_attention_at(q.contiguous(), k_cache, v_cache, pos_dev)
+
+
+# ------------------------------------------------------------------ B200 additions: fused decode glue
+def topk_threshold_select_abs(gate: torch.Tensor, k: int) -> torch.Tensor:
+    """B200 addition: topk_threshold_select(gate.float().abs(), k) on an fp16 gate, without the fp32 copy."""
+    return _C.topk_threshold_select_abs_f16(gate, k)[0]
+
+
+def add_rmsnorm(x: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6):
+    """B200 addition: (rmsnorm(x + x2), x + x2) in one kernel, bit-identical to the fp16 add then rmsnorm."""
+    return _C.add_rmsnorm(x, x2, weight, eps)
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor, idx: torch.Tensor | None = None) -> torch.Tensor:
+    """B200 addition: (F.silu(gate[idx].float()) * up.float()).half() in one kernel."""
+    return _C.swiglu(gate, up, idx)
+
+
+def head_norm_rope(q, k, v, q_norm, k_norm, cos_vals, sin_vals, k_cache, v_cache, pos: int = 0, pos_dev=None,
+                   eps: float = 1e-6) -> None:
+    """B200 addition: qk_norm of q and k, RoPE of both, q in place, k / v appended to the caches at pos (or the
+    device position pos_dev with cos / sin tables) -- one kernel for reference ops.py:238-250's sequence."""
+    _C.head_norm_rope(q, k, v, q_norm, k_norm, cos_vals, sin_vals, k_cache, v_cache, pos, pos_dev, eps)

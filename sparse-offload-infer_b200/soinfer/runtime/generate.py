@@ -151,8 +151,9 @@ class DevicePosition:
 
 def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
                      k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-    """rmsnorm -> q/k/v GEMVs -> q/k norm -> RoPE -> KV append -> GQA decode
-    attention -> o GEMV -> residual.  Returns (h2, h3 = post-attention rmsnorm(h2))."""
+    """rmsnorm -> q/k/v GEMVs -> q/k norm + RoPE + KV append (one kernel) ->
+    GQA decode attention -> o GEMV -> residual add + post-attention rmsnorm
+    (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2))."""
     NQ, NKV, HD = model.num_attention_heads, model.num_key_value_heads, model.head_dim
     eps = model.rms_norm_eps
     norms = model.layer_norms[layer_idx]
@@ -160,22 +161,18 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
     q = pipeline.next_gemv(h).view(NQ, HD)
     k = pipeline.next_gemv(h).view(NKV, HD)
     v = pipeline.next_gemv(h).view(NKV, HD)
-    q = ops.qk_norm(q, norms["q_norm"], eps)
-    k = ops.qk_norm(k, norms["k_norm"], eps)
     if isinstance(pos, DevicePosition):
-        q = ops.apply_rope_at(q, pos.cos_table, pos.sin_table, pos.pos)
-        k = ops.apply_rope_at(k, pos.cos_table, pos.sin_table, pos.pos)
-        ops.kv_cache_append_at(k_cache, v_cache, k, v, pos.pos)
+        ops.head_norm_rope(q, k, v, norms["q_norm"], norms["k_norm"], pos.cos_table, pos.sin_table, k_cache, v_cache,
+                           pos_dev=pos.pos, eps=eps)
         attn = ops.decode_attention_at(q, k_cache, v_cache, pos.pos).reshape(NQ * HD)
     else:
         cos_vals, sin_vals = ops.precompute_rope_cos_sin(HD, model.rope_theta, pos, device=x_flat.device)
-        q = ops.apply_rope(q, cos_vals, sin_vals)
-        k = ops.apply_rope(k, cos_vals, sin_vals)
-        ops.kv_cache_append(k_cache, v_cache, k, v, pos)
+        ops.head_norm_rope(q, k, v, norms["q_norm"], norms["k_norm"], cos_vals, sin_vals, k_cache, v_cache, pos=pos,
+                           eps=eps)
         attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
-    h2 = x_flat + pipeline.next_gemv(attn)
-    h3 = ops.rmsnorm(h2.unsqueeze(0), norms["post_attention_layernorm"], eps).squeeze(0)
-    return h2, h3
+    o = pipeline.next_gemv(attn)
+    h3, h2 = ops.add_rmsnorm(x_flat.unsqueeze(0), o.unsqueeze(0), norms["post_attention_layernorm"], eps)
+    return h2.squeeze(0), h3.squeeze(0)
 
 
 def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
@@ -185,8 +182,7 @@ def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel,
     h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     gate = pipeline.next_gemv(h3)
     up = pipeline.next_gemv(h3)
-    mlp_h = (F.silu(gate.float()) * up.float()).half()
-    return h2 + pipeline.next_gemv(mlp_h)
+    return h2 + pipeline.next_gemv(ops.swiglu(gate, up))
 
 
 # --------------------------------------------------------------------- DIP
@@ -218,8 +214,8 @@ class DipBuffers:
 
 
 def _select(gate: torch.Tensor, dip_k: int) -> torch.Tensor:
-    """The reference's DIP selector on |gate| (fp32): int32 [dip_k] ascending channel indices."""
-    return ops.topk_threshold_select(gate.float().abs(), dip_k)
+    """The reference's DIP selector on |gate| (fp32 |float(g)|): int32 [dip_k] ascending channel indices."""
+    return ops.topk_threshold_select_abs(gate, dip_k)
 
 
 def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor,
@@ -234,7 +230,9 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
     h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     gate = pipeline.next_gemv(h3)
     idx = _select(gate, dip_k)
-    idx_long = idx.long()
+    idx_long = idx.long() if (channel_counts is not None or selected_out is not None
+                              or not model.is_resident(model.matrix(layer_idx, "mlp.up_proj.weight").handle.name)
+                              or not model.is_resident(model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX).handle.name)) else None
     if channel_counts is not None:
         channel_counts[layer_idx].scatter_add_(0, idx_long, torch.ones_like(idx_long))
     if selected_out is not None:
@@ -248,7 +246,7 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
         rows = bufs.up_rows(dip_k)
         ops.gather_rows_device(model.weight_source(up), idx, rows)
         u_sel = ops.gemv_w4a16_group_lop3(rows, up.scale.index_select(0, idx_long), h3, up.packed_k, g)
-    h_sel = (F.silu(gate.index_select(0, idx_long).float()) * u_sel.float()).half()
+    h_sel = ops.swiglu(gate, u_sel, idx)
     if model.is_resident(down_t.handle.name):
         down = ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, idx, h_sel,
                                           model.hidden_size, g)
@@ -288,7 +286,7 @@ def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel
         miss_bytes[layer_idx] += mc * (bufs.up_row_nbytes + bufs.down_row_nbytes)
     u_sel = ops.gemv_dip_fused_up(cache.up_Wq, cache.up_scale, up_rows, up.scale.index_select(0, miss_long), desc,
                                   h3, up.packed_k, g)
-    h_sel = (F.silu(gate.index_select(0, idx.long()).float()) * u_sel.float()).half()
+    h_sel = ops.swiglu(gate, u_sel, idx)
     down = ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows,
                                    down_t.scale.index_select(0, miss_long), desc, h_sel, model.hidden_size, g)
     return h2 + down
