@@ -100,6 +100,15 @@ typedef struct soinfer_gemv_task {
   soinfer_half* y;
   int64_t N, K, group_size, num_groups;
   int64_t dep;
+  /* Optional epilogue (NULL = off), applied to d = fp16(dot) in this order:
+   * glu_gate: d = fp16(silu(float(glu_gate[n])) * float(d))  (SwiGLU: y = the
+   *   MLP hidden state when this task is up_proj and glu_gate gate_proj's y);
+   * residual: d = fp16(float(residual[n]) + float(d))  (the residual add).
+   * Each equals the unfused op on the fp16 GEMV output.  A glu_gate /
+   * residual buffer is either ready before the launch or the y of an earlier
+   * task of the batch with the same N. */
+  const soinfer_half* residual;
+  const soinfer_half* glu_gate;
 } soinfer_gemv_task;
 
 /* Bytes of zero-initialised device workspace soinfer_gemv_w4a16_batch needs

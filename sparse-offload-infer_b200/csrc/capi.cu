@@ -112,6 +112,10 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
     REQUIRE(t.N >= 1, "%s: N must be >= 1", tn);
     REQUIRE(t.Wq && t.scale && t.x && t.y, "%s: null pointer", tn);
     REQUIRE(t.dep >= -1 && t.dep < i, "%s: dep must be -1 or an earlier task index", tn);
+    for (int64_t j = 0; j < i; ++j) {  // an epilogue input made in this batch must share the row split
+      if (tasks[j].y == t.glu_gate || tasks[j].y == t.residual)
+        REQUIRE(tasks[j].N == t.N, "%s: glu_gate / residual is task %lld's y but N differs", tn, (long long)j);
+    }
     fast = fast && t.K % 128 == 0 && t.group_size % 128 == 0 && t.num_groups % 4 == 0 && aligned(t.Wq, 16) &&
            aligned(t.scale, 16) && aligned(t.x, 16) && t.N < (1 << 30) && t.K < (1 << 30);
   }
@@ -133,6 +137,8 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
       d.G = (int)t.num_groups;
       d.cpg = (int)(t.group_size / 128);
       d.dep = (int)t.dep;
+      d.resid = as_half(t.residual);
+      d.glu = as_half(t.glu_gate);
     }
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -154,6 +160,12 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
     if (int rc = cuda_result(launch_gemv_w4(RowMode::kPlain, src, as_half(t.x), as_half(t.y), t.N, t.K, t.group_size, st),
                              name))
       return rc;
+    if (t.glu_gate)
+      if (int rc = cuda_result(launch_swiglu(as_half(t.glu_gate), as_half(t.y), nullptr, as_half(t.y), t.N, st), name))
+        return rc;
+    if (t.residual)
+      if (int rc = cuda_result(launch_add_half(as_half(t.residual), as_half(t.y), as_half(t.y), t.N, st), name))
+        return rc;
   }
   return SOINFER_OK;
 }

@@ -407,7 +407,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < kRedRows / 32; ++i) {
           const int r = lane + 32 * i;
-          if (r < v.rows) tk.y[v.row0 + r] = __float2half_rn(sums[i]);
+          if (r < v.rows) {
+            // optional epilogues; a glu / resid row written by an earlier task of
+            // this batch was stored by this same lane (same N, same row split)
+            half hv = __float2half_rn(sums[i]);
+            if (tk.glu) {
+              const float gv = __half2float(__ldcg(tk.glu + v.row0 + r));
+              hv = __float2half_rn((gv / (1.0f + expf(-gv))) * __half2float(hv));
+            }
+            if (tk.resid) hv = __float2half_rn(__half2float(__ldcg(tk.resid + v.row0 + r)) + __half2float(hv));
+            tk.y[v.row0 + r] = hv;
+          }
         }
         ++a;
       }

@@ -74,6 +74,14 @@ __global__ void swiglu_kernel(const half* __restrict__ gate, const half* __restr
   }
 }
 
+__global__ void add_half_kernel(const half* __restrict__ a, const half* __restrict__ b, half* __restrict__ out,
+                                const int64_t n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(__half2float(a[i]) + __half2float(b[i]));
+}
+
 // After the q / k / v GEMVs of one decode token (rows: q heads, then k heads,
 // then v heads; one warp per row): q and k rows get RMSNorm over the head
 // (fp32 sum of squares, out = fp16((x * rsqrt(mean + eps)) * w)) followed by
@@ -222,6 +230,14 @@ cudaError_t launch_swiglu(const half* gate, const half* up, const int32_t* idx, 
   if (blocks > 1184) blocks = 1184;
   if (blocks < 1) blocks = 1;
   return launch_ex(swiglu_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, false, gate, up, idx, out, n);
+}
+
+cudaError_t launch_add_half(const half* a, const half* b, half* out, int64_t n, cudaStream_t stream) {
+  const int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  if (blocks > 1184) blocks = 1184;
+  if (blocks < 1) blocks = 1;
+  return launch_ex(add_half_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, false, a, b, out, n);
 }
 
 cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const half* qw, const half* kw,

@@ -43,6 +43,8 @@ struct GemvBatchTask {
   half* y;
   int N, K, G, cpg, dep;
   int rows_per_cta, tiles_per_item, publish;  // filled by plan_gemv_batch (publish: a later task depends on it)
+  const half* resid;  // optional epilogue: y = fp16(resid + fp16(dot))
+  const half* glu;    // optional epilogue: y = fp16(silu(glu) * fp16(dot)), applied before resid
 };
 constexpr int kMaxBatchTasks = 256;
 struct GemvBatchParams {
@@ -102,6 +104,8 @@ cudaError_t launch_add_rmsnorm(const half* x, const half* x2, const half* w, hal
                                int64_t hidden, float eps, cudaStream_t stream);
 cudaError_t launch_swiglu(const half* gate, const half* up, const int32_t* idx, half* out, int64_t n,
                           cudaStream_t stream);
+// out = fp16(float(a) + float(b)) elementwise (the fp16 tensor add).
+cudaError_t launch_add_half(const half* a, const half* b, half* out, int64_t n, cudaStream_t stream);
 cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const half* qw, const half* kw,
                                   const float* cv, const float* sv, half* kc, half* vc, int64_t nq, int64_t nkv,
                                   int64_t hd, int64_t max_seq, int64_t pos, const int32_t* pos_dev,

@@ -262,7 +262,7 @@ def gemv_fp16_argmax(W, x, logits: bool = False, out_idx=None):
 
 class _GemvTask(ctypes.Structure):
     _fields_ = [("Wq", _P), ("scale", _P), ("x", _P), ("y", _P), ("N", _I64), ("K", _I64), ("group_size", _I64),
-                ("num_groups", _I64), ("dep", _I64)]
+                ("num_groups", _I64), ("dep", _I64), ("residual", _P), ("glu_gate", _P)]
 
 
 MAX_BATCH_TASKS = 256
@@ -271,16 +271,21 @@ MAX_BATCH_TASKS = 256
 class GemvBatch:
     """A prepared list of INT4 GEMVs run as one persistent kernel
     (soinfer_gemv_w4a16_batch).  tasks: sequence of
-    (Wq_packed, scale, x, y, K, group_size, dep) with dep = index of an
-    earlier task whose output feeds this task's x, or -1.  The tensors must
-    stay alive and keep their storage while the batch is used."""
+    (Wq_packed, scale, x, y, K, group_size, dep[, residual[, glu_gate]]) with
+    dep = index of an earlier task whose output feeds this task's x, or -1;
+    residual / glu_gate (fp16 [N] or None) add the epilogues
+    y = residual + fp16(silu(glu_gate) * fp16(W x)) of the C ABI.  The tensors
+    must stay alive and keep their storage while the batch is used."""
 
     def __init__(self, tasks):
         n = len(tasks)
         _check(0 < n <= MAX_BATCH_TASKS, "gemv_w4a16_batch: 1 ..", MAX_BATCH_TASKS, " tasks")
         arr = (_GemvTask * n)()
         dev = None
-        for i, (W, scale, x, y, K, group_size, dep) in enumerate(tasks):
+        for i, task in enumerate(tasks):
+            W, scale, x, y, K, group_size, dep = task[:7]
+            residual = task[7] if len(task) > 7 else None
+            glu = task[8] if len(task) > 8 else None
             name = f"gemv_w4a16_batch[task {i}]"
             _check(W.is_cuda and W.dtype == torch.uint8 and W.is_contiguous() and W.dim() == 2, name,
                    "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
@@ -292,13 +297,17 @@ class GemvBatch:
             _f16(y, name + "(y)")
             _check(y.numel() == W.size(0), name, ": y must hold N values")
             _check(-1 <= dep < i, name, ": dep must be -1 or an earlier task index")
+            for e, en in ((residual, "residual"), (glu, "glu_gate")):
+                if e is not None:
+                    _f16(e, f"{name}({en})")
+                    _check(e.numel() == W.size(0) and e.is_contiguous(), name, f": {en} must hold N values")
             d = _same_device(W, scale, x, y)
             _check(dev is None or d == dev, name, ": all tasks must be on one device")
             dev = d
             arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), y.data_ptr(), W.size(0), K, group_size,
-                               scale.size(1), dep)
+                               scale.size(1), dep, _ptr(residual), _ptr(glu))
         self._arr, self.n, self.device = arr, n, dev
-        self._keep = [t[:4] for t in tasks]
+        self._keep = [tuple(t) for t in tasks]
 
     def run(self) -> None:
         dev = self.device

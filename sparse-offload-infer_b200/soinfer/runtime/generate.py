@@ -18,13 +18,12 @@ reference's one sync per layer (the miss count sizes the staging rows).
 """
 from __future__ import annotations
 
-import itertools
 from dataclasses import dataclass, field
 
 import torch
 import torch.nn.functional as F
 
-from .. import ops
+from .. import _C, ops
 from ..offload.hot_cache import HotCache
 from ..offload.load_hf_checkpoint import DOWN_PROJ_T_SUFFIX, LINEAR_SUFFIXES, LoadedMatrix
 from ..offload.stream_manager import StreamManager
@@ -64,6 +63,7 @@ class StreamingModel:
     rope_theta: float
     group_size: int = 128
     resident: dict[str, torch.Tensor] | None = None
+    batch_gemvs: bool = True  # resident GEMVs sharing an input run as one batched launch
     stream_manager: StreamManager = field(init=False)
 
     def __post_init__(self) -> None:
@@ -103,10 +103,15 @@ class WeightPipeline:
         if streamed:
             max_bytes = max(model.matrices[n].n * model.matrices[n].handle.row_nbytes for n in streamed)
             self.bufs = [torch.empty(max_bytes, dtype=torch.uint8, device=model.device) for _ in range(2)]
-        self._names = itertools.cycle(seq)
+        self._seq = seq
+        self._i = 0  # index of the weight in flight
         self.cur_buf = 0
-        self.cur_name = next(self._names)
+        self.cur_name = seq[0]
         self._prefetch_into(self.cur_buf, self.cur_name)
+
+    def _advance(self) -> str:
+        self._i = (self._i + 1) % len(self._seq)
+        return self._seq[self._i]
 
     def _view(self, buf_idx: int, m: LoadedMatrix) -> torch.Tensor:
         nbytes = m.n * m.handle.row_nbytes
@@ -130,10 +135,50 @@ class WeightPipeline:
                                           self.model.group_size)
             self.sm.mark_read_done(self.cur_buf)
         nxt = 1 - self.cur_buf
-        name_next = next(self._names)
+        name_next = self._advance()
         self._prefetch_into(nxt, name_next)
         self.cur_buf, self.cur_name = nxt, name_next
         return y
+
+    def next_gemvs(self, x_in: torch.Tensor, count: int) -> list[torch.Tensor]:
+        """The next `count` GEMVs, all on the same input.  When they are all
+        HBM-resident they run as one persistent batched launch (one kernel for
+        q / k / v or gate / up); otherwise one after another."""
+        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(count)]
+        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+            tasks = []
+            for name in names:
+                m = self.model.matrices[name]
+                y = torch.empty(m.n, dtype=torch.float16, device=x_in.device)
+                tasks.append((self.model.resident[name], m.scale, x_in, y, m.packed_k, self.model.group_size, -1))
+            for _ in range(count):
+                self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
+            _C.gemv_w4a16_batch(tasks)
+            return [t[3] for t in tasks]
+        return [self.next_gemv(x_in) for _ in range(count)]
+
+    def next_mlp(self, h3: torch.Tensor, h2: torch.Tensor) -> torch.Tensor:
+        """The next gate / up / down weights as a dense SwiGLU MLP plus the
+        residual: h2 + down(fp16(silu(gate(h3)) * up(h3))).  Resident weights:
+        one persistent launch (up's epilogue applies SwiGLU, down depends on up
+        and adds the residual); otherwise three GEMVs, swiglu and an add."""
+        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(3)]
+        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+            mg, mu, md = (self.model.matrices[n] for n in names)
+            res, g = self.model.resident, self.model.group_size
+            dev = h3.device
+            gate = torch.empty(mg.n, dtype=torch.float16, device=dev)
+            hidden = torch.empty(mu.n, dtype=torch.float16, device=dev)
+            out = torch.empty(md.n, dtype=torch.float16, device=dev)
+            tasks = [(res[names[0]], mg.scale, h3, gate, mg.packed_k, g, -1),
+                     (res[names[1]], mu.scale, h3, hidden, mu.packed_k, g, -1, None, gate),
+                     (res[names[2]], md.scale, hidden, out, md.packed_k, g, 1, h2)]
+            for _ in range(3):
+                self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
+            _C.gemv_w4a16_batch(tasks)
+            return out
+        gate, up = self.next_gemvs(h3, 2)
+        return h2 + self.next_gemv(ops.swiglu(gate, up))
 
 
 # --------------------------------------------------------------- attention
@@ -158,9 +203,8 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
     eps = model.rms_norm_eps
     norms = model.layer_norms[layer_idx]
     h = ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
-    q = pipeline.next_gemv(h).view(NQ, HD)
-    k = pipeline.next_gemv(h).view(NKV, HD)
-    v = pipeline.next_gemv(h).view(NKV, HD)
+    q, k, v = pipeline.next_gemvs(h, 3)
+    q, k, v = q.view(NQ, HD), k.view(NKV, HD), v.view(NKV, HD)
     if isinstance(pos, DevicePosition):
         ops.head_norm_rope(q, k, v, norms["q_norm"], norms["k_norm"], pos.cos_table, pos.sin_table, k_cache, v_cache,
                            pos_dev=pos.pos, eps=eps)
@@ -180,9 +224,7 @@ def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel,
                                 v_cache: torch.Tensor) -> torch.Tensor:
     """Dense layer: all 7 linear weights through the pipeline (reference generate.py:141-182)."""
     h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
-    gate = pipeline.next_gemv(h3)
-    up = pipeline.next_gemv(h3)
-    return h2 + pipeline.next_gemv(ops.swiglu(gate, up))
+    return pipeline.next_mlp(h3, h2)
 
 
 # --------------------------------------------------------------------- DIP

@@ -112,3 +112,32 @@ def test_batch_rejects_bad_tasks():
         _C.gemv_w4a16_batch([(Wd, sd[:, :1].contiguous(), x, y, 256, 128, -1)])
     with pytest.raises(RuntimeError):
         _C.gemv_w4a16_batch([])
+
+
+def test_glu_and_residual_epilogues_equal_unfused():
+    H, I = 2048, 6144
+    gw, uw, dw = int4_weights(I, H, 128, seed=41), int4_weights(I, H, 128, seed=42), int4_weights(H, I, 128, seed=43)
+    h3 = fp16_randn(H, 44).to(DEV)
+    h2 = fp16_randn(H, 45).to(DEV)
+    gate = torch.empty(I, dtype=torch.float16, device=DEV)
+    hidden = torch.empty(I, dtype=torch.float16, device=DEV)
+    out = torch.empty(H, dtype=torch.float16, device=DEV)
+    up_plain = torch.empty(I, dtype=torch.float16, device=DEV)
+    down_plain = torch.empty(H, dtype=torch.float16, device=DEV)
+    G = [(w[0].to(DEV), w[1].to(DEV)) for w in (gw, uw, dw)]
+    _C.gemv_w4a16_batch([(G[0][0], G[0][1], h3, gate, H, 128, -1),
+                         (G[1][0], G[1][1], h3, hidden, H, 128, -1, None, gate),
+                         (G[2][0], G[2][1], hidden, out, I, 128, 1, h2)])
+    _C.gemv_w4a16_batch([(G[1][0], G[1][1], h3, up_plain, H, 128, -1)])
+    assert torch.equal(hidden, ops.swiglu(gate, up_plain))
+    _C.gemv_w4a16_batch([(G[2][0], G[2][1], hidden, down_plain, I, 128, -1)])
+    assert torch.equal(out, h2 + down_plain)
+    # the per-task fallback (K not a multiple of 128) applies the same epilogues
+    p, s, pk = int4_weights(100, 200, 8, seed=46)
+    x = fp16_randn(pk, 47).to(DEV)
+    r = fp16_randn(100, 48).to(DEV)
+    gv = fp16_randn(100, 49).to(DEV)
+    y = torch.empty(100, dtype=torch.float16, device=DEV)
+    _C.gemv_w4a16_batch([(p.to(DEV), s.to(DEV), x, y, pk, 8, -1, r, gv)])
+    plain = ops.gemv_w4a16_group_lop3(p.to(DEV), s.to(DEV), x, pk, 8)
+    assert torch.equal(y, r + ops.swiglu(gv, plain))
