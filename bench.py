@@ -328,6 +328,8 @@ def run_ours(args) -> None:
 
     # ---- e2e through the public streaming API (weights from the pinned arena)
     e2e = run_e2e(args, layers, device, world, dist)
+    del layers
+    decode = run_decode(args, device) if args.decode else None
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -355,6 +357,7 @@ def run_ours(args) -> None:
                    "l2": "inputs larger than L2 (weights far above the 126 MB L2), no flush",
                    "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "steps": csteps,
                                          "note": "each down_proj reads its gate_proj output (in-kernel dependency)"},
+                   "decode": decode,
                    "parallelism": f"{world} independent replicas (no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -423,16 +426,46 @@ def run_e2e(args, layers, device, world, dist) -> dict:
             "path": "soinfer.runtime.generate.WeightPipeline (copy-engine double buffering from the pinned arena)"}
 
 
+def run_decode(args, device) -> dict:
+    """batch-1 greedy decode of the Qwen3-1.7B-shaped INT4 model
+    (random-init weights resident in HBM), 70 random prompt tokens then
+    args.decode_tokens new tokens, one CUDA graph per token; dense and DIP
+    k/I = 0.5.  tok/s counts the generating replays only (prompt timed apart)."""
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import QWEN3_1_7B, synthetic_streaming_model
+
+    model = synthetic_streaming_model(QWEN3_1_7B, seed=1, resident=True, offload=False, device=device)
+    prompt = torch.randint(0, QWEN3_1_7B.vocab_size, (70,), generator=torch.Generator().manual_seed(0)).tolist()
+    out = {"model": "Qwen3-1.7B-shaped: 28 layers, hidden 2048, intermediate 6144, 16 q / 8 kv heads, head_dim 128, "
+                    "vocab 151936; INT4 g128 random-init weights resident in HBM",
+           "prompt_tokens": len(prompt), "new_tokens": args.decode_tokens, "max_seq_len": 2048,
+           "step": "one CUDA graph per token (soinfer.runtime.generate.GraphDecoder)"}
+    for name, dip_k in (("dense", None), ("dip_k3072", 3072)):
+        gd = gen.GraphDecoder(model, dip_k=dip_k, max_seq_len=2048)
+        gd.generate(prompt, 4)  # capture + warm-up
+        tm = {}
+        gd.generate(prompt, args.decode_tokens, timings=tm)
+        n = args.decode_tokens - 1
+        out[name] = {"tok_s": round(n / (tm["decode_ms"] / 1e3), 1), "ms_per_token": round(tm["decode_ms"] / n, 4),
+                     "prefill_ms": round(tm["prefill_ms"], 2)}
+        del gd
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=64)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", type=int, default=1, help="also measure configs[3] decode tok/s (reported in config)")
+    ap.add_argument("--decode-tokens", type=int, default=128)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
