@@ -329,7 +329,8 @@ def run_ours(args) -> None:
     # ---- e2e through the public streaming API (weights from the pinned arena)
     e2e = run_e2e(args, layers, device, world, dist)
     del layers
-    decode = run_decode(args, device) if args.decode else None
+    decode = run_decode(args, device) if args.decode and rank == 0 and world == 1 else None
+    decode_tp = run_decode_tp(args, device, world, rank, dist) if args.tp_decode else None
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -358,6 +359,7 @@ def run_ours(args) -> None:
                    "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "steps": csteps,
                                          "note": "each down_proj reads its gate_proj output (in-kernel dependency)"},
                    "decode": decode,
+                   "decode_14b_tp": decode_tp,
                    "parallelism": f"{world} independent replicas (no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -454,6 +456,71 @@ def run_decode(args, device) -> dict:
     return out
 
 
+def run_decode_tp(args, device, world, rank, dist) -> dict:
+    """batch-1 greedy decode of the Qwen3-14B-shaped INT4 model,
+    tensor-parallel over the `world` GPUs (one process each; q/k/v/gate/up
+    split by output rows, o/down by input columns with one NCCL all-reduce
+    after each, vocabulary-parallel LM head); world 1 runs the unsharded
+    model.  A random prompt of args.tp_prompt tokens fills the KV cache, then
+    args.tp_tokens tokens are generated, one CUDA graph per token (collectives
+    captured in it).  ms/token is the max over ranks of the CUDA-event time."""
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import QWEN3_14B, synthetic_streaming_model
+    from soinfer.runtime.tp import ShardPlan, build_tp_model, graph_decoder_tp
+
+    arch = QWEN3_14B
+    max_seq = 4096
+    n_prompt, n_new = args.tp_prompt, args.tp_tokens
+    if n_prompt + n_new > max_seq:
+        raise ValueError("tp prompt + tokens must fit the 4096 context")
+    if world == 1:
+        model = synthetic_streaming_model(arch, seed=2, resident=True, offload=False, include_dip=False,
+                                          device=device)
+        gd = gen.GraphDecoder(model, max_seq_len=max_seq)
+    else:
+        plan = ShardPlan(rank, world, arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim,
+                         arch.hidden_size, arch.intermediate_size, arch.vocab_size)
+        model = build_tp_model(arch, plan, seed=2, device=device)
+        gd = graph_decoder_tp(model, plan, max_seq_len=max_seq)
+    weight_bytes = sum(t.numel() for t in model.resident.values()) + sum(
+        m.scale.numel() * m.scale.element_size() for m in model.matrices.values())
+    prompt = torch.randint(0, arch.vocab_size, (n_prompt,), generator=torch.Generator().manual_seed(1)).tolist()
+    gd.generate(prompt[:8], 4)  # capture + warm-up
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    tm = {}
+    ids = gd.generate(prompt, n_new, timings=tm)
+    t = torch.tensor([tm["decode_ms"], tm["prefill_ms"]], dtype=torch.float64, device=device)
+    same = torch.tensor(ids[-n_new:], dtype=torch.int64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ref = same.clone()
+        dist.broadcast(ref, 0)
+        agree = bool(torch.equal(ref, same))
+    else:
+        agree = True
+    decode_ms, prefill_ms = (float(v) for v in t.tolist())
+    del gd, model
+    torch.cuda.empty_cache()
+    n = n_new - 1
+    ms_tok = decode_ms / n
+    # per-token HBM floor of one rank: its weight shard + LM-head shard + KV read at the mean context
+    kv_per_pos = 2 * (arch.num_key_value_heads // world) * arch.head_dim * 2 * arch.num_layers
+    mean_ctx = n_prompt + n_new / 2
+    lm_bytes = -(-arch.vocab_size // world) * arch.hidden_size * 2
+    rank_bytes = weight_bytes + lm_bytes + kv_per_pos * mean_ctx
+    return {"model": "Qwen3-14B-shaped: 40 layers, hidden 5120, intermediate 17408, 40 q / 8 kv heads, head_dim 128, "
+                     "vocab 151936; INT4 g128 random-init weights resident in HBM",
+            "tp": world, "prompt_tokens": n_prompt, "new_tokens": n_new, "max_seq_len": max_seq,
+            "tok_s": round(n / (decode_ms / 1e3), 1), "ms_per_token": round(ms_tok, 4),
+            "prefill_ms": round(prefill_ms, 1), "tokens_agree_across_ranks": agree,
+            "hbm_bytes_per_token_per_rank": int(rank_bytes),
+            "hbm_floor_ms": round(rank_bytes / (measured_peaks().get("hbm_gbs") or 6650.0) / 1e6, 4),
+            "collectives_per_token": 2 * arch.num_layers + 1,
+            "step": "one CUDA graph per token; fp32 all-reduce of the o / down partials (NCCL over NVLink)"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,6 +533,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode", type=int, default=1, help="also measure configs[3] decode tok/s (reported in config)")
     ap.add_argument("--decode-tokens", type=int, default=128)
+    ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
+    ap.add_argument("--tp-prompt", type=int, default=3840)
+    ap.add_argument("--tp-tokens", type=int, default=256)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

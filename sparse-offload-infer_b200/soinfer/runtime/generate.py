@@ -157,6 +157,23 @@ class WeightPipeline:
             return [t[3] for t in tasks]
         return [self.next_gemv(x_in) for _ in range(count)]
 
+    def next_glu(self, h3: torch.Tensor) -> torch.Tensor:
+        """The next gate / up weights as fp16(silu(gate(h3)) * up(h3)): one batched
+        launch with the SwiGLU epilogue when resident, else two GEMVs and swiglu."""
+        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(2)]
+        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+            mg, mu = (self.model.matrices[n] for n in names)
+            res, g = self.model.resident, self.model.group_size
+            gate = torch.empty(mg.n, dtype=torch.float16, device=h3.device)
+            hidden = torch.empty(mu.n, dtype=torch.float16, device=h3.device)
+            for _ in range(2):
+                self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
+            _C.gemv_w4a16_batch([(res[names[0]], mg.scale, h3, gate, mg.packed_k, g, -1),
+                                 (res[names[1]], mu.scale, h3, hidden, mu.packed_k, g, -1, None, gate)])
+            return hidden
+        gate, up = self.next_gemvs(h3, 2)
+        return ops.swiglu(gate, up)
+
     def next_mlp(self, h3: torch.Tensor, h2: torch.Tensor) -> torch.Tensor:
         """The next gate / up / down weights as a dense SwiGLU MLP plus the
         residual: h2 + down(fp16(silu(gate(h3)) * up(h3))).  Resident weights:
@@ -195,10 +212,13 @@ class DevicePosition:
 
 
 def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
-                     k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+                     k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     reduce_o=None) -> tuple[torch.Tensor, torch.Tensor]:
     """rmsnorm -> q/k/v GEMVs -> q/k norm + RoPE + KV append (one kernel) ->
     GQA decode attention -> o GEMV -> residual add + post-attention rmsnorm
-    (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2))."""
+    (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2)).  reduce_o maps the
+    o GEMV output before the residual (the cross-rank sum of row-parallel
+    partials under tensor parallelism)."""
     NQ, NKV, HD = model.num_attention_heads, model.num_key_value_heads, model.head_dim
     eps = model.rms_norm_eps
     norms = model.layer_norms[layer_idx]
@@ -215,6 +235,8 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
                            eps=eps)
         attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
     o = pipeline.next_gemv(attn)
+    if reduce_o is not None:
+        o = reduce_o(o)
     h3, h2 = ops.add_rmsnorm(x_flat.unsqueeze(0), o.unsqueeze(0), norms["post_attention_layernorm"], eps)
     return h2.squeeze(0), h3.squeeze(0)
 
@@ -357,8 +379,12 @@ def _kv_caches(model: StreamingModel, max_seq_len: int):
             [torch.zeros(shape, dtype=torch.float16, device=dev) for _ in range(model.num_layers)])
 
 
+def _next_token(model: StreamingModel, xn: torch.Tensor) -> torch.Tensor:
+    return ops.lm_head_argmax(model.lm_head, xn)
+
+
 def _greedy(model: StreamingModel, prompt_ids: list[int], n_new: int, run_layer, eos_token_id: int | None,
-            max_seq_len: int) -> list[int]:
+            max_seq_len: int, token_fn=None) -> list[int]:
     """Prefill the prompt one token at a time, then greedy-decode n_new tokens.
     run_layer(layer_idx, x, pos, k_cache, v_cache) -> x.  Token ids stay on
     the device until the end (a host sync per token only with an EOS id)."""
@@ -379,7 +405,7 @@ def _greedy(model: StreamingModel, prompt_ids: list[int], n_new: int, run_layer,
     pos = len(prompt_ids)
     for _ in range(n_new):
         xn = ops.rmsnorm(x.unsqueeze(0), model.final_norm, model.rms_norm_eps).squeeze(0)
-        idx = ops.lm_head_argmax(model.lm_head, xn)  # int32 [1] on the device
+        idx = (token_fn or _next_token)(model, xn)  # int32 [1] on the device
         new_ids.append(idx)
         if eos_token_id is not None and int(idx.item()) == eos_token_id:
             break
@@ -433,7 +459,11 @@ class GraphDecoder:
     between.  Weights must be HBM-resident.  Tokens equal generate_streaming /
     generate_dip on the same model (same kernels, same order)."""
 
-    def __init__(self, model: StreamingModel, dip_k: int | None = None, max_seq_len: int = 2048):
+    def __init__(self, model: StreamingModel, dip_k: int | None = None, max_seq_len: int = 2048, layer_fn=None,
+                 token_fn=None):
+        """layer_fn(pipeline, model, layer_idx, x, where, k_cache, v_cache) -> x and
+        token_fn(model, xn) -> int32 [1] replace the dense / DIP layer and the
+        fused LM-head argmax (tensor parallelism plugs in here)."""
         names = [f"model.layers.{i}.{s}" for i in range(model.num_layers) for s in LINEAR_SUFFIXES]
         if dip_k is not None:
             names.append(f"model.layers.0.{DOWN_PROJ_T_SUFFIX}")
@@ -452,18 +482,21 @@ class GraphDecoder:
         self.pipeline = WeightPipeline(model, suffixes=suffixes)
         self.bufs = DipBuffers.make(model, dip_k) if dip_k is not None else None
         self.graph = None
+        self.layer_fn, self.token_fn = layer_fn, token_fn or _next_token
 
     def _step(self) -> None:
         m, where = self.model, self.where
         x = m.embed_tokens.index_select(0, self.ids.index_select(0, self.pos.long()).long()).view(-1)
         for li in range(m.num_layers):
-            if self.dip_k is None:
+            if self.layer_fn is not None:
+                x = self.layer_fn(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
+            elif self.dip_k is None:
                 x = run_decoder_layer_streaming(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
             else:
                 x = run_decoder_layer_dip(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li],
                                           self.dip_k, self.bufs)
         xn = ops.rmsnorm(x.unsqueeze(0), m.final_norm, m.rms_norm_eps).squeeze(0)
-        nxt = ops.lm_head_argmax(m.lm_head, xn)
+        nxt = self.token_fn(m, xn)
         at = (self.pos + 1).long()
         keep = (self.pos + 1) < self.prompt_len  # still inside the prompt: keep its token
         self.ids.index_copy_(0, at, torch.where(keep, self.ids.index_select(0, at), nxt))

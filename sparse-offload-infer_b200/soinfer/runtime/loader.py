@@ -19,7 +19,7 @@ import torch
 
 from ..offload.load_hf_checkpoint import (DOWN_PROJ_T_SUFFIX, LINEAR_SUFFIXES, LoadedMatrix, packed_int4_bytes,
                                           quantize_and_pack, stream_load_layers)
-from ..offload.weight_store import PinnedWeightStore
+from ..offload.weight_store import PinnedWeightStore, WeightHandle
 from ..quant import formats, pack
 from .generate import StreamingModel
 
@@ -97,6 +97,42 @@ def _linear_shapes(arch: Architecture) -> dict[str, tuple[int, int]]:
     }
 
 
+def synthetic_weights(arch: Architecture, seed: int, group_size: int, include_dip: bool, std: float, device):
+    """Yields (layer, suffix, packed uint8 CUDA, scale fp32 CUDA, packed_k, n, k) for every decoder
+    linear weight in load order -- the seeded random-init matrices quantized to group-wise INT4 (the
+    transposed down_proj right after its down_proj) -- then returns the generator for the embeddings."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    shapes = _linear_shapes(arch)
+    for layer in range(arch.num_layers):
+        for suffix in LINEAR_SUFFIXES:
+            n, k = shapes[suffix]
+            w = torch.randn(n, k, generator=gen, device=device) * std
+            yield _quantized(layer, suffix, w, group_size)
+            if include_dip and suffix == "mlp.down_proj.weight":
+                yield _quantized(layer, DOWN_PROJ_T_SUFFIX, w.t().contiguous(), group_size)
+            del w
+    return gen
+
+
+def _quantized(layer, suffix, w, group_size):
+    qt = formats.quantize(w, formats.QuantConfig(bits=4, granularity="group", group_size=group_size))
+    packed, packed_k = pack.pack_int4(qt.qweight)
+    return layer, suffix, packed.contiguous(), qt.scale.contiguous(), packed_k, w.shape[0], w.shape[1]
+
+
+def synthetic_small_tensors(arch: Architecture, gen: torch.Generator, std: float, embed_std: float, device):
+    """Norm weights (ones), embeddings N(0, embed_std), LM head N(0, std) -- drawn after the linear weights."""
+    H = arch.hidden_size
+    ones = torch.ones(H, dtype=torch.float16, device=device)
+    norms = [{"input_layernorm": ones, "post_attention_layernorm": ones,
+              "q_norm": torch.ones(arch.head_dim, dtype=torch.float16, device=device),
+              "k_norm": torch.ones(arch.head_dim, dtype=torch.float16, device=device)}
+             for _ in range(arch.num_layers)]
+    embed = (torch.randn(arch.vocab_size, H, generator=gen, device=device) * embed_std).half()
+    lm_head = (torch.randn(arch.vocab_size, H, generator=gen, device=device) * std).half()
+    return norms, embed, lm_head, ones
+
+
 def synthetic_streaming_model(arch: Architecture, seed: int = 0, group_size: int = 128, include_dip: bool = True,
                               resident: bool = True, offload: bool = True, std: float = 0.02,
                               embed_std: float = 1.0, device=None) -> StreamingModel:
@@ -106,57 +142,40 @@ def synthetic_streaming_model(arch: Architecture, seed: int = 0, group_size: int
     if not (resident or offload):
         raise ValueError("a model needs its weights resident, in the arena, or both")
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    gen = torch.Generator(device=device).manual_seed(seed)
     shapes = _linear_shapes(arch)
-    names = []
-    for layer in range(arch.num_layers):
-        for suffix in LINEAR_SUFFIXES:
-            names.append((layer, suffix, shapes[suffix], False))
-            if include_dip and suffix == "mlp.down_proj.weight":
-                names.append((layer, DOWN_PROJ_T_SUFFIX, shapes[suffix], True))
     store = None
     if offload:
-        total = sum(packed_int4_bytes(*(s[::-1] if t else s), group_size) for _, _, s, t in names)
+        total = 0
+        for _layer in range(arch.num_layers):
+            for suffix in LINEAR_SUFFIXES:
+                total += packed_int4_bytes(*shapes[suffix], group_size)
+                if include_dip and suffix == "mlp.down_proj.weight":
+                    total += packed_int4_bytes(*shapes[suffix][::-1], group_size)
         store = PinnedWeightStore(total)
     matrices: dict[str, LoadedMatrix] = {}
     res: dict[str, torch.Tensor] | None = {} if resident else None
-    down_w = None
-    for layer, suffix, (n, k), transposed in names:
+    weights = synthetic_weights(arch, seed, group_size, include_dip, std, device)
+    while True:
+        try:
+            layer, suffix, packed, scale, packed_k, n, k = next(weights)
+        except StopIteration as done:
+            gen = done.value
+            break
         name = f"model.layers.{layer}.{suffix}"
-        if transposed:
-            w = down_w.t().contiguous()  # the same matrix as the layer's down_proj
-            n, k = k, n
-        else:
-            w = torch.randn(n, k, generator=gen, device=device) * std
-            if suffix == "mlp.down_proj.weight":
-                down_w = w
-        qt = formats.quantize(w, formats.QuantConfig(bits=4, granularity="group", group_size=group_size))
-        packed, packed_k = pack.pack_int4(qt.qweight)
-        packed = packed.contiguous()
         if store is not None:
             handle = store.register(name, packed.cpu())
         else:
-            from ..offload.weight_store import WeightHandle
-
             handle = WeightHandle(name, -1, packed.shape[0], packed.shape[1])
         if res is not None:
             res[name] = packed
-        matrices[name] = LoadedMatrix(handle, qt.scale.contiguous(), packed_k, n, k)
-        del w, qt
-    H = arch.hidden_size
-    ones = torch.ones(H, dtype=torch.float16, device=device)
-    norms = [{"input_layernorm": ones, "post_attention_layernorm": ones,
-              "q_norm": torch.ones(arch.head_dim, dtype=torch.float16, device=device),
-              "k_norm": torch.ones(arch.head_dim, dtype=torch.float16, device=device)}
-             for _ in range(arch.num_layers)]
-    embed = (torch.randn(arch.vocab_size, H, generator=gen, device=device) * embed_std).half()
-    lm_head = (torch.randn(arch.vocab_size, H, generator=gen, device=device) * std).half()
+        matrices[name] = LoadedMatrix(handle, scale, packed_k, n, k)
+    norms, embed, lm_head, ones = synthetic_small_tensors(arch, gen, std, embed_std, device)
     return StreamingModel(store=store, matrices=matrices, num_layers=arch.num_layers, embed_tokens=embed,
-                          lm_head=lm_head, final_norm=ones, layer_norms=norms, hidden_size=H,
+                          lm_head=lm_head, final_norm=ones, layer_norms=norms, hidden_size=arch.hidden_size,
                           num_attention_heads=arch.num_attention_heads, num_key_value_heads=arch.num_key_value_heads,
                           head_dim=arch.head_dim, rms_norm_eps=arch.rms_norm_eps, rope_theta=arch.rope_theta,
                           group_size=group_size, resident=res)
 
 
-__all__ = ["load_streaming_model", "synthetic_streaming_model", "Architecture", "QWEN3_1_7B", "QWEN3_14B",
-           "quantize_and_pack"]
+__all__ = ["load_streaming_model", "synthetic_streaming_model", "synthetic_weights", "synthetic_small_tensors",
+           "Architecture", "QWEN3_1_7B", "QWEN3_14B", "quantize_and_pack"]

@@ -1,0 +1,237 @@
+"""Tensor-parallel decode across the GPUs of one node (
+the 14B-shaped model on 1/2/4/8 B200s).
+
+Sharding (Megatron-style, one process per GPU):
+* column-parallel (output rows split): q_proj / k_proj / v_proj by heads
+  (rank r owns query heads [r*NQ/G, (r+1)*NQ/G) and kv heads likewise),
+  gate_proj / up_proj by intermediate channels;
+* row-parallel (input K split): o_proj by the query-head slice of its input,
+  down_proj by the intermediate slice.  K/G is a multiple of the 128 group
+  size for every supported G, so a shard's scale columns are whole groups and
+  slicing the quantized matrix equals quantizing the slice;
+* per layer two all-reduces (sum): after o_proj and after down_proj -- the
+  partial products of the row-parallel GEMVs;
+* KV cache: each rank keeps its own kv heads;
+* LM head: vocabulary rows split; each rank's fused argmax gives (logit,
+  index) and the ranks agree on the global argmax (largest fp16 logit, then
+  lowest index) from an all-gather.
+
+Each rank's o / down GEMV rounds its partial to fp16; the partials cross the
+wire in fp32 and their sum is rounded to fp16 once, so TP differs from the
+single-GPU result by those roundings and the summation order (a tolerance,
+not bit identity).
+
+The shard plan is host logic (tested on CPU with gloo); the rank model is a
+StreamingModel of shard matrices and runs through the same kernels.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    rank: int
+    world: int
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    hidden: int
+    intermediate: int
+    vocab: int
+    group_size: int = 128
+
+    def __post_init__(self):
+        G = self.world
+        if not 0 <= self.rank < G:
+            raise ValueError(f"rank {self.rank} out of range for world size {G}")
+        if self.num_heads % G or self.num_kv_heads % G:
+            raise ValueError(f"head counts ({self.num_heads}, {self.num_kv_heads}) must divide by world size {G}")
+        if self.intermediate % G or (self.intermediate // G) % self.group_size:
+            raise ValueError(f"intermediate {self.intermediate} / {G} must be a multiple of {self.group_size}")
+        if (self.num_heads // G * self.head_dim) % self.group_size:
+            raise ValueError("the o_proj input slice must be whole quantization groups")
+
+    # -- slices (start, stop) of the full dimension owned by this rank
+    def _slice(self, total: int) -> tuple[int, int]:
+        per = total // self.world
+        return self.rank * per, (self.rank + 1) * per
+
+    @property
+    def q_rows(self) -> tuple[int, int]:
+        a, b = self._slice(self.num_heads)
+        return a * self.head_dim, b * self.head_dim
+
+    @property
+    def kv_rows(self) -> tuple[int, int]:
+        a, b = self._slice(self.num_kv_heads)
+        return a * self.head_dim, b * self.head_dim
+
+    @property
+    def inter_rows(self) -> tuple[int, int]:
+        return self._slice(self.intermediate)
+
+    @property
+    def vocab_rows(self) -> tuple[int, int]:
+        per = -(-self.vocab // self.world)
+        return min(self.rank * per, self.vocab), min((self.rank + 1) * per, self.vocab)
+
+    @property
+    def local_heads(self) -> int:
+        return self.num_heads // self.world
+
+    @property
+    def local_kv_heads(self) -> int:
+        return self.num_kv_heads // self.world
+
+    # -- which dimension of each linear weight is split, and the slice
+    def weight_slice(self, suffix: str) -> tuple[int, tuple[int, int]]:
+        """(axis, (start, stop)) of the full [N, K] weight this rank holds."""
+        if suffix.endswith("q_proj.weight"):
+            return 0, self.q_rows
+        if suffix.endswith(("k_proj.weight", "v_proj.weight")):
+            return 0, self.kv_rows
+        if suffix.endswith(("gate_proj.weight", "up_proj.weight")):
+            return 0, self.inter_rows
+        if suffix.endswith("o_proj.weight"):
+            return 1, self.q_rows
+        if suffix.endswith("down_proj.weight"):
+            return 1, self.inter_rows
+        if suffix.endswith("down_proj_T.weight"):
+            return 0, self.inter_rows
+        raise KeyError(suffix)
+
+
+def shard_packed(packed: torch.Tensor, scale: torch.Tensor, axis: int, sl: tuple[int, int], group_size: int):
+    """The rows (axis 0) or K columns (axis 1) [sl) of a quantized matrix
+    (packed uint8 [N, K/2], fp32 scales [N, K/g]); K slices are whole groups."""
+    a, b = sl
+    if axis == 0:
+        return packed[a:b].contiguous(), scale[a:b].contiguous()
+    if a % group_size or b % group_size:
+        raise ValueError(f"K slice {sl} must be whole {group_size}-groups")
+    return packed[:, a // 2:b // 2].contiguous(), scale[:, a // group_size:b // group_size].contiguous()
+
+
+def agree_argmax(local_logit: torch.Tensor, local_idx: torch.Tensor, offset: int, group=None) -> torch.Tensor:
+    """Global greedy token from every rank's (fp16 logit, local index): the
+    largest logit, ties to the lowest global index.  local_logit: fp16 [1],
+    local_idx: int32 [1]; returns int32 [1] on the local device (same value on
+    every rank).  One all-gather of an int64 key per rank."""
+    import torch.distributed as dist
+
+    key = _order_key(local_logit) * (1 << 32) + (0xFFFFFFFF - (local_idx.long() + offset))
+    world = dist.get_world_size(group)
+    if key.is_cuda:
+        keys = torch.empty(world, dtype=key.dtype, device=key.device)
+        dist.all_gather_into_tensor(keys, key, group=group)
+    else:
+        parts = [torch.empty_like(key) for _ in range(world)]
+        dist.all_gather(parts, key, group=group)
+        keys = torch.cat(parts)
+    best = keys.max()
+    return (0xFFFFFFFF - (best & 0xFFFFFFFF)).to(torch.int32).view(1)
+
+
+def _order_key(h: torch.Tensor) -> torch.Tensor:
+    """fp16 -> order-preserving non-negative int64 key (as the fused argmax kernel)."""
+    b = h.view(torch.int16).long() & 0xFFFF
+    b = torch.where(b == 0x8000, torch.zeros_like(b), b)  # -0 -> +0
+    return torch.where(b & 0x8000 != 0, 0xFFFF - b, b | 0x8000)
+
+
+def build_tp_model(arch, plan: ShardPlan, seed: int = 0, group_size: int = 128, include_dip: bool = False,
+                   std: float = 0.02, embed_std: float = 1.0, device=None):
+    """This rank's shard of the seeded synthetic model (the same full matrices
+    as runtime.loader.synthetic_streaming_model(arch, seed), sliced per the
+    plan), weights resident in HBM; embeddings and norms replicated, LM head
+    rows split."""
+    from ..offload.load_hf_checkpoint import LoadedMatrix
+    from ..offload.weight_store import WeightHandle
+    from .generate import StreamingModel
+    from .loader import synthetic_small_tensors, synthetic_weights
+
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    matrices, resident = {}, {}
+    weights = synthetic_weights(arch, seed, group_size, include_dip, std, device)
+    while True:
+        try:
+            layer, suffix, packed, scale, packed_k, n, k = next(weights)
+        except StopIteration as done:
+            gen = done.value
+            break
+        name = f"model.layers.{layer}.{suffix}"
+        axis, sl = plan.weight_slice(suffix)
+        pk, sc = shard_packed(packed, scale, axis, sl, group_size)
+        del packed, scale
+        if axis == 0:
+            n_s, k_s, pk_k = sl[1] - sl[0], k, packed_k
+        else:
+            n_s, k_s, pk_k = n, sl[1] - sl[0], sl[1] - sl[0]
+        matrices[name] = LoadedMatrix(WeightHandle(name, -1, pk.shape[0], pk.shape[1]), sc, pk_k, n_s, k_s)
+        resident[name] = pk
+    norms, embed, lm_head, ones = synthetic_small_tensors(arch, gen, std, embed_std, device)
+    lo, hi = plan.vocab_rows
+    lm_shard = lm_head[lo:hi].contiguous()
+    del lm_head
+    return StreamingModel(store=None, matrices=matrices, num_layers=arch.num_layers, embed_tokens=embed,
+                          lm_head=lm_shard, final_norm=ones, layer_norms=norms, hidden_size=arch.hidden_size,
+                          num_attention_heads=plan.local_heads, num_key_value_heads=plan.local_kv_heads,
+                          head_dim=arch.head_dim, rms_norm_eps=arch.rms_norm_eps, rope_theta=arch.rope_theta,
+                          group_size=group_size, resident=resident)
+
+
+def all_reduce_sum(partial: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of the ranks' fp16 partial vectors, accumulated in fp32, rounded once."""
+    import torch.distributed as dist
+
+    f = partial.float()
+    dist.all_reduce(f, group=group)
+    return f.half()
+
+
+def run_decoder_layer_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, group=None):
+    """Dense decoder layer on this rank's shard: local q / k / v heads and
+    attention, row-parallel o_proj partial + all-reduce, residual + rmsnorm,
+    local gate / up (SwiGLU), row-parallel down partial + all-reduce, residual."""
+    from .. import ops
+    from .generate import _attention_block
+
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache,
+                              reduce_o=lambda o: all_reduce_sum(o, group))
+    down = pipeline.next_gemv(pipeline.next_glu(h3))
+    return h2 + all_reduce_sum(down, group)
+
+
+def tp_next_token(model, xn: torch.Tensor, plan: ShardPlan, group=None) -> torch.Tensor:
+    """Greedy token over the vocabulary-parallel LM head: each rank's fused
+    argmax of its rows, then agree_argmax across ranks."""
+    from .. import _C
+
+    idx, logits = _C.gemv_fp16_argmax(model.lm_head, xn, logits=True)
+    return agree_argmax(logits.index_select(0, idx.long()), idx, plan.vocab_rows[0], group)
+
+
+def generate_tp(model, plan: ShardPlan, prompt_ids: list[int], n_new: int, group=None, max_seq_len: int = 512):
+    """Eager greedy decode of the TP model (every rank returns the same ids)."""
+    from .generate import WeightPipeline, _greedy
+
+    pipeline = WeightPipeline(model)
+    return _greedy(model, prompt_ids, n_new,
+                   lambda li, x, p, kc, vc: run_decoder_layer_tp(pipeline, model, li, x, p, kc, vc, group),
+                   None, max_seq_len, token_fn=lambda m, xn: tp_next_token(m, xn, plan, group))
+
+
+def graph_decoder_tp(model, plan: ShardPlan, group=None, max_seq_len: int = 2048):
+    """GraphDecoder whose captured step is the TP layer stack (NCCL collectives inside the graph)."""
+    from .generate import GraphDecoder
+
+    return GraphDecoder(model, max_seq_len=max_seq_len,
+                        layer_fn=lambda p, m, li, x, w, kc, vc: run_decoder_layer_tp(p, m, li, x, w, kc, vc, group),
+                        token_fn=lambda m, xn: tp_next_token(m, xn, plan, group))
+
+
+__all__ = ["ShardPlan", "shard_packed", "agree_argmax", "build_tp_model", "all_reduce_sum", "run_decoder_layer_tp",
+           "tp_next_token", "generate_tp", "graph_decoder_tp"]
