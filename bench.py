@@ -466,13 +466,14 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
     captured in it).  ms/token is the max over ranks of the CUDA-event time."""
     from soinfer.runtime import generate as gen
     from soinfer.runtime.loader import QWEN3_14B, synthetic_streaming_model
-    from soinfer.runtime.tp import ShardPlan, build_tp_model, graph_decoder_tp
+    from soinfer.runtime.tp import PeerExchange, ShardPlan, build_tp_model, graph_decoder_tp
 
     arch = QWEN3_14B
     max_seq = 4096
     n_prompt, n_new = args.tp_prompt, args.tp_tokens
     if n_prompt + n_new > max_seq:
         raise ValueError("tp prompt + tokens must fit the 4096 context")
+    exchange = None
     if world == 1:
         model = synthetic_streaming_model(arch, seed=2, resident=True, offload=False, include_dip=False,
                                           device=device)
@@ -481,7 +482,9 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
         plan = ShardPlan(rank, world, arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim,
                          arch.hidden_size, arch.intermediate_size, arch.vocab_size)
         model = build_tp_model(arch, plan, seed=2, device=device)
-        gd = graph_decoder_tp(model, plan, max_seq_len=max_seq)
+        if not args.tp_nccl:
+            exchange = PeerExchange(device=device)
+        gd = graph_decoder_tp(model, plan, max_seq_len=max_seq, exchange=exchange)
     weight_bytes = sum(t.numel() for t in model.resident.values()) + sum(
         m.scale.numel() * m.scale.element_size() for m in model.matrices.values())
     prompt = torch.randint(0, arch.vocab_size, (n_prompt,), generator=torch.Generator().manual_seed(1)).tolist()
@@ -501,7 +504,13 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
     else:
         agree = True
     decode_ms, prefill_ms = (float(v) for v in t.tolist())
-    del gd, model
+    del gd
+    if exchange is not None:
+        from soinfer import _C
+
+        assert _C.device_errors() == 0, "device error bits set during TP decode (peer exchange)"
+        exchange.close()
+    del model
     torch.cuda.empty_cache()
     n = n_new - 1
     ms_tok = decode_ms / n
@@ -518,7 +527,10 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
             "hbm_bytes_per_token_per_rank": int(rank_bytes),
             "hbm_floor_ms": round(rank_bytes / (measured_peaks().get("hbm_gbs") or 6650.0) / 1e6, 4),
             "collectives_per_token": 2 * arch.num_layers + 1,
-            "step": "one CUDA graph per token; fp32 all-reduce of the o / down partials (NCCL over NVLink)"}
+            "step": "one CUDA graph per token; " + (
+                "NCCL fp32 all-reduce of the o / down partials" if world > 1 and args.tp_nccl else
+                "row-parallel GEMV stores its rows into every rank's inbox over NVLink, one exchange kernel "
+                "sums + residual + RMSNorm (soinfer.runtime.tp.PeerExchange)" if world > 1 else "single GPU")}
 
 
 def main() -> None:
@@ -536,6 +548,7 @@ def main() -> None:
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
     ap.add_argument("--tp-tokens", type=int, default=256)
+    ap.add_argument("--tp-nccl", type=int, default=0, help="TP collectives through NCCL instead of the peer exchange")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -379,6 +379,69 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                                 const int32_t* pos_dev, void* workspace, int64_t workspace_bytes,
                                 void* stream);
 
+/* ---- Tensor-parallel exchange over peer memory (no reference counterpart:
+ * the reference runs on one GPU; this is the row-parallel all-reduce, the
+ * all-gather and the greedy-token agreement of tensor-parallel decode across
+ * the GPUs of one node, one process per GPU).
+ *
+ * Each rank creates one exchange buffer (soinfer_peer_buffer_create: device
+ * memory, zeroed, plus a CUDA IPC handle of SOINFER_IPC_HANDLE_BYTES bytes),
+ * hands the handle to the other ranks (any host channel), and maps theirs
+ * (soinfer_peer_buffer_open).  A soinfer_peer_set lists every rank's buffer as
+ * mapped in this process (base[rank] = its own), the rank, the world size
+ * (1..8) and the inbox slot size (a multiple of 16 bytes, at least the
+ * largest payload).  Kernels store straight into the peers' buffers over
+ * NVLink, then signal them with system-scope release flags; every wait is
+ * bounded (1 s) and a timeout raises a device error bit
+ * (soinfer_device_errors) instead of hanging.  All ranks must issue the same
+ * sequence of exchange calls on their streams.
+ *
+ * allreduce_add_rmsnorm: out_sum = fp16(residual + fp16(sum over ranks of
+ * partial)) (sum in fp32, rank order; residual may be NULL), and when
+ * out_norm is not NULL out_norm = RMSNorm(out_sum) * weight (eps); n % 8 == 0.
+ * partial == NULL: the partials were already pushed by
+ * soinfer_gemv_w4a16_tp_partial, which computes the row-parallel INT4 GEMV
+ * (same arguments and arithmetic as soinfer_gemv_w4a16_group_lop3) and stores
+ * its fp16 rows into every rank's inbox instead of an output vector (K and
+ * group_size multiples of 128, 16-byte aligned rows).
+ * allgather: out [world * nbytes] = every rank's local [nbytes] in rank order
+ * (nbytes % 16 == 0).
+ * argmax: with a vocabulary-parallel LM head (rank r owns rows from offset),
+ * out_idx int32 [1] = the global greedy token -- the largest fp16
+ * logits[local_idx] over ranks, ties to the lowest global index (the rule of
+ * soinfer_gemv_fp16_argmax). */
+#define SOINFER_IPC_HANDLE_BYTES 64
+#define SOINFER_MAX_PEERS 8
+typedef struct soinfer_peer_set {
+  void* base[SOINFER_MAX_PEERS];
+  int32_t rank;
+  int32_t world;
+  int64_t slot_bytes;
+} soinfer_peer_set;
+
+int64_t soinfer_peer_buffer_bytes(int64_t slot_bytes, int32_t world);
+int soinfer_peer_buffer_create(int64_t bytes, void** dptr, void* ipc_handle);
+int soinfer_peer_buffer_open(const void* ipc_handle, void** dptr);
+int soinfer_peer_buffer_close(void* dptr);
+int soinfer_peer_buffer_destroy(void* dptr);
+int soinfer_tp_allreduce_add_rmsnorm(const soinfer_peer_set* peers, const soinfer_half* partial,
+                                     const soinfer_half* residual, const soinfer_half* weight,
+                                     soinfer_half* out_sum, soinfer_half* out_norm, int64_t n, float eps,
+                                     void* stream);
+int soinfer_gemv_w4a16_tp_partial(const soinfer_peer_set* peers, const uint8_t* Wq_packed,
+                                  const float* scale, const soinfer_half* x, int64_t N, int64_t K,
+                                  int64_t group_size, int64_t num_groups, void* stream);
+/* Tensor-parallel form of soinfer_gemv_w4a16_batch: at most one task may have
+ * y == NULL (no glu_gate / residual); its rows go to every rank's inbox as
+ * with soinfer_gemv_w4a16_tp_partial, signalled when the whole launch is done.
+ * Finish with soinfer_tp_allreduce_add_rmsnorm(partial = NULL). */
+int soinfer_gemv_w4a16_batch_tp(const soinfer_peer_set* peers, const soinfer_gemv_task* tasks,
+                                int64_t num_tasks, void* workspace, int64_t workspace_bytes, void* stream);
+int soinfer_tp_allgather(const soinfer_peer_set* peers, const void* local, int64_t nbytes, void* out,
+                         void* stream);
+int soinfer_tp_argmax(const soinfer_peer_set* peers, const soinfer_half* logits, const int32_t* local_idx,
+                      int64_t offset, int32_t* out_idx, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

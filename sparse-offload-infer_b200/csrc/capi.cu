@@ -4,6 +4,7 @@
 // the thread's last-error message.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -89,6 +90,8 @@ int soinfer_device_errors(int* flags) {
   *flags |= f;
   if (int st = cuda_result(read_and_clear_gemv_batch_error(&f), "device_errors")) return st;
   *flags |= f;
+  if (int st = cuda_result(read_and_clear_tp_error(&f), "device_errors")) return st;
+  *flags |= f;
   return SOINFER_OK;
 }
 
@@ -97,27 +100,37 @@ int64_t soinfer_gemv_batch_workspace_bytes(int64_t num_tasks) {
   return gemv_batch_workspace_bytes(num_tasks);
 }
 
-int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,
-                             int64_t workspace_bytes, void* stream) {
-  const char* name = "gemv_w4a16_batch";
+static int gemv_batch_common(const char* name, const PeerSet* peers, const soinfer_gemv_task* tasks,
+                             int64_t num_tasks, void* workspace, int64_t workspace_bytes, void* stream) {
   REQUIRE(num_tasks >= 0 && num_tasks <= kMaxBatchTasks, "%s: num_tasks must be in [0, %d]", name, kMaxBatchTasks);
   if (num_tasks == 0) return SOINFER_OK;
   REQUIRE(tasks, "%s: null task list", name);
   bool fast = true;
+  int npeer = 0;
   for (int64_t i = 0; i < num_tasks; ++i) {
     const soinfer_gemv_task& t = tasks[i];
     char tn[64];
     snprintf(tn, sizeof(tn), "%s[task %lld]", name, (long long)i);
     if (int st = check_int4_layout(tn, t.K, t.group_size, t.num_groups)) return st;
     REQUIRE(t.N >= 1, "%s: N must be >= 1", tn);
-    REQUIRE(t.Wq && t.scale && t.x && t.y, "%s: null pointer", tn);
+    REQUIRE(t.Wq && t.scale && t.x && (t.y || peers), "%s: null pointer", tn);
     REQUIRE(t.dep >= -1 && t.dep < i, "%s: dep must be -1 or an earlier task index", tn);
+    if (!t.y) {  // the row-parallel task whose rows go to the peers' inboxes
+      ++npeer;
+      REQUIRE(npeer == 1, "%s: at most one task per batch may send its rows to the peers (y == NULL)", tn);
+      REQUIRE(t.N * 2 <= peers->slot_bytes, "%s: N rows exceed the exchange slot", tn);
+      REQUIRE(!t.glu_gate && !t.residual, "%s: a peer task takes no epilogue (the exchange adds the residual)", tn);
+      REQUIRE(t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.Wq, 16) && aligned(t.x, 16) &&
+                  aligned(t.scale, 4),
+              "%s: a peer task needs K and group_size multiples of 128 and 16-byte aligned rows / x", tn);
+    }
     for (int64_t j = 0; j < i; ++j) {  // an epilogue input made in this batch must share the row split
-      if (tasks[j].y == t.glu_gate || tasks[j].y == t.residual)
+      if (tasks[j].y && (tasks[j].y == t.glu_gate || tasks[j].y == t.residual))
         REQUIRE(tasks[j].N == t.N, "%s: glu_gate / residual is task %lld's y but N differs", tn, (long long)j);
     }
-    fast = fast && t.K % 128 == 0 && t.group_size % 128 == 0 && t.num_groups % 4 == 0 && aligned(t.Wq, 16) &&
-           aligned(t.scale, 16) && aligned(t.x, 16) && t.N < (1 << 30) && t.K < (1 << 30);
+    fast = fast && t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.Wq, 16) && aligned(t.scale, 4) &&
+           (t.num_groups % 4 != 0 || aligned(t.scale, 16)) && aligned(t.x, 16) && t.N < (1 << 30) &&
+           t.K < (1 << 30);
   }
   cudaStream_t st = as_stream(stream);
   if (fast) {
@@ -125,6 +138,12 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
     static std::mutex mu;
     std::lock_guard<std::mutex> lk(mu);
     B.num = (int)num_tasks;
+    if (peers) {
+      B.peers = *peers;
+    } else {
+      B.peers = PeerSet{};
+      B.peers.world = 0;
+    }
     for (int64_t i = 0; i < num_tasks; ++i) {
       const soinfer_gemv_task& t = tasks[i];
       GemvBatchTask& d = B.tasks[i];
@@ -139,6 +158,7 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
       d.dep = (int)t.dep;
       d.resid = as_half(t.residual);
       d.glu = as_half(t.glu_gate);
+      d.peer = t.y ? 0 : 1;
     }
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -157,6 +177,13 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
     src.rows1 = t.N;
     src.row_bytes = int4_row_bytes(t.K);
     src.num_groups = t.num_groups;
+    if (!t.y) {
+      const cudaError_t e = launch_gemv_w4_peer(src, as_half(t.x), t.N, t.K, t.group_size, *peers, st);
+      if (e == cudaErrorNotSupported)
+        return set_error(SOINFER_ERR_UNSUPPORTED, "%s: peer task shape outside the bulk GEMV path", name);
+      if (int rc = cuda_result(e, name)) return rc;
+      continue;
+    }
     if (int rc = cuda_result(launch_gemv_w4(RowMode::kPlain, src, as_half(t.x), as_half(t.y), t.N, t.K, t.group_size, st),
                              name))
       return rc;
@@ -168,6 +195,11 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
         return rc;
   }
   return SOINFER_OK;
+}
+
+int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  return gemv_batch_common("gemv_w4a16_batch", nullptr, tasks, num_tasks, workspace, workspace_bytes, stream);
 }
 
 static int gemv_w4_plain(const char* name, const uint8_t* Wq, const float* scale, const soinfer_half* x,
@@ -600,6 +632,145 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                                                 num_q_heads, num_kv_heads, max_seq_len, head_dim, pos_dev, workspace,
                                                 as_stream(stream)),
                      name);
+}
+
+// ---------------------------------------------------------------- tensor-parallel exchange
+
+static_assert(sizeof(cudaIpcMemHandle_t) == SOINFER_IPC_HANDLE_BYTES, "IPC handle size");
+static_assert(SOINFER_MAX_PEERS == kMaxPeers, "peer count");
+
+namespace {
+int to_peer_set(const char* name, const soinfer_peer_set* in, PeerSet& ps) {
+  REQUIRE(in, "%s: null peer set", name);
+  REQUIRE(in->world >= 1 && in->world <= kMaxPeers, "%s: world size must be in [1, %d]", name, kMaxPeers);
+  REQUIRE(in->rank >= 0 && in->rank < in->world, "%s: rank out of range", name);
+  REQUIRE(in->slot_bytes >= 16 && in->slot_bytes % 16 == 0 && in->slot_bytes < (1ll << 31),
+          "%s: slot_bytes must be a positive multiple of 16", name);
+  for (int r = 0; r < kMaxPeers; ++r) {
+    if (r < in->world) {
+      REQUIRE(in->base[r] && aligned(in->base[r], 256), "%s: peer buffer %d null or not 256-byte aligned", name, r);
+    }
+    ps.base[r] = r < in->world ? static_cast<uint8_t*>(in->base[r]) : nullptr;
+  }
+  ps.rank = in->rank;
+  ps.world = in->world;
+  ps.slot_bytes = in->slot_bytes;
+  return SOINFER_OK;
+}
+}  // namespace
+
+int64_t soinfer_peer_buffer_bytes(int64_t slot_bytes, int32_t world) {
+  if (slot_bytes < 16 || slot_bytes % 16 || world < 1 || world > kMaxPeers) return 0;
+  return peer_buffer_bytes(slot_bytes, world);
+}
+
+int soinfer_peer_buffer_create(int64_t bytes, void** dptr, void* ipc_handle) {
+  const char* name = "peer_buffer_create";
+  REQUIRE(dptr && ipc_handle, "%s: null output pointer", name);
+  REQUIRE(bytes >= kPeerHeaderBytes, "%s: buffer smaller than its header", name);
+  *dptr = nullptr;
+  void* p = nullptr;
+  if (int st = cuda_result(cudaMalloc(&p, (size_t)bytes), name)) return st;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMemset(p, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any stream (blocking or not) uses it
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_result(e, name);
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dptr = p;
+  return SOINFER_OK;
+}
+
+int soinfer_peer_buffer_open(const void* ipc_handle, void** dptr) {
+  const char* name = "peer_buffer_open";
+  REQUIRE(ipc_handle && dptr, "%s: null pointer", name);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  *dptr = nullptr;
+  return cuda_result(cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess), name);
+}
+
+int soinfer_peer_buffer_close(void* dptr) {
+  REQUIRE(dptr, "peer_buffer_close: null pointer");
+  return cuda_result(cudaIpcCloseMemHandle(dptr), "peer_buffer_close");
+}
+
+int soinfer_peer_buffer_destroy(void* dptr) {
+  REQUIRE(dptr, "peer_buffer_destroy: null pointer");
+  return cuda_result(cudaFree(dptr), "peer_buffer_destroy");
+}
+
+int soinfer_tp_allreduce_add_rmsnorm(const soinfer_peer_set* peers, const soinfer_half* partial,
+                                     const soinfer_half* residual, const soinfer_half* weight, soinfer_half* out_sum,
+                                     soinfer_half* out_norm, int64_t n, float eps, void* stream) {
+  const char* name = "tp_allreduce_add_rmsnorm";
+  PeerSet ps;
+  if (int st = to_peer_set(name, peers, ps)) return st;
+  REQUIRE(n >= 8 && n % 8 == 0 && n * 2 <= ps.slot_bytes, "%s: n must be a multiple of 8 with 2n <= slot_bytes",
+          name);
+  REQUIRE(out_sum && (!out_norm || weight), "%s: null output (or weight with out_norm)", name);
+  REQUIRE(aligned(out_sum, 16) && aligned(partial, 16) && aligned(residual, 16) && aligned(weight, 16) &&
+              aligned(out_norm, 16),
+          "%s: vectors must be 16-byte aligned", name);
+  return cuda_result(launch_tp_allreduce_norm(ps, as_half(partial), as_half(residual), as_half(weight),
+                                              as_half(out_sum), as_half(out_norm), n, eps, as_stream(stream)),
+                     name);
+}
+
+int soinfer_gemv_w4a16_tp_partial(const soinfer_peer_set* peers, const uint8_t* Wq, const float* scale,
+                                  const soinfer_half* x, int64_t N, int64_t K, int64_t group_size, int64_t num_groups,
+                                  void* stream) {
+  const char* name = "gemv_w4a16_tp_partial";
+  PeerSet ps;
+  if (int st = to_peer_set(name, peers, ps)) return st;
+  if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
+  REQUIRE(N >= 1 && N * 2 <= ps.slot_bytes, "%s: N must be >= 1 with 2N <= slot_bytes", name);
+  REQUIRE(K % 128 == 0 && group_size % 128 == 0, "%s: K and group_size must be multiples of 128", name);
+  REQUIRE(Wq && scale && x, "%s: null pointer", name);
+  REQUIRE(aligned(Wq, 16) && aligned(scale, 16) && aligned(x, 16), "%s: Wq, scale and x must be 16-byte aligned",
+          name);
+  RowSource src;
+  src.W = Wq;
+  src.S = scale;
+  src.rows1 = N;
+  src.row_bytes = int4_row_bytes(K);
+  src.num_groups = num_groups;
+  const cudaError_t e = launch_gemv_w4_peer(src, as_half(x), N, K, group_size, ps, as_stream(stream));
+  if (e == cudaErrorNotSupported)
+    return set_error(SOINFER_ERR_UNSUPPORTED, "%s: shape outside the bulk GEMV path (rows too wide for one CTA)", name);
+  return cuda_result(e, name);
+}
+
+int soinfer_gemv_w4a16_batch_tp(const soinfer_peer_set* peers, const soinfer_gemv_task* tasks, int64_t num_tasks,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* name = "gemv_w4a16_batch_tp";
+  PeerSet ps;
+  if (int st = to_peer_set(name, peers, ps)) return st;
+  return gemv_batch_common(name, &ps, tasks, num_tasks, workspace, workspace_bytes, stream);
+}
+
+int soinfer_tp_allgather(const soinfer_peer_set* peers, const void* local, int64_t nbytes, void* out, void* stream) {
+  const char* name = "tp_allgather";
+  PeerSet ps;
+  if (int st = to_peer_set(name, peers, ps)) return st;
+  REQUIRE(nbytes >= 16 && nbytes % 16 == 0 && nbytes <= ps.slot_bytes,
+          "%s: nbytes must be a positive multiple of 16, at most slot_bytes", name);
+  REQUIRE(local && out && aligned(local, 16) && aligned(out, 16), "%s: null or misaligned buffer", name);
+  return cuda_result(launch_tp_allgather(ps, local, nbytes, out, as_stream(stream)), name);
+}
+
+int soinfer_tp_argmax(const soinfer_peer_set* peers, const soinfer_half* logits, const int32_t* local_idx,
+                      int64_t offset, int32_t* out_idx, void* stream) {
+  const char* name = "tp_argmax";
+  PeerSet ps;
+  if (int st = to_peer_set(name, peers, ps)) return st;
+  REQUIRE(ps.slot_bytes >= 16, "%s: slot too small", name);
+  REQUIRE(logits && local_idx && out_idx, "%s: null pointer", name);
+  REQUIRE(offset >= 0 && offset < (1ll << 31), "%s: offset out of range", name);
+  return cuda_result(launch_tp_argmax(ps, as_half(logits), local_idx, offset, out_idx, as_stream(stream)), name);
 }
 
 }  // extern "C"

@@ -162,7 +162,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32
 }
 
 // Device-side error bits (reported through soinfer_device_errors()).
-enum DeviceError : int { kErrCopyTimeout = 1 };
+enum DeviceError : int { kErrCopyTimeout = 1, kErrPeerTimeout = 2 };
 
 // Row source of a cache-or-stream descriptor (reference gemv_dip_fused.cu:11-12).
 __device__ __forceinline__ bool desc_is_staging(int32_t d) { return d < 0; }

@@ -15,8 +15,14 @@
 // slab is cut into items of whole 16-row tiles (as many as fit in
 // kMaxItemBytes); each item is exactly two bulk copies (cp.async.bulk, one
 // for the packed rows, one for their scale rows) completing on one mbarrier.
-// Items of any size share a circular byte ring, so the bytes in flight stay
-// near the ring size whatever the matrix shape.
+// A tile too long for one item (K above ~6K, e.g. a 14B down_proj) is cut
+// along K into segments of ks 128-chunks, one item each (one bulk copy per
+// row); the consumers accumulate a tile's segments in their partial rows.
+// Scale rows that are not whole 16-byte pieces (tensor-parallel shards with
+// 5, 10, 17 or 34 groups per row) are staged with 4-byte cp.async copies that
+// arrive on the item's barrier; segment scales go as one bulk copy per row.  Items of any size
+// share a circular byte ring, so the bytes in flight stay near the ring size
+// whatever the matrix shape.
 //
 // Roles (one CTA per SM, 19 warps):
 //   warps 0..15  consumers in two groups of 8 that take alternate tasks; a
@@ -30,6 +36,9 @@
 //   warp 18      epilogue: sums the 8 partials per row, frees the partial
 //                buffer, writes y and -- only for a task that a later task
 //                depends on -- fences and publishes its completion counter.
+//                A peer task (tensor parallelism) stores its rows into every
+//                rank's exchange inbox instead (NVLink stores); the last CTA
+//                to finish the launch signals the exchange (peer.cuh).
 // All lanes of a warp wait on an mbarrier together: a lane-0 poll with the
 // rest of the warp parked in __syncwarp delays the hand-offs measurably.
 //
@@ -50,6 +59,7 @@
 // sparse-offload-infer.
 #include "common.cuh"
 #include "kernels.h"
+#include "peer.cuh"
 
 namespace soinfer {
 
@@ -68,7 +78,7 @@ constexpr int kMaxTiles = 8;                  // 16-row tiles per CTA per task
 constexpr int kRedRows = kMaxTiles * 16;
 constexpr int kRedBytes = 2 * kGroupWarps * kRedRows * 4;
 constexpr int kMaxItemBytes = 52 * 1024;
-constexpr int kMaxChunksPerWarp = 8;          // K <= kGroupWarps * kMaxChunksPerWarp * 128 = 8192
+constexpr int kMaxChunksPerWarp = 24;         // K <= kGroupWarps * kMaxChunksPerWarp * 128 = 24576
 constexpr int kSmemLimit = 227 * 1024;
 constexpr uint64_t kWaitNs = 1000000000ull;   // 1 s
 
@@ -92,6 +102,15 @@ __device__ __forceinline__ void cp_async_16(void* dst_smem, const void* src) {
 }
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 4-byte form (scale rows of any length), and the counted arrive-on: the
+// barrier's pending count is raised now and lowered when this thread's
+// earlier cp.async copies have landed (net zero: the init count is unchanged).
+__device__ __forceinline__ void cp_async_4(void* dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -169,6 +188,15 @@ struct TaskView {
   int64_t row0;
 };
 
+// Item k of a task (in issue order): tiles [tile0, tile0 + nt), K-segment seg.
+struct ItemView {
+  int tile0, nt, seg;
+};
+
+__device__ __forceinline__ int task_items(const GemvBatchTask& tk, const TaskView& v) {
+  return (v.tiles + tk.tiles_per_item - 1) / tk.tiles_per_item * tk.nsegs;
+}
+
 __device__ __forceinline__ TaskView task_view(const GemvBatchTask& tk, int cta) {
   TaskView v;
   v.row0 = (int64_t)cta * tk.rows_per_cta;
@@ -215,7 +243,7 @@ __device__ __forceinline__ void consume_unit(const uint4 xf[4], const uint8_t* w
 // nm chunks.  G128: group size 128, one scale column per chunk.
 template <int NM, bool G128>
 __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint8_t* wbase, const float* sbase,
-                                              int rows, int tile0, int nt, int nm) {
+                                              int rows, int tile0, int nt, int nm, bool accum) {
   uint4 xr[2][4];
   float br[2] = {0.f, 0.f};
 #pragma unroll
@@ -250,9 +278,163 @@ __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint
         consume_unit(xf, wa, w1, sa[sc], s1p[sc], ct.sbias[i], i, acc0, acc1);
       }
     }
+    if (accum) {  // a later K-segment of the tile
+      acc0 += ct.rr[tt * 16 + ct.g];
+      acc1 += ct.rr[tt * 16 + ct.g + 8];
+    }
     ct.rr[tt * 16 + ct.g] = acc0;
     ct.rr[tt * 16 + ct.g + 8] = acc1;
   }
+}
+
+// The producer warp's loop.
+__device__ __forceinline__ void producer_loop(const GemvBatchParams& B, int cta, int lane, uint8_t* ring,
+                                           uint64_t* full, uint64_t* empty, int* item_off,
+                                           volatile int* abort_flag) {
+  // ------------------------------------------------------------ producer
+  // Ring allocation is FIFO: items are consumed in issue order, so the
+  // occupied bytes are [item_off[oldest], head) circularly.
+  int head = 0, issued = 0, oldest = 0;
+  bool stop = false;
+  for (int ti = 0; ti < B.num && !stop; ++ti) {
+    const GemvBatchTask& tk = B.tasks[ti];
+    const TaskView v = task_view(tk, cta);
+    const int row_bytes = tk.K / 2;
+    const bool segd = tk.nsegs > 1;
+    const int wrow = segd ? tk.ks * 64 : row_bytes;     // weight row stride in the item
+    const int srow_f = segd ? tk.ks / tk.cpg : tk.G;    // scale row stride in the item (floats)
+    const int nitems = task_items(tk, v);
+    int tile0 = 0, seg = 0;  // item (tile0, seg): segments of a tile are consecutive
+    for (int it = 0; it < nitems && !stop; ++it, seg = (seg + 1 == tk.nsegs) ? (tile0 += tk.tiles_per_item, 0) : seg + 1) {
+      const int nt = min(tk.tiles_per_item, v.tiles - tile0);
+      const int rows = item_rows(v, tile0, nt);
+      const int nks = segd ? min(tk.ks, v.chunks - seg * tk.ks) : v.chunks;
+      const int wb = rows * wrow, sb = rows * srow_f * 4;
+      const int bytes = round128(wb) + round128(sb);
+      if (head + bytes > B.ring_bytes) head = 0;
+      while (issued > oldest) {
+        const int start = item_off[oldest % kMaxItems];
+        const bool overlap = head <= start && head + bytes > start;
+        if (issued - oldest < kMaxItems && !overlap) break;
+        if (!warp_wait(&empty[oldest % kMaxItems], (uint32_t)((oldest / kMaxItems) & 1), abort_flag)) {
+          stop = true;
+          break;
+        }
+        ++oldest;
+      }
+      if (stop) break;
+      const int d = issued % kMaxItems;
+      __syncwarp();  // every lane has read item_off[] before lane 0 rewrites a slot
+      const int64_t r0 = v.row0 + tile0 * 16;
+      if (lane == 0) item_off[d] = head;
+      if (B.any_cp_async) fence_proxy_async_smem();  // earlier cp.async writes into the ring precede bulk writes
+      float* sdst = reinterpret_cast<float*>(ring + head + round128(wb));
+      const int gs = segd ? nks / tk.cpg : tk.G;  // scale columns of the item's rows
+      // segment scales as one bulk copy per row when every piece is whole 16 bytes
+      const bool seg_bulk = segd && (tk.G % 4) == 0 && (srow_f % 4) == 0 && (gs % 4) == 0;
+      if (tk.scale_plain && !seg_bulk) {
+        // scale rows not in 16-byte pieces: 4-byte cp.async copies; each
+        // lane's arrive-on (counted before lane 0's arrive below) completes
+        // when its copies have landed, so the producer never waits on them
+        const float* src = tk.S + r0 * tk.G + (segd ? seg * srow_f : 0);
+        for (int i = lane; i < rows * gs; i += 32) {
+          const int rr = i / gs, c = i - rr * gs;
+          cp_async_4(sdst + rr * srow_f + c, src + (int64_t)rr * tk.G + c);
+        }
+        cp_async_arrive(&full[d]);
+        __syncwarp();
+      }
+      if (!segd) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[d], (uint32_t)(wb + (tk.scale_plain ? 0 : sb)));
+          bulk_g2s(ring + head, tk.W + r0 * row_bytes, (uint32_t)wb, &full[d]);
+          if (!tk.scale_plain) bulk_g2s(sdst, tk.S + r0 * tk.G, (uint32_t)sb, &full[d]);
+        }
+      } else {
+        if (lane == 0) mbar_arrive_expect_tx(&full[d], (uint32_t)(rows * (nks * 64 + (seg_bulk ? gs * 4 : 0))));
+        if (lane < rows)
+          bulk_g2s(ring + head + lane * wrow, tk.W + (r0 + lane) * row_bytes + (int64_t)seg * tk.ks * 64,
+                   (uint32_t)(nks * 64), &full[d]);
+        if (seg_bulk && lane >= 16 && lane - 16 < rows)
+          bulk_g2s(sdst + (lane - 16) * srow_f, tk.S + (r0 + lane - 16) * tk.G + seg * srow_f, (uint32_t)(gs * 4),
+                   &full[d]);
+      }
+      __syncwarp();
+      head += bytes;
+      ++issued;
+    }
+  }
+  if (stop) raise_abort(abort_flag);
+  // every issued copy must land before this CTA's shared memory is released
+  for (int q = max(oldest, issued - kMaxItems); q < issued; ++q)
+    (void)mbar_wait_bounded(&full[q % kMaxItems], (uint32_t)((q / kMaxItems) & 1), kWaitNs / 4);
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// The epilogue warp's loop.
+__device__ __forceinline__ void epilogue_loop(const GemvBatchParams& B, int cta, int lane, const float* red,
+                                           uint64_t* rfull, uint64_t* rempty, uint8_t* const* s_inbox,
+                                           int* counters, volatile int* abort_flag) {
+  // ------------------------------------------------------------ epilogue
+  int a = 0;
+  bool stop = false;
+  for (int ti = 0; ti < B.num && !stop; ++ti) {
+    const GemvBatchTask& tk = B.tasks[ti];
+    const TaskView v = task_view(tk, cta);
+    if (v.rows > 0) {
+      const int rb = a & 1;
+      if (!warp_wait(&rfull[rb], (uint32_t)((a >> 1) & 1), abort_flag)) {
+        stop = true;
+        break;
+      }
+      const float* rr = red + rb * (kGroupWarps * kRedRows);
+      // warps holding partials of a row: the whole group, or -- with fewer chunks
+      // than group warps -- the `chunks` warps that own the row's tile
+      const int nsplit = v.chunks >= kGroupWarps ? 1 : kGroupWarps / v.chunks;
+      const int nw = v.chunks >= kGroupWarps ? kGroupWarps : v.chunks;
+      float sums[kRedRows / 32];
+#pragma unroll
+      for (int i = 0; i < kRedRows / 32; ++i) {
+        const int r = lane + 32 * i;
+        sums[i] = 0.f;
+        if (r < v.rows) {
+          const int w0 = ((r >> 4) % nsplit) * nw;
+          for (int w = w0; w < w0 + nw; ++w) sums[i] += rr[w * kRedRows + r];
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[rb]);  // partials consumed: the consumers may refill the buffer
+#pragma unroll
+      for (int i = 0; i < kRedRows / 32; ++i) {
+        const int r = lane + 32 * i;
+        if (r < v.rows) {
+          // optional epilogues; a glu / resid row written by an earlier task of
+          // this batch was stored by this same lane (same N, same row split)
+          half hv = __float2half_rn(sums[i]);
+          if (tk.glu) {
+            const float gv = __half2float(__ldcg(tk.glu + v.row0 + r));
+            hv = __float2half_rn((gv / (1.0f + expf(-gv))) * __half2float(hv));
+          }
+          if (tk.resid) hv = __float2half_rn(__half2float(__ldcg(tk.resid + v.row0 + r)) + __half2float(hv));
+          if (tk.peer) {
+            for (int pr = 0; pr < B.peers.world; ++pr) reinterpret_cast<half*>(s_inbox[pr])[v.row0 + r] = hv;
+          } else {
+            tk.y[v.row0 + r] = hv;
+          }
+        }
+      }
+      ++a;
+    }
+    if (tk.peer) {  // rows pushed: system-visible before this CTA counts itself done (kernel end)
+      __threadfence_system();
+    } else if (tk.publish) {  // a later task reads this y: make it visible GPU-wide, then count this CTA in
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) red_release_add(counters + ti, 1);
+    }
+    __syncwarp();
+  }
+  if (stop) raise_abort(abort_flag);
 }
 
 // 19 warps put 5 warps on some of the SM's four 16K-register partitions:
@@ -266,8 +448,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint64_t full[kMaxItems], empty[kMaxItems];
   __shared__ uint64_t xfull[2], xempty[2], rfull[2], rempty[2];
   __shared__ int item_off[kMaxItems];
-  __shared__ float s_bias[kCWarps][kMaxChunksPerWarp];
+  __shared__ float s_bias[kCWarps][kMaxChunksPerWarp];  // 1.5 KB
   __shared__ int s_abort;
+  __shared__ uint8_t* s_inbox[kMaxPeers];  // peer task: rank r's inbox slot (parity, this rank)
+  __shared__ uint32_t* s_flag[kMaxPeers];  // and its flag for this rank
+  __shared__ uint32_t s_epoch;             // the exchange this launch signals
   volatile int* abort_flag = &s_abort;
 
   const int tid = threadIdx.x;
@@ -287,55 +472,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
     s_abort = 0;
+    if (B.peers.world > 0) {
+      const uint32_t e = peer_next_epoch(B.peers);
+      const int par = (int)(e & 1u);
+      s_epoch = e;
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r) {
+        s_inbox[r] = B.peers.base[r] + kPeerHeaderBytes + ((int64_t)par * B.peers.world + B.peers.rank) * B.peers.slot_bytes;
+        s_flag[r] = reinterpret_cast<uint32_t*>(B.peers.base[r]) + par * kMaxPeers + B.peers.rank;
+      }
+    }
   }
   __syncthreads();
 
   if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    // Ring allocation is FIFO: items are consumed in issue order, so the
-    // occupied bytes are [item_off[oldest], head) circularly.
-    int head = 0, issued = 0, oldest = 0;
-    bool stop = false;
-    for (int ti = 0; ti < B.num && !stop; ++ti) {
-      const GemvBatchTask& tk = B.tasks[ti];
-      const TaskView v = task_view(tk, cta);
-      const int row_bytes = tk.K / 2;
-      const int srow = tk.G * 4;
-      for (int tile0 = 0; tile0 < v.tiles && !stop; tile0 += tk.tiles_per_item) {
-        const int nt = min(tk.tiles_per_item, v.tiles - tile0);
-        const int rows = item_rows(v, tile0, nt);
-        const int wb = rows * row_bytes, sb = rows * srow;
-        const int bytes = round128(wb) + round128(sb);
-        if (head + bytes > B.ring_bytes) head = 0;
-        while (issued > oldest) {
-          const int start = item_off[oldest % kMaxItems];
-          const bool overlap = head <= start && head + bytes > start;
-          if (issued - oldest < kMaxItems && !overlap) break;
-          if (!warp_wait(&empty[oldest % kMaxItems], (uint32_t)((oldest / kMaxItems) & 1), abort_flag)) {
-            stop = true;
-            break;
-          }
-          ++oldest;
-        }
-        if (stop) break;
-        const int d = issued % kMaxItems;
-        __syncwarp();  // every lane has read item_off[] before lane 0 rewrites a slot
-        if (lane == 0) {
-          item_off[d] = head;
-          const int64_t r = v.row0 + tile0 * 16;
-          mbar_arrive_expect_tx(&full[d], (uint32_t)(wb + sb));
-          bulk_g2s(ring + head, tk.W + r * row_bytes, (uint32_t)wb, &full[d]);
-          bulk_g2s(ring + head + round128(wb), tk.S + r * tk.G, (uint32_t)sb, &full[d]);
-        }
-        __syncwarp();
-        head += bytes;
-        ++issued;
-      }
-    }
-    if (stop) raise_abort(abort_flag);
-    // every issued copy must land before this CTA's shared memory is released
-    for (int q = max(oldest, issued - kMaxItems); q < issued; ++q)
-      (void)mbar_wait_bounded(&full[q % kMaxItems], (uint32_t)((q / kMaxItems) & 1), kWaitNs / 4);
+    producer_loop(B, cta, lane, ring, full, empty, item_off, abort_flag);
   } else if (warp == kLoaderWarp) {
     // ------------------------------------------------------------ x loader
     int a = 0;  // index among this CTA's active (rows > 0) tasks
@@ -375,60 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (stop) raise_abort(abort_flag);
     asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into this CTA's shared memory outlives it
   } else if (warp == kEpilogueWarp) {
-    // ------------------------------------------------------------ epilogue
-    int a = 0;
-    bool stop = false;
-    for (int ti = 0; ti < B.num && !stop; ++ti) {
-      const GemvBatchTask& tk = B.tasks[ti];
-      const TaskView v = task_view(tk, cta);
-      if (v.rows > 0) {
-        const int rb = a & 1;
-        if (!warp_wait(&rfull[rb], (uint32_t)((a >> 1) & 1), abort_flag)) {
-          stop = true;
-          break;
-        }
-        const float* rr = red + rb * (kGroupWarps * kRedRows);
-        // warps holding partials of a row: the whole group, or -- with fewer chunks
-        // than group warps -- the `chunks` warps that own the row's tile
-        const int nsplit = v.chunks >= kGroupWarps ? 1 : kGroupWarps / v.chunks;
-        const int nw = v.chunks >= kGroupWarps ? kGroupWarps : v.chunks;
-        float sums[kRedRows / 32];
-#pragma unroll
-        for (int i = 0; i < kRedRows / 32; ++i) {
-          const int r = lane + 32 * i;
-          sums[i] = 0.f;
-          if (r < v.rows) {
-            const int w0 = ((r >> 4) % nsplit) * nw;
-            for (int w = w0; w < w0 + nw; ++w) sums[i] += rr[w * kRedRows + r];
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rempty[rb]);  // partials consumed: the consumers may refill the buffer
-#pragma unroll
-        for (int i = 0; i < kRedRows / 32; ++i) {
-          const int r = lane + 32 * i;
-          if (r < v.rows) {
-            // optional epilogues; a glu / resid row written by an earlier task of
-            // this batch was stored by this same lane (same N, same row split)
-            half hv = __float2half_rn(sums[i]);
-            if (tk.glu) {
-              const float gv = __half2float(__ldcg(tk.glu + v.row0 + r));
-              hv = __float2half_rn((gv / (1.0f + expf(-gv))) * __half2float(hv));
-            }
-            if (tk.resid) hv = __float2half_rn(__half2float(__ldcg(tk.resid + v.row0 + r)) + __half2float(hv));
-            tk.y[v.row0 + r] = hv;
-          }
-        }
-        ++a;
-      }
-      if (tk.publish) {  // a later task reads this y: make it visible GPU-wide, then count this CTA in
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) red_release_add(counters + ti, 1);
-      }
-      __syncwarp();
-    }
-    if (stop) raise_abort(abort_flag);
+    epilogue_loop(B, cta, lane, red, rfull, rempty, s_inbox, counters, abort_flag);
   } else {
     // ------------------------------------------------------------ consumers
     // Two groups of kGroupWarps warps alternate over this CTA's active tasks
@@ -444,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TaskView v = task_view(tk, cta);
       if (v.rows == 0) continue;
       const int tpi = tk.tiles_per_item;
-      const int nitems = (v.tiles + tpi - 1) / tpi;
+      const int nitems = task_items(tk, v);
       if ((a & 1) != group) {  // the other group's task
         item += nitems;
         ++a;
@@ -487,24 +585,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // 1, 2: unrolled (group size 128); 3: rolled, group size 128; 4: rolled, general; 0: idle
       const int kind = nmine == 0 ? 0 : (tk.cpg == 1 ? (nmine <= 2 ? nmine : 3) : 4);
-      for (int tile0 = 0; tile0 < v.tiles; tile0 += tpi) {
-        const int nt = min(tpi, v.tiles - tile0);
-        const int rows = item_rows(v, tile0, nt);
-        const int d = item % kMaxItems;
-        if (!warp_wait(&full[d], (uint32_t)((item / kMaxItems) & 1), abort_flag)) {
-          stop = true;
-          break;
+      if (tk.nsegs == 1) {
+        for (int tile0 = 0; tile0 < v.tiles; tile0 += tpi) {
+          const int nt = min(tpi, v.tiles - tile0);
+          const int rows = item_rows(v, tile0, nt);
+          const int d = item % kMaxItems;
+          if (!warp_wait(&full[d], (uint32_t)((item / kMaxItems) & 1), abort_flag)) {
+            stop = true;
+            break;
+          }
+          const uint8_t* ib = ring + item_off[d];
+          const uint8_t* wbase = ib + c_first * 64 + t * 16;
+          const float* sbase = reinterpret_cast<const float*>(ib + round128(rows * row_bytes));
+          if (kind == 1) consume_tiles<1, true>(ct, wbase, sbase, rows, tile0, nt, 1, false);
+          else if (kind == 2) consume_tiles<2, true>(ct, wbase, sbase, rows, tile0, nt, 2, false);
+          else if (kind == 3) consume_tiles<0, true>(ct, wbase, sbase, rows, tile0, nt, nmine, false);
+          else if (kind == 4) consume_tiles<0, false>(ct, wbase, sbase, rows, tile0, nt, nmine, false);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[d]);
+          ++item;
         }
-        const uint8_t* ib = ring + item_off[d];
-        const uint8_t* wbase = ib + c_first * 64 + t * 16;
-        const float* sbase = reinterpret_cast<const float*>(ib + round128(rows * row_bytes));
-        if (kind == 1) consume_tiles<1, true>(ct, wbase, sbase, rows, tile0, nt, 1);
-        else if (kind == 2) consume_tiles<2, true>(ct, wbase, sbase, rows, tile0, nt, 2);
-        else if (kind == 3) consume_tiles<0, true>(ct, wbase, sbase, rows, tile0, nt, nmine);
-        else if (kind == 4) consume_tiles<0, false>(ct, wbase, sbase, rows, tile0, nt, nmine);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[d]);
-        ++item;
+      } else {
+        // K-segmented task: items are (tile, segment), segments of a tile consecutive; item rows
+        // hold one segment, scale columns are segment-local (the item holds the segment's groups)
+        ct.row_bytes = tk.ks * 64;
+        ct.G = tk.ks / tk.cpg;
+        for (int tile0 = 0; tile0 < v.tiles && !stop; ++tile0) {
+          const int rows = item_rows(v, tile0, 1);
+          for (int seg = 0; seg < tk.nsegs; ++seg) {
+            const int d = item % kMaxItems;
+            if (!warp_wait(&full[d], (uint32_t)((item / kMaxItems) & 1), abort_flag)) {
+              stop = true;
+              break;
+            }
+            const uint8_t* ib = ring + item_off[d];
+            const uint8_t* wbase = ib + c_first * 64 + t * 16;
+            const float* sbase = reinterpret_cast<const float*>(ib + round128(rows * ct.row_bytes));
+            // owned chunks gw + 8j of the segment (ks is a multiple of 8), their x and biases
+            const int nks = min(tk.ks, v.chunks - seg * tk.ks);
+            const int nm = nks > gw ? (nks - gw + kGroupWarps - 1) / kGroupWarps : 0;
+            ct.xq = reinterpret_cast<const uint4*>(xbuf + xs * B.x_bytes) + (c_first + seg * tk.ks) * 16 + t * 4;
+            ct.sbias = s_bias[warp] + seg * (tk.ks / kGroupWarps);
+            if (nm > 0) {
+              if (tk.cpg == 1) consume_tiles<0, true>(ct, wbase, sbase, rows, tile0, 1, nm, seg > 0);
+              else consume_tiles<0, false>(ct, wbase, sbase, rows, tile0, 1, nm, seg > 0);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[d]);
+            ++item;
+          }
+        }
       }
       if (stop) break;
       __syncwarp();
@@ -523,6 +653,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (done == grid - 1) {  // every CTA is past every dependency wait: reset for the next launch
       for (int i = 0; i <= B.num; ++i) atomicExch(counters + i, 0);
       __threadfence();
+      if (B.peers.world > 0) {  // every CTA pushed its rows of the peer task: signal every rank
+        __threadfence_system();
+        for (int pr = 0; pr < B.peers.world; ++pr) st_release_sys_u32(s_flag[pr], s_epoch);
+      }
     }
   }
 }
@@ -536,19 +670,43 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
   for (int i = 0; i < B.num; ++i) B.tasks[i].publish = 0;
   for (int i = 0; i < B.num; ++i)
     if (B.tasks[i].dep >= 0) B.tasks[B.tasks[i].dep].publish = 1;
+  int npeer = 0;
+  B.any_cp_async = 0;
   for (int i = 0; i < B.num; ++i) {
     GemvBatchTask& tk = B.tasks[i];
     tk.rows_per_cta = (tk.N + sms - 1) / sms;
     if (tk.rows_per_cta > kMaxTiles * 16) return false;
-    if (tk.K % 128 != 0 || (tk.G * 4) % 16 != 0 || tk.K / 128 > kGroupWarps * kMaxChunksPerWarp) return false;
+    if (tk.K % 128 != 0 || tk.K / 128 > kGroupWarps * kMaxChunksPerWarp) return false;
+    const int chunks = tk.K / 128;
+    tk.scale_plain = (tk.G * 4) % 16 != 0 ? 1 : 0;
     const int tile_bytes = round128(16 * (tk.K / 2)) + round128(16 * tk.G * 4);
-    if (tile_bytes > kMaxItemBytes) return false;  // rows too long for whole-row items
-    tk.tiles_per_item = kMaxItemBytes / tile_bytes;
+    if (tile_bytes <= kMaxItemBytes) {
+      tk.nsegs = 1;
+      tk.ks = chunks;
+      tk.tiles_per_item = kMaxItemBytes / tile_bytes;
+    } else {
+      // K-segments of ks chunks: whole scale groups, a multiple of the group's warps
+      if (chunks % tk.cpg != 0 || tk.G != chunks / tk.cpg) return false;
+      const int step = kGroupWarps * tk.cpg;
+      int ks = 0;
+      for (int c = step; c <= chunks; c += step)
+        if (round128(16 * c * 64) + round128(16 * (c / tk.cpg) * 4) <= kMaxItemBytes) ks = c;
+      if (ks == 0) return false;
+      tk.ks = ks;
+      tk.nsegs = (chunks + ks - 1) / ks;
+      tk.tiles_per_item = 1;
+      tk.scale_plain = 1;
+    }
+    if (tk.peer) ++npeer;
+    if (tk.scale_plain && !(tk.nsegs > 1 && tk.G % 4 == 0 && (tk.ks / tk.cpg) % 4 == 0 &&
+                            ((chunks - (tk.nsegs - 1) * tk.ks) / tk.cpg) % 4 == 0))
+      B.any_cp_async = 1;  // the producer's seg_bulk test fails for some item of this task
     max_k = tk.K > max_k ? tk.K : max_k;
   }
+  if (npeer > 1 || (npeer == 1 && B.peers.world < 1)) return false;
   B.grid = sms;
   B.x_bytes = round128(max_k * 2);
-  const int static_smem = 2048;  // mbarriers, item offsets, per-warp biases, flags (1 KB used)
+  const int static_smem = 3072;  // mbarriers, item offsets, per-warp biases, flags (~2 KB used)
   B.ring_bytes = ((kSmemLimit - static_smem - 2 * B.x_bytes - kRedBytes - 256) / 128) * 128;
   if (B.ring_bytes < kMaxItemBytes + 128) return false;
   B.smem_bytes = B.ring_bytes + 2 * B.x_bytes + kRedBytes;

@@ -38,6 +38,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
+#include "peer.cuh"
 
 namespace soinfer {
 
@@ -64,6 +65,7 @@ struct BulkPlan {
   int resident;      // 1: every stage of the CTA has its own slot
   int cpg;           // chunks per scale group (group_size / 128)
   int G;             // scale columns per row
+  int scale_simt;    // 1: scale rows are not 16-byte multiples -- staged with plain loads, not bulk copies
   int slot_stride;   // bytes between rows inside a stage slot
   int smem_x, smem_scale, smem_stage, smem_total;
 };
@@ -125,10 +127,13 @@ __device__ __forceinline__ void chunk_dot(const uint4 wa, const uint4 wb, const 
   s1 = e[2] + o[2];
 }
 
-template <RowMode M>
+// PEER: row-parallel tensor-parallel form -- each output row is stored into
+// slot (parity, rank) of every rank's exchange inbox instead of y, and the
+// last CTA to finish (ticket) signals the exchange to every rank.
+template <RowMode M, bool PEER>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_w4_bulk_kernel(const RowSource src, const half* __restrict__ x, half* __restrict__ y, const int nrows,
-                        const int K, const BulkPlan p) {
+                        const int K, const BulkPlan p, const PeerSet ps) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint4* xs = reinterpret_cast<uint4*>(smem);
   float* ss = reinterpret_cast<float*>(smem + p.smem_x);
@@ -175,7 +180,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   if (warp == 0) {
     // scale rows of this CTA (contiguous in plain mode)
-    if constexpr (M == RowMode::kPlain) {
+    if (p.scale_simt) {
+      // staged by all threads below
+    } else if constexpr (M == RowMode::kPlain) {
       if (lane == 0) {
         const uint32_t bytes = (uint32_t)rows_here * scale_row_bytes;
         mbar_arrive_expect_tx(scale_bar, bytes);
@@ -195,13 +202,52 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int s = 0; s < first; ++s) issue(s);
   }
   if constexpr (M == RowMode::kPlain) pdl_wait();
+  uint32_t epoch = 0;
+  int par = 0;
+  if constexpr (PEER) {
+    epoch = peer_next_epoch(ps);
+    par = (int)(epoch & 1u);
+  }
+  auto put = [&](int64_t row, float v) {
+    const half h = __float2half_rn(v);
+    if constexpr (PEER) {
+      for (int r = 0; r < ps.world; ++r) reinterpret_cast<half*>(peer_slot(ps, r, par, ps.rank))[row] = h;
+    } else {
+      y[row] = h;
+    }
+  };
+  // every row stored: the last CTA signals the exchange (PEER only)
+  auto finish = [&]() {
+    if constexpr (PEER) {
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence_system();
+        const unsigned prev = atomicAdd(peer_ticket(ps), 1u);
+        if (prev == gridDim.x - 1) {
+          *peer_ticket(ps) = 0u;
+          __threadfence_system();
+          for (int r = 0; r < ps.world; ++r) st_release_sys_u32(peer_flag(ps, r, par, ps.rank), epoch);
+        }
+      }
+    }
+  };
   // x -> shared memory (L2-coherent loads: x may come from the previous kernel)
   {
     const uint4* xg = reinterpret_cast<const uint4*>(x);
     const int n16 = K / 8;
     for (int i = tid; i < n16; i += kThreads) xs[x_slot(i)] = __ldcg(xg + i);
   }
-  const bool scales_ok = mbar_wait_bounded(scale_bar, 0, kWaitNs);
+  if (p.scale_simt) {
+    // (tensor-parallel shards: e.g. 10 or 17 groups per row) -- made visible by the barrier below
+    for (int i = tid; i < rows_here * p.G; i += kThreads) {
+      const int r = i / p.G, gi = i - r * p.G;
+      const uint8_t* w;
+      const float* sc;
+      row_ptrs<M>(src, row_begin + r, w, sc);
+      ss[i] = __ldg(sc + gi);
+    }
+  }
+  const bool scales_ok = p.scale_simt ? true : mbar_wait_bounded(scale_bar, 0, kWaitNs);
   const int lr0 = g, lr1 = g + 8;
 
   if (p.resident) {
@@ -252,8 +298,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += red[w * (kMaxTiles * 16) + r];
-      y[row_begin + r] = __float2half_rn(sum);
+      put(row_begin + r, sum);
     }
+    finish();
     return;
   }
 
@@ -308,13 +355,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += red[w * 16 + tid];
       const int lr = tile * 16 + tid;
-      if (lr < rows_here) y[row_begin + lr] = __float2half_rn(sum);
+      if (lr < rows_here) put(row_begin + lr, sum);
     }
     if (warp == 0 && s + p.stages < total) {
       fence_proxy_async_smem();
       issue(s + p.stages);
     }
   }
+  finish();
 }
 
 // Generic path: any group_size % 8 == 0, any K, 4-byte aligned rows.
@@ -375,6 +423,7 @@ bool make_plan(int64_t nrows, int64_t K, int64_t gsz, int64_t G, BulkPlan& p, in
   p.chunks = (int)(K / 128);
   p.cpg = (int)(gsz / 128);
   p.G = (int)G;
+  p.scale_simt = (G * 4) % 16 != 0 ? 1 : 0;
   p.piece_chunks = p.chunks < kMaxPieceChunks ? p.chunks : kMaxPieceChunks;
   p.pieces = (p.chunks + p.piece_chunks - 1) / p.piece_chunks;
   p.slot_stride = p.piece_chunks * 64 + kSlotPad;
@@ -390,25 +439,36 @@ bool make_plan(int64_t nrows, int64_t K, int64_t gsz, int64_t G, BulkPlan& p, in
 }
 
 template <RowMode M>
+bool bulk_ok(const RowSource& src, const half* x, int64_t nrows, int64_t K, int64_t gsz, BulkPlan& plan, int& grid) {
+  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return (K % 128 == 0) && (gsz % 128 == 0) && src.row_bytes % 16 == 0 && aligned16(src.W) &&
+         (M != RowMode::kDesc || aligned16(src.W2)) && aligned16(x) && nrows < (1ll << 31) &&
+         (((src.num_groups * 4) % 16 == 0 && aligned16(src.S) && (M != RowMode::kDesc || aligned16(src.S2))) ||
+          ((src.num_groups * 4) % 16 != 0 && (reinterpret_cast<uintptr_t>(src.S) & 3u) == 0)) &&
+         K < (1ll << 30) && make_plan(nrows, K, gsz, src.num_groups, plan, grid);
+}
+
+template <RowMode M, bool PEER>
+cudaError_t launch_bulk(const RowSource& src, const half* x, half* y, int64_t nrows, int64_t K, const BulkPlan& plan,
+                        int grid, const PeerSet& ps, cudaStream_t stream, bool pdl) {
+  auto kernel = gemv_w4_bulk_kernel<M, PEER>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  return launch_ex(kernel, dim3(grid), dim3(kThreads), (size_t)plan.smem_total, stream, 1, pdl, src, x, y,
+                   (int)nrows, (int)K, plan, ps);
+}
+
+template <RowMode M>
 cudaError_t launch_mode(const RowSource& src, const half* x, half* y, int64_t nrows, int64_t K, int64_t gsz,
                         cudaStream_t stream, LaunchOpts opts) {
-  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   BulkPlan plan;
   int grid = 0;
-  const bool fast = (K % 128 == 0) && (gsz % 128 == 0) && src.row_bytes % 16 == 0 && aligned16(src.W) &&
-                    (M != RowMode::kDesc || aligned16(src.W2)) && aligned16(x) && nrows < (1ll << 31) &&
-                    (src.num_groups * 4) % 16 == 0 && aligned16(src.S) && (M != RowMode::kDesc || aligned16(src.S2)) &&
-                    K < (1ll << 30) && make_plan(nrows, K, gsz, src.num_groups, plan, grid);
-  if (fast) {
-    auto kernel = gemv_w4_bulk_kernel<M>;
-    static bool attr_set[3] = {false, false, false};
-    if (!attr_set[(int)M]) {
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      if (e != cudaSuccess) return e;
-      attr_set[(int)M] = true;
-    }
-    return launch_ex(kernel, dim3(grid), dim3(kThreads), (size_t)plan.smem_total, stream, 1, opts.pdl, src, x, y,
-                     (int)nrows, (int)K, plan);
+  if (bulk_ok<M>(src, x, nrows, K, gsz, plan, grid)) {
+    return launch_bulk<M, false>(src, x, y, nrows, K, plan, grid, PeerSet{}, stream, opts.pdl);
   }
   const int64_t blocks = (nrows + 3) / 4;
   return launch_ex(gemv_w4_simt_kernel<M>, dim3((unsigned)blocks), dim3(128), 0, stream, 1, opts.pdl, src, x, y,
@@ -428,6 +488,14 @@ cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, ha
       return launch_mode<RowMode::kDesc>(src, x, y, nrows, K, group_size, stream, opts);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_w4_peer(const RowSource& src, const half* x, int64_t nrows, int64_t K, int64_t group_size,
+                                const PeerSet& ps, cudaStream_t stream) {
+  BulkPlan plan;
+  int grid = 0;
+  if (!bulk_ok<RowMode::kPlain>(src, x, nrows, K, group_size, plan, grid)) return cudaErrorNotSupported;
+  return launch_bulk<RowMode::kPlain, true>(src, x, nullptr, nrows, K, plan, grid, ps, stream, false);
 }
 
 cudaError_t read_and_clear_gemv_w4_error(int* out) {

@@ -23,6 +23,18 @@ struct RowSource {
   int64_t num_groups = 0;       // scale columns per row
 };
 
+// Tensor-parallel peer exchange (peer.cuh has the buffer layout and protocol).
+constexpr int kMaxPeers = 8;
+constexpr int64_t kPeerHeaderBytes = 256;
+struct PeerSet {
+  uint8_t* base[kMaxPeers];  // every rank's exchange buffer as mapped in this process (own at [rank])
+  int rank, world;
+  int64_t slot_bytes;        // one inbox slot (multiple of 16)
+};
+inline int64_t peer_buffer_bytes(int64_t slot_bytes, int world) {
+  return kPeerHeaderBytes + 2 * (int64_t)world * slot_bytes;
+}
+
 struct LaunchOpts {
   bool pdl = false;  // programmatic dependent launch (weights not produced by the previous kernel)
 };
@@ -34,6 +46,30 @@ cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, ha
 // Reads and clears the INT4 GEMV module's device error bits (DeviceError).
 cudaError_t read_and_clear_gemv_w4_error(int* out);
 
+// Row-parallel INT4 GEMV whose output rows go straight into every rank's
+// inbox slot of the next exchange (peer stores over NVLink); the last CTA
+// signals the exchange.  Finish it with launch_tp_allreduce_norm(partial =
+// nullptr).  Needs the bulk-path layout (K, group size multiples of 128,
+// 16-byte aligned rows); returns cudaErrorNotSupported otherwise.
+cudaError_t launch_gemv_w4_peer(const RowSource& src, const half* x, int64_t nrows, int64_t K, int64_t group_size,
+                                const PeerSet& ps, cudaStream_t stream);
+
+// Exchanges (tp_comm.cu), one CTA each:
+// all-reduce of fp16 [n] partials (summed in fp32 in rank order, rounded
+// once), then out_sum = fp16(residual + sum) (residual optional) and, if
+// out_norm, out_norm = rmsnorm(out_sum) * w.  partial == nullptr: the data was
+// already pushed and signalled by launch_gemv_w4_peer.
+cudaError_t launch_tp_allreduce_norm(const PeerSet& ps, const half* partial, const half* residual, const half* w,
+                                     half* out_sum, half* out_norm, int64_t n, float eps, cudaStream_t stream);
+// out [world * nbytes] = every rank's `local` [nbytes] in rank order.
+cudaError_t launch_tp_allgather(const PeerSet& ps, const void* local, int64_t nbytes, void* out, cudaStream_t stream);
+// Global greedy token of a vocabulary-parallel LM head: every rank's
+// (logits[local_idx], local_idx + offset), the largest fp16 logit, ties to the
+// lowest global index; out_idx int32 [1].
+cudaError_t launch_tp_argmax(const PeerSet& ps, const half* logits, const int32_t* local_idx, int64_t offset,
+                             int32_t* out_idx, cudaStream_t stream);
+cudaError_t read_and_clear_tp_error(int* out);
+
 // Persistent batched INT4 GEMV (gemv_batch.cu).  Tasks run in order; a task
 // with dep >= 0 reads x only after every CTA finished task `dep`.
 struct GemvBatchTask {
@@ -42,13 +78,19 @@ struct GemvBatchTask {
   const half* x;
   half* y;
   int N, K, G, cpg, dep;
-  int rows_per_cta, tiles_per_item, publish;  // filled by plan_gemv_batch (publish: a later task depends on it)
+  // filled by plan_gemv_batch: rows per CTA, 16-row tiles per item, publish (a later task depends on it),
+  // ks / nsegs (K split into segments of ks 128-chunks when a 16-row tile is too long for one item),
+  // scale_plain (scale rows staged by plain loads: not 16-byte rows, or segmented)
+  int rows_per_cta, tiles_per_item, publish, ks, nsegs, scale_plain;
   const half* resid;  // optional epilogue: y = fp16(resid + fp16(dot))
   const half* glu;    // optional epilogue: y = fp16(silu(glu) * fp16(dot)), applied before resid
+  int peer;           // y == nullptr: rows go to every rank's exchange inbox (PeerSet), the last CTA signals
 };
 constexpr int kMaxBatchTasks = 256;
 struct GemvBatchParams {
   int num, grid, x_bytes, ring_bytes, smem_bytes;
+  int any_cp_async;  // some task stages scales with cp.async (proxy fence before later bulk copies)
+  PeerSet peers;  // used by a peer task (at most one per batch)
   GemvBatchTask tasks[kMaxBatchTasks];
 };
 int64_t gemv_batch_workspace_bytes(int64_t num_tasks);

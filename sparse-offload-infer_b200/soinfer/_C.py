@@ -69,6 +69,16 @@ _SIGNATURES = {
     "soinfer_rope_apply_at": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
+    "soinfer_peer_buffer_bytes": (_I64, [_I64, ctypes.c_int32]),
+    "soinfer_peer_buffer_create": (_INT, [_I64, _P, _P]),
+    "soinfer_peer_buffer_open": (_INT, [_P, _P]),
+    "soinfer_peer_buffer_close": (_INT, [_P]),
+    "soinfer_peer_buffer_destroy": (_INT, [_P]),
+    "soinfer_tp_allreduce_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _F32, _P]),
+    "soinfer_gemv_w4a16_tp_partial": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "soinfer_gemv_w4a16_batch_tp": (_INT, [_P, _P, _I64, _P, _I64, _P]),
+    "soinfer_tp_allgather": (_INT, [_P, _P, _I64, _P, _P]),
+    "soinfer_tp_argmax": (_INT, [_P, _P, _P, _I64, _P, _P]),
 }
 
 
@@ -275,9 +285,12 @@ class GemvBatch:
     dep = index of an earlier task whose output feeds this task's x, or -1;
     residual / glu_gate (fp16 [N] or None) add the epilogues
     y = residual + fp16(silu(glu_gate) * fp16(W x)) of the C ABI.  The tensors
-    must stay alive and keep their storage while the batch is used."""
+    must stay alive and keep their storage while the batch is used.
+    peers (a PeerSetStruct): tensor-parallel batch (soinfer_gemv_w4a16_batch_tp)
+    in which one task may have y = None -- its rows go to every rank's
+    exchange inbox."""
 
-    def __init__(self, tasks):
+    def __init__(self, tasks, peers=None):
         n = len(tasks)
         _check(0 < n <= MAX_BATCH_TASKS, "gemv_w4a16_batch: 1 ..", MAX_BATCH_TASKS, " tasks")
         arr = (_GemvTask * n)()
@@ -294,32 +307,40 @@ class GemvBatch:
             _check(scale.dim() == 2 and scale.size(0) == W.size(0), name, ": scale must be 2D [N, num_groups]")
             _f16(x, name + "(x)")
             _check(x.numel() == K, name, ": x must hold K values")
-            _f16(y, name + "(y)")
-            _check(y.numel() == W.size(0), name, ": y must hold N values")
+            if y is None:
+                _check(peers is not None, name, ": y may be None only in a tensor-parallel batch (peers)")
+            else:
+                _f16(y, name + "(y)")
+                _check(y.numel() == W.size(0), name, ": y must hold N values")
             _check(-1 <= dep < i, name, ": dep must be -1 or an earlier task index")
             for e, en in ((residual, "residual"), (glu, "glu_gate")):
                 if e is not None:
                     _f16(e, f"{name}({en})")
                     _check(e.numel() == W.size(0) and e.is_contiguous(), name, f": {en} must hold N values")
-            d = _same_device(W, scale, x, y)
+            d = _same_device(W, scale, x, *([y] if y is not None else []))
             _check(dev is None or d == dev, name, ": all tasks must be on one device")
             dev = d
-            arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), y.data_ptr(), W.size(0), K, group_size,
+            arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), _ptr(y), W.size(0), K, group_size,
                                scale.size(1), dep, _ptr(residual), _ptr(glu))
         self._arr, self.n, self.device = arr, n, dev
         self._keep = [tuple(t) for t in tasks]
+        self.peers = peers
 
     def run(self) -> None:
         dev = self.device
         with torch.cuda.device(dev):
             ws = _workspace("batch", dev, lib().soinfer_gemv_batch_workspace_bytes(self.n))
-            _call("soinfer_gemv_w4a16_batch", ctypes.addressof(self._arr), self.n, ws.data_ptr(), ws.numel(),
-                  _stream(dev))
+            if self.peers is None:
+                _call("soinfer_gemv_w4a16_batch", ctypes.addressof(self._arr), self.n, ws.data_ptr(), ws.numel(),
+                      _stream(dev))
+            else:
+                _call("soinfer_gemv_w4a16_batch_tp", ctypes.byref(self.peers), ctypes.addressof(self._arr), self.n,
+                      ws.data_ptr(), ws.numel(), _stream(dev))
 
 
-def gemv_w4a16_batch(tasks) -> None:
+def gemv_w4a16_batch(tasks, peers=None) -> None:
     """Runs the tasks (see GemvBatch) as one persistent kernel on the current stream."""
-    GemvBatch(tasks).run()
+    GemvBatch(tasks, peers).run()
 
 
 def reset_workspaces() -> None:
@@ -819,3 +840,92 @@ def decode_attention(q, k_cache, v_cache, cur_len: int, out: torch.Tensor | None
         _call("soinfer_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(y), nq, nkv, max_seq, hd,
               cur_len, ws.data_ptr(), ws.numel(), _stream(dev))
     return y
+
+
+# ------------------------------------------------------------ tensor-parallel exchange
+IPC_HANDLE_BYTES = 64
+MAX_PEERS = 8
+
+
+class PeerSetStruct(ctypes.Structure):
+    _fields_ = [("base", _P * MAX_PEERS), ("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("slot_bytes", _I64)]
+
+
+def peer_buffer_bytes(slot_bytes: int, world: int) -> int:
+    n = lib().soinfer_peer_buffer_bytes(slot_bytes, world)
+    _check(n > 0, "peer_buffer_bytes: slot_bytes must be a positive multiple of 16 and world in [1, 8]")
+    return n
+
+
+def peer_buffer_create(nbytes: int, device) -> tuple[int, bytes]:
+    """A zeroed device buffer for peer exchange on `device` and its CUDA IPC handle."""
+    ptr = _P()
+    handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _call("soinfer_peer_buffer_create", nbytes, ctypes.byref(ptr), handle)
+    return ptr.value, handle.raw
+
+
+def peer_buffer_open(handle: bytes, device) -> int:
+    """Maps another process's exchange buffer (its IPC handle) into this one."""
+    _check(len(handle) == IPC_HANDLE_BYTES, "peer_buffer_open: handle must be 64 bytes")
+    ptr = _P()
+    with torch.cuda.device(device):
+        _call("soinfer_peer_buffer_open", ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr))
+    return ptr.value
+
+
+def peer_buffer_close(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        _call("soinfer_peer_buffer_close", ptr)
+
+
+def peer_buffer_destroy(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        _call("soinfer_peer_buffer_destroy", ptr)
+
+
+def tp_allreduce_add_rmsnorm(peers: PeerSetStruct, partial, residual, weight, out_sum, out_norm, eps: float,
+                             device) -> None:
+    """See soinfer_tp_allreduce_add_rmsnorm (partial None: pushed by gemv_w4a16_tp_partial)."""
+    n = out_sum.numel()
+    for t, nm in ((partial, "partial"), (residual, "residual"), (out_norm, "out_norm")):
+        if t is not None:
+            _f16(t, f"tp_allreduce_add_rmsnorm({nm})")
+            _check(t.numel() == n and t.device == device, f"tp_allreduce_add_rmsnorm: {nm} must match out_sum")
+    with torch.cuda.device(device):
+        _call("soinfer_tp_allreduce_add_rmsnorm", ctypes.byref(peers), _ptr(partial), _ptr(residual), _ptr(weight),
+              _ptr(out_sum), _ptr(out_norm), n, eps, _stream(device))
+
+
+def gemv_w4a16_tp_partial(peers: PeerSetStruct, Wq_packed, scale, x, K: int, group_size: int) -> None:
+    """Row-parallel INT4 GEMV whose rows go to every rank's exchange inbox."""
+    name = "gemv_w4a16_tp_partial"
+    _check(Wq_packed.is_cuda and Wq_packed.dtype == torch.uint8 and Wq_packed.is_contiguous() and Wq_packed.dim() == 2,
+           name, "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
+    _f32(scale, name + "(scale)")
+    _f16(x, name + "(x)")
+    _check(x.dim() == 1 and x.size(0) == K, name, ": x must be 1D [K]")
+    dev = _same_device(Wq_packed, scale, x)
+    with torch.cuda.device(dev):
+        _call("soinfer_gemv_w4a16_tp_partial", ctypes.byref(peers), _ptr(Wq_packed), _ptr(scale), _ptr(x),
+              Wq_packed.size(0), K, group_size, scale.size(1), _stream(dev))
+
+
+def tp_allgather(peers: PeerSetStruct, local, out) -> None:
+    _check(local.is_cuda and local.is_contiguous() and out.is_contiguous(), "tp_allgather: contiguous CUDA tensors")
+    nbytes = local.numel() * local.element_size()
+    _check(out.numel() * out.element_size() == nbytes * peers.world, "tp_allgather: out must be world x local")
+    with torch.cuda.device(local.device):
+        _call("soinfer_tp_allgather", ctypes.byref(peers), _ptr(local), nbytes, _ptr(out), _stream(local.device))
+
+
+def tp_argmax(peers: PeerSetStruct, logits, local_idx, offset: int, out_idx) -> None:
+    _f16(logits, "tp_argmax(logits)")
+    _check_cuda(local_idx, "tp_argmax(local_idx)", torch.int32, ": must be int32")
+    _check_cuda(out_idx, "tp_argmax(out_idx)", torch.int32, ": must be int32")
+    dev = _same_device(logits, local_idx, out_idx)
+    with torch.cuda.device(dev):
+        _call("soinfer_tp_argmax", ctypes.byref(peers), _ptr(logits), _ptr(local_idx), offset, _ptr(out_idx),
+              _stream(dev))

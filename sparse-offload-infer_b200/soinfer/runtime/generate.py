@@ -140,6 +140,16 @@ class WeightPipeline:
         self.cur_buf, self.cur_name = nxt, name_next
         return y
 
+    def next_resident(self) -> tuple[torch.Tensor, LoadedMatrix]:
+        """The HBM-resident weight in flight and its matrix record, consumed
+        (the caller runs its own kernel on it)."""
+        name = self.cur_name
+        if not self.model.is_resident(name):
+            raise ValueError(f"{name} is not resident in HBM")
+        self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
+        self._prefetch_into(self.cur_buf, self.cur_name)
+        return self.model.resident[name], self.model.matrices[name]
+
     def next_gemvs(self, x_in: torch.Tensor, count: int) -> list[torch.Tensor]:
         """The next `count` GEMVs, all on the same input.  When they are all
         HBM-resident they run as one persistent batched launch (one kernel for
@@ -212,17 +222,20 @@ class DevicePosition:
 
 
 def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
-                     k_cache: torch.Tensor, v_cache: torch.Tensor,
-                     reduce_o=None) -> tuple[torch.Tensor, torch.Tensor]:
+                     k_cache: torch.Tensor, v_cache: torch.Tensor, reduce_o=None, h_in: torch.Tensor | None = None,
+                     o_block=None) -> tuple[torch.Tensor, torch.Tensor]:
     """rmsnorm -> q/k/v GEMVs -> q/k norm + RoPE + KV append (one kernel) ->
     GQA decode attention -> o GEMV -> residual add + post-attention rmsnorm
-    (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2)).  reduce_o maps the
-    o GEMV output before the residual (the cross-rank sum of row-parallel
-    partials under tensor parallelism)."""
+    (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2)).  Tensor-parallel
+    hooks: reduce_o maps the o GEMV output before the residual (the cross-rank
+    sum of row-parallel partials); h_in is rmsnorm(x) when already computed;
+    o_block(attn, x, post_norm_weight, eps) -> (h2, h3) replaces the o GEMV,
+    the residual add and the rmsnorm (it consumes the o weight from the
+    pipeline itself)."""
     NQ, NKV, HD = model.num_attention_heads, model.num_key_value_heads, model.head_dim
     eps = model.rms_norm_eps
     norms = model.layer_norms[layer_idx]
-    h = ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
+    h = h_in if h_in is not None else ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
     q, k, v = pipeline.next_gemvs(h, 3)
     q, k, v = q.view(NQ, HD), k.view(NKV, HD), v.view(NKV, HD)
     if isinstance(pos, DevicePosition):
@@ -234,6 +247,8 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
         ops.head_norm_rope(q, k, v, norms["q_norm"], norms["k_norm"], cos_vals, sin_vals, k_cache, v_cache, pos=pos,
                            eps=eps)
         attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
+    if o_block is not None:
+        return o_block(attn, x_flat, norms["post_attention_layernorm"], eps)
     o = pipeline.next_gemv(attn)
     if reduce_o is not None:
         o = reduce_o(o)
@@ -503,6 +518,8 @@ class GraphDecoder:
         self.pos.add_(1)
 
     def _capture(self) -> None:
+        # the buffers, caches and weights were made on the caller's stream
+        self.stream.wait_stream(torch.cuda.current_stream(self.model.device))
         with torch.cuda.stream(self.stream):
             self.pos.zero_()
             self._step()  # warm-up: workspaces and lazy initialisation outside the capture
@@ -520,6 +537,7 @@ class GraphDecoder:
             raise ValueError(f"need 1 <= prompt length and prompt + n_new <= max_seq_len ({self.max_seq_len})")
         if self.graph is None:
             self._capture()
+        self.stream.wait_stream(torch.cuda.current_stream(self.model.device))
         with torch.cuda.stream(self.stream):
             self.ids.zero_()
             self.ids[:P].copy_(torch.tensor(prompt_ids, dtype=torch.int32), non_blocking=False)

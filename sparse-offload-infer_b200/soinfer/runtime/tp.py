@@ -23,6 +23,14 @@ not bit identity).
 
 The shard plan is host logic (tested on CPU with gloo); the rank model is a
 StreamingModel of shard matrices and runs through the same kernels.
+
+Collectives: with a PeerExchange (the default for GPU decode) they are this
+library's own kernels over peer memory -- the row-parallel GEMV stores its
+fp16 output rows straight into every rank's inbox over NVLink and signals
+them, and one exchange kernel sums the ranks' rows, adds the residual and
+applies the following RMSNorm; the greedy token is agreed by one exchange
+kernel.  Without one, torch.distributed collectives (NCCL, or gloo on CPU)
+do the same steps.
 """
 from __future__ import annotations
 
@@ -183,6 +191,108 @@ def build_tp_model(arch, plan: ShardPlan, seed: int = 0, group_size: int = 128, 
                           group_size=group_size, resident=resident)
 
 
+class PeerExchange:
+    """Peer-memory exchange among the ranks of `group` (one process per GPU,
+    every rank on its own device of one node).  Creates this rank's exchange
+    buffer, trades CUDA IPC handles with an all_gather_object, and maps every
+    peer's buffer; all ranks must then issue the same sequence of exchange
+    calls (each call is one or two kernels on the current stream).
+    slot_bytes bounds the payload of one rank (fp16 hidden vector, gate
+    shard, ...)."""
+
+    def __init__(self, group=None, slot_bytes: int = 64 * 1024, device=None):
+        import torch.distributed as dist
+
+        from .. import _C
+
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > _C.MAX_PEERS:
+            raise ValueError(f"at most {_C.MAX_PEERS} ranks per exchange")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.slot_bytes = slot_bytes
+        self._own, handle = _C.peer_buffer_create(_C.peer_buffer_bytes(slot_bytes, self.world), self.device)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self._mapped = []
+        self.peers = _C.PeerSetStruct()
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.peers.base[r] = self._own
+            else:
+                p = _C.peer_buffer_open(h, self.device)
+                self._mapped.append(p)
+                self.peers.base[r] = p
+        self.peers.rank, self.peers.world, self.peers.slot_bytes = self.rank, self.world, slot_bytes
+        self._next_normed = None  # (x, rmsnorm(x)) left by the last fused all-reduce for the next layer
+        dist.barrier(group=group)
+
+    def allreduce_add_rmsnorm(self, partial, residual=None, weight=None, eps: float = 1e-6):
+        """(out_norm or None, out_sum): out_sum = fp16(residual + sum of the ranks' partials)."""
+        from .. import _C
+
+        out_sum = torch.empty_like(partial)
+        out_norm = torch.empty_like(partial) if weight is not None else None
+        _C.tp_allreduce_add_rmsnorm(self.peers, partial, residual, weight, out_sum, out_norm, eps, self.device)
+        return out_norm, out_sum
+
+    def row_parallel(self, W, scale, x, n: int, group_size: int, residual=None, weight=None, eps: float = 1e-6,
+                     before=()):
+        """Row-parallel INT4 GEMV + all-reduce (+ residual, + RMSNorm): one
+        persistent batched launch whose last task (this GEMV) pushes its rows
+        to every rank -- `before` are batch tasks (GemvBatch tuples) run ahead
+        of it in the same launch, and x may be one of their outputs (the GEMV
+        then depends on the task producing it) -- then one exchange kernel
+        finishes.  Returns (out_norm or None, out_sum) like
+        allreduce_add_rmsnorm."""
+        from .. import _C
+
+        before = list(before)
+        dep = next((i for i, t in enumerate(before) if t[3] is x), -1)
+        _C.gemv_w4a16_batch(before + [(W, scale, x, None, x.numel(), group_size, dep)], self.peers)
+        return self.finish(n, residual, weight, eps)
+
+    def finish(self, n: int, residual=None, weight=None, eps: float = 1e-6):
+        """The exchange after a launch that pushed the partial rows (row_parallel)."""
+        from .. import _C
+
+        out_sum = torch.empty(n, dtype=torch.float16, device=self.device)
+        out_norm = torch.empty_like(out_sum) if weight is not None else None
+        _C.tp_allreduce_add_rmsnorm(self.peers, None, residual, weight, out_sum, out_norm, eps, self.device)
+        return out_norm, out_sum
+
+    def allgather(self, local: torch.Tensor) -> torch.Tensor:
+        from .. import _C
+
+        out = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        _C.tp_allgather(self.peers, local.contiguous(), out)
+        return out
+
+    def argmax(self, logits: torch.Tensor, local_idx: torch.Tensor, offset: int) -> torch.Tensor:
+        from .. import _C
+
+        out = torch.empty(1, dtype=torch.int32, device=logits.device)
+        _C.tp_argmax(self.peers, logits, local_idx, offset, out)
+        return out
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective: every rank calls it)."""
+        import torch.distributed as dist
+
+        from .. import _C
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._mapped:
+            _C.peer_buffer_close(p, self.device)
+        self._mapped = []
+        dist.barrier(group=self.group)
+        _C.peer_buffer_destroy(self._own, self.device)
+        self._own = None
+
+
 def all_reduce_sum(partial: torch.Tensor, group=None) -> torch.Tensor:
     """Sum of the ranks' fp16 partial vectors, accumulated in fp32, rounded once."""
     import torch.distributed as dist
@@ -192,46 +302,79 @@ def all_reduce_sum(partial: torch.Tensor, group=None) -> torch.Tensor:
     return f.half()
 
 
-def run_decoder_layer_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, group=None):
+def run_decoder_layer_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, group=None, exchange=None):
     """Dense decoder layer on this rank's shard: local q / k / v heads and
     attention, row-parallel o_proj partial + all-reduce, residual + rmsnorm,
-    local gate / up (SwiGLU), row-parallel down partial + all-reduce, residual."""
-    from .. import ops
+    local gate / up (SwiGLU), row-parallel down partial + all-reduce, residual.
+    With a PeerExchange each row-parallel GEMV and its all-reduce, residual
+    and following RMSNorm (post-attention, or the next layer's input norm)
+    are two kernels -- the MLP's gate / up / down one launch plus the
+    exchange -- and the next layer picks up its normed input."""
     from .generate import _attention_block
 
-    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache,
-                              reduce_o=lambda o: all_reduce_sum(o, group))
-    down = pipeline.next_gemv(pipeline.next_glu(h3))
-    return h2 + all_reduce_sum(down, group)
+    if exchange is None:
+        h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache,
+                                  reduce_o=lambda o: all_reduce_sum(o, group))
+        down = pipeline.next_gemv(pipeline.next_glu(h3))
+        return h2 + all_reduce_sum(down, group)
+
+    g = model.group_size
+
+    def o_block(attn, x, post_w, eps):
+        W, m = pipeline.next_resident()
+        h3, h2 = exchange.row_parallel(W, m.scale, attn, model.hidden_size, g, residual=x, weight=post_w, eps=eps)
+        return h2, h3
+
+    prev = exchange._next_normed
+    h_in = prev[1] if prev is not None and prev[0] is x_flat else None
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, h_in=h_in, o_block=o_block)
+    # MLP: gate, up (SwiGLU epilogue) and the row-parallel down in one launch, then the exchange
+    (Wg, mg), (Wu, mu), (Wd, md) = (pipeline.next_resident() for _ in range(3))
+    gate = torch.empty(mg.n, dtype=torch.float16, device=h3.device)
+    hidden = torch.empty(mu.n, dtype=torch.float16, device=h3.device)
+    nxt = layer_idx + 1
+    w_next = model.layer_norms[nxt]["input_layernorm"] if nxt < model.num_layers else None
+    h_next, out = exchange.row_parallel(Wd, md.scale, hidden, model.hidden_size, g, residual=h2, weight=w_next,
+                                        eps=model.rms_norm_eps,
+                                        before=[(Wg, mg.scale, h3, gate, mg.packed_k, g, -1),
+                                                (Wu, mu.scale, h3, hidden, mu.packed_k, g, -1, None, gate)])
+    exchange._next_normed = (out, h_next) if h_next is not None else None
+    return out
 
 
-def tp_next_token(model, xn: torch.Tensor, plan: ShardPlan, group=None) -> torch.Tensor:
+def tp_next_token(model, xn: torch.Tensor, plan: ShardPlan, group=None, exchange=None) -> torch.Tensor:
     """Greedy token over the vocabulary-parallel LM head: each rank's fused
-    argmax of its rows, then agree_argmax across ranks."""
+    argmax of its rows, then the ranks agree (exchange kernel, or
+    agree_argmax's all-gather)."""
     from .. import _C
 
     idx, logits = _C.gemv_fp16_argmax(model.lm_head, xn, logits=True)
+    if exchange is not None:
+        return exchange.argmax(logits, idx, plan.vocab_rows[0])
     return agree_argmax(logits.index_select(0, idx.long()), idx, plan.vocab_rows[0], group)
 
 
-def generate_tp(model, plan: ShardPlan, prompt_ids: list[int], n_new: int, group=None, max_seq_len: int = 512):
+def generate_tp(model, plan: ShardPlan, prompt_ids: list[int], n_new: int, group=None, max_seq_len: int = 512,
+                exchange=None):
     """Eager greedy decode of the TP model (every rank returns the same ids)."""
     from .generate import WeightPipeline, _greedy
 
     pipeline = WeightPipeline(model)
     return _greedy(model, prompt_ids, n_new,
-                   lambda li, x, p, kc, vc: run_decoder_layer_tp(pipeline, model, li, x, p, kc, vc, group),
-                   None, max_seq_len, token_fn=lambda m, xn: tp_next_token(m, xn, plan, group))
+                   lambda li, x, p, kc, vc: run_decoder_layer_tp(pipeline, model, li, x, p, kc, vc, group, exchange),
+                   None, max_seq_len, token_fn=lambda m, xn: tp_next_token(m, xn, plan, group, exchange))
 
 
-def graph_decoder_tp(model, plan: ShardPlan, group=None, max_seq_len: int = 2048):
-    """GraphDecoder whose captured step is the TP layer stack (NCCL collectives inside the graph)."""
+def graph_decoder_tp(model, plan: ShardPlan, group=None, max_seq_len: int = 2048, exchange=None):
+    """GraphDecoder whose captured step is the TP layer stack (the exchange
+    kernels, or NCCL collectives, inside the graph)."""
     from .generate import GraphDecoder
 
     return GraphDecoder(model, max_seq_len=max_seq_len,
-                        layer_fn=lambda p, m, li, x, w, kc, vc: run_decoder_layer_tp(p, m, li, x, w, kc, vc, group),
-                        token_fn=lambda m, xn: tp_next_token(m, xn, plan, group))
+                        layer_fn=lambda p, m, li, x, w, kc, vc: run_decoder_layer_tp(p, m, li, x, w, kc, vc, group,
+                                                                                     exchange),
+                        token_fn=lambda m, xn: tp_next_token(m, xn, plan, group, exchange))
 
 
-__all__ = ["ShardPlan", "shard_packed", "agree_argmax", "build_tp_model", "all_reduce_sum", "run_decoder_layer_tp",
-           "tp_next_token", "generate_tp", "graph_decoder_tp"]
+__all__ = ["ShardPlan", "shard_packed", "agree_argmax", "build_tp_model", "PeerExchange", "all_reduce_sum",
+           "run_decoder_layer_tp", "tp_next_token", "generate_tp", "graph_decoder_tp"]

@@ -41,6 +41,33 @@ def test_independent_tasks_match_oracle(shapes):
         assert_close(t[3], refs[i], f"batch task {i} {shapes[i]}")
 
 
+@pytest.mark.parametrize("shapes,g", [
+    # tensor-parallel shards of the 14B layer: K-segmented down_proj (TP 1 / 2), scale rows of
+    # 17, 10, 5 groups (not 16-byte rows: staged by plain loads)
+    ([(5120, 17408), (5120, 8704), (5120, 2176), (5120, 1280), (5120, 640)], 128),
+    ([(2048, 17408), (1000, 8192)], 256),   # segments of whole 256-groups
+    ([(4352, 5120), (17, 8704)], 128),      # gate/up shard at TP 4 next to a ragged segmented task
+])
+def test_segmented_and_unaligned_scale_tasks_match_oracle(shapes, g):
+    tasks, refs = [], []
+    for i, (n, k) in enumerate(shapes):
+        p, s, pk = int4_weights(n, k, g, seed=40 + i)
+        x = fp16_randn(pk, 50 + i)
+        y = torch.empty(n, dtype=torch.float16, device=DEV)
+        tasks.append((p.to(DEV), s.to(DEV), x.to(DEV), y, pk, g, -1))
+        refs.append(port.gemv_w4a16(p.numpy(), s.numpy(), x.numpy(), pk, g))
+    batch = _C.GemvBatch(tasks)
+    for rep in range(2):
+        batch.run()
+        torch.cuda.synchronize()
+        assert _C.device_errors() == 0
+        for i, t in enumerate(tasks):
+            assert_close(t[3], refs[i], f"batch task {i} {shapes[i]} g{g}")
+        if rep == 0:
+            first = [t[3].clone() for t in tasks]
+    assert all(torch.equal(a, t[3]) for a, t in zip(first, tasks)), "results differ across launches"
+
+
 def test_chained_gate_down_layers():
     H, I, L = 2048, 6144, 8
     x0 = fp16_randn(H, 1).to(DEV)

@@ -37,7 +37,10 @@ def test_w4a16_dequant_exact_via_basis_vectors(fn, K):
 
 
 @pytest.mark.parametrize("N,K,g", [(6144, 2048, 128), (2048, 6144, 128), (512, 4096, 128), (3072, 2048, 128),
-                                   (17408, 5120, 128), (5120, 17408, 128), (1, 128, 128), (33, 256, 128)])
+                                   (17408, 5120, 128), (5120, 17408, 128), (1, 128, 128), (33, 256, 128),
+                                   # 14B tensor-parallel row-parallel shards: o_proj / down_proj at TP 4 and 8
+                                   # (10, 5, 34, 17 scale groups per row: not 16-byte scale rows)
+                                   (5120, 1280, 128), (5120, 640, 128), (5120, 4352, 128), (5120, 2176, 128)])
 def test_w4a16_matches_oracle_config_shapes(N, K, g):
     packed, scale, pk = int4_weights(N, K, g, seed=N + K)
     x = fp16_randn(pk, seed=K)

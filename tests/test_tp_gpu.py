@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on two GPUs (NCCL, one process per GPU), each rank
+"""Tensor-parallel decode on 2 / 4 / 8 GPUs (one process per GPU), each rank
 also holding the unsharded model on its own device:
 
 * a rank's shard matrices are exactly the slices of the full quantized
@@ -9,9 +9,15 @@ also holding the unsharded model on its own device:
 * the vocabulary-parallel LM head picks exactly the single-GPU argmax for
   the same normed hidden state;
 * eager TP decode gives the same tokens on every rank, and the CUDA-graph TP
-  decoder (NCCL collectives inside the graph) gives the eager tokens.
+  decoder (NCCL collectives inside the graph) gives the eager tokens;
+* the peer-memory exchange kernels: all-gather is the exact concatenation,
+  the all-reduce + residual equals the NCCL fp32 all-reduce bit for bit (two
+  ranks: a + b is order-free) with its RMSNorm within an fp16 ulp of the
+  unfused kernel, the greedy-token agreement breaks ties to the lowest global
+  index, the fused row-parallel GEMV + all-reduce equals the same GEMV + NCCL, and
+  decode through the exchange (eager and graph) matches the NCCL decode.
 
-Skipped with fewer than two GPUs."""
+Each world size is skipped when fewer GPUs are visible."""
 import os
 import socket
 from datetime import timedelta
@@ -23,8 +29,9 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-ARCH_ARGS = dict(num_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4, num_key_value_heads=2,
-                 head_dim=128, vocab_size=512)
+# shardable 2 / 4 / 8 ways: 16 q / 8 kv heads of 64, intermediate 1024 (128 channels per rank at 8)
+ARCH_ARGS = dict(num_layers=2, hidden_size=512, intermediate_size=1024, num_attention_heads=16, num_key_value_heads=8,
+                 head_dim=64, vocab_size=512)
 
 
 def _free_port():
@@ -41,8 +48,9 @@ def _rel_l2(a, b):
 def _worker(rank, world, port_no, results):
     from soinfer.runtime import generate as gen
     from soinfer.runtime.loader import Architecture, synthetic_streaming_model
-    from soinfer.runtime.tp import (ShardPlan, build_tp_model, generate_tp, graph_decoder_tp, run_decoder_layer_tp,
-                                    tp_next_token)
+    from soinfer import _C, ops
+    from soinfer.runtime.tp import (PeerExchange, ShardPlan, all_reduce_sum, build_tp_model, generate_tp,
+                                    graph_decoder_tp, run_decoder_layer_tp, tp_next_token)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -107,16 +115,75 @@ def _worker(rank, world, port_no, results):
         out.update(eager=eager, graph=graph, graph2=graph2, eager2=eager2,
                    full=gen.generate_streaming(full, prompt, 6, max_seq_len=64))
         del gd
+
+        # ---- peer-memory exchange kernels
+        ex = PeerExchange(device=dev)
+        g2 = torch.Generator(device=dev).manual_seed(100 + rank)
+        loc = torch.randn(1000, generator=g2, device=dev).half()[:992]
+        gathered = ex.allgather(loc)
+        parts = [torch.empty_like(loc) for _ in range(world)]
+        dist.all_gather(parts, loc)
+        out["allgather_exact"] = bool(torch.equal(gathered, torch.stack(parts)))
+        H = arch.hidden_size
+        partial = torch.randn(H, generator=g2, device=dev).half()
+        torch.manual_seed(0)  # identical residual / weight on every rank
+        resid = torch.randn(H, device=dev).half()
+        w = (torch.rand(H, device=dev) + 0.5).half()
+        h3x, h2x = ex.allreduce_add_rmsnorm(partial, resid, w, 1e-6)
+        o = all_reduce_sum(partial)
+        h3r, h2r = ops.add_rmsnorm(resid.unsqueeze(0), o.unsqueeze(0), w, 1e-6)
+        out["ar_sum_exact"] = bool(torch.equal(h2x, h2r.squeeze(0)))
+        out["ar_norm_maxdiff"] = float((h3x.float() - h3r.squeeze(0).float()).abs().max())
+        # argmax agreement: every rank holds the same max logit -> lowest global index wins;
+        # then the last rank's larger logit wins
+        lg = torch.zeros(16, dtype=torch.float16, device=dev)
+        lg[5] = 3.5
+        li = torch.tensor([5], dtype=torch.int32, device=dev)
+        out["argmax_tie"] = int(ex.argmax(lg, li, rank * 16).item())
+        lg[5] = 1.0 + rank
+        out["argmax_win"] = int(ex.argmax(lg, li, rank * 16).item())
+        # fused row-parallel GEMV (o_proj shard) + all-reduce vs GEMV + NCCL
+        name = "model.layers.0.self_attn.o_proj.weight"
+        m = tp.matrices[name]
+        xa = torch.randn(m.k, generator=g2, device=dev).half()
+        h3f, h2f = ex.row_parallel(tp.resident[name], m.scale, xa, H, 128, residual=resid, weight=w)
+        part = torch.empty(H, dtype=torch.float16, device=dev)  # the same batched kernel, output to y
+        _C.gemv_w4a16_batch([(tp.resident[name], m.scale, xa, part, m.packed_k, 128, -1)])
+        h3n, h2n = ops.add_rmsnorm(resid.unsqueeze(0), all_reduce_sum(part).unsqueeze(0), w, 1e-6)
+        out["fused_sum_exact"] = bool(torch.equal(h2f, h2n.squeeze(0)))
+        out["fused_norm_maxdiff"] = float((h3f.float() - h3n.squeeze(0).float()).abs().max())
+        # decode through the exchange
+        kx, vx = gen._kv_caches(tp, 16)
+        kn, vn = gen._kv_caches(tp, 16)
+        px, pn = gen.WeightPipeline(tp), gen.WeightPipeline(tp)
+        x = tp.embed_tokens[7]
+        xe = xn_ = x
+        worst = 0.0
+        for pos in range(3):
+            for li_ in range(arch.num_layers):
+                xe = run_decoder_layer_tp(px, tp, li_, xe, pos, kx[li_], vx[li_], exchange=ex)
+                xn_ = run_decoder_layer_tp(pn, tp, li_, xn_, pos, kn[li_], vn[li_])
+                worst = max(worst, _rel_l2(xe, xn_))
+        out["exchange_layer_rel_l2"] = worst
+        out["ex_eager"] = generate_tp(tp, plan, prompt, 6, max_seq_len=64, exchange=ex)
+        gdx = graph_decoder_tp(tp, plan, max_seq_len=64, exchange=ex)
+        out["ex_graph"] = gdx.generate(prompt, 6)
+        out["ex_graph2"] = gdx.generate([7, 7], 5)
+        out["ex_eager2"] = generate_tp(tp, plan, [7, 7], 5, max_seq_len=64, exchange=ex)
+        del gdx
         torch.cuda.synchronize()
+        out["device_errors"] = _C.device_errors()
+        ex.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
     results[rank] = out
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tensor_parallel_two_gpus():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
@@ -127,7 +194,16 @@ def test_tensor_parallel_two_gpus():
         assert o["layer_rel_l2"] < 3e-3, f"rank {r}: TP layer rel-L2 {o['layer_rel_l2']}"
         assert o["argmax_agree"], f"rank {r}: {o['argmax_pairs']}"
         assert o["graph"] == o["eager"] and o["graph2"] == o["eager2"], f"rank {r}: graph tokens differ"
-    assert res[0]["eager"] == res[1]["eager"] and res[0]["eager2"] == res[1]["eager2"]
+    assert all(res[r]["eager"] == res[0]["eager"] and res[r]["eager2"] == res[0]["eager2"] for r in range(world))
+    for r in range(world):
+        o = res[r]
+        assert o["device_errors"] == 0, f"rank {r}: device error bits {o['device_errors']}"
+        assert o["allgather_exact"] and o["ar_sum_exact"] and o["fused_sum_exact"], o
+        assert o["ar_norm_maxdiff"] < 4e-3 and o["fused_norm_maxdiff"] < 4e-3, o
+        assert o["argmax_tie"] == 5 and o["argmax_win"] == 16 * (world - 1) + 5, o
+        assert o["exchange_layer_rel_l2"] < 2e-3, o["exchange_layer_rel_l2"]
+        assert o["ex_graph"] == o["ex_eager"] and o["ex_graph2"] == o["ex_eager2"], o
+    assert all(res[r]["ex_eager"] == res[0]["ex_eager"] for r in range(world))
     # not asserted equal (fp16 partial rounding), recorded for the failure message of a gross error
     same = sum(a == b for a, b in zip(res[0]["eager"], res[0]["full"]))
     assert same >= len(res[0]["full"]) - 3, (res[0]["eager"], res[0]["full"])
