@@ -288,7 +288,8 @@ __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint
 }
 
 // The producer warp's loop.
-__device__ __forceinline__ void producer_loop(const GemvBatchParams& B, int cta, int lane, uint8_t* ring,
+template <class Params>
+__device__ __forceinline__ void producer_loop(const Params& B, int cta, int lane, uint8_t* ring,
                                            uint64_t* full, uint64_t* empty, int* item_off,
                                            volatile int* abort_flag) {
   // ------------------------------------------------------------ producer
@@ -326,38 +327,47 @@ __device__ __forceinline__ void producer_loop(const GemvBatchParams& B, int cta,
       const int d = issued % kMaxItems;
       __syncwarp();  // every lane has read item_off[] before lane 0 rewrites a slot
       const int64_t r0 = v.row0 + tile0 * 16;
-      if (lane == 0) item_off[d] = head;
-      if (B.any_cp_async) fence_proxy_async_smem();  // earlier cp.async writes into the ring precede bulk writes
-      float* sdst = reinterpret_cast<float*>(ring + head + round128(wb));
-      const int gs = segd ? nks / tk.cpg : tk.G;  // scale columns of the item's rows
-      // segment scales as one bulk copy per row when every piece is whole 16 bytes
-      const bool seg_bulk = segd && (tk.G % 4) == 0 && (srow_f % 4) == 0 && (gs % 4) == 0;
-      if (tk.scale_plain && !seg_bulk) {
-        // scale rows not in 16-byte pieces: 4-byte cp.async copies; each
-        // lane's arrive-on (counted before lane 0's arrive below) completes
-        // when its copies have landed, so the producer never waits on them
-        const float* src = tk.S + r0 * tk.G + (segd ? seg * srow_f : 0);
-        for (int i = lane; i < rows * gs; i += 32) {
-          const int rr = i / gs, c = i - rr * gs;
-          cp_async_4(sdst + rr * srow_f + c, src + (int64_t)rr * tk.G + c);
-        }
-        cp_async_arrive(&full[d]);
-        __syncwarp();
-      }
-      if (!segd) {
+      if (!segd && !tk.scale_plain) {
+        // whole 16-row tiles with 16-byte scale rows: one bulk copy each for rows and scales
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[d], (uint32_t)(wb + (tk.scale_plain ? 0 : sb)));
+          item_off[d] = head;
+          mbar_arrive_expect_tx(&full[d], (uint32_t)(wb + sb));
           bulk_g2s(ring + head, tk.W + r0 * row_bytes, (uint32_t)wb, &full[d]);
-          if (!tk.scale_plain) bulk_g2s(sdst, tk.S + r0 * tk.G, (uint32_t)sb, &full[d]);
+          bulk_g2s(ring + head + round128(wb), tk.S + r0 * tk.G, (uint32_t)sb, &full[d]);
         }
       } else {
-        if (lane == 0) mbar_arrive_expect_tx(&full[d], (uint32_t)(rows * (nks * 64 + (seg_bulk ? gs * 4 : 0))));
-        if (lane < rows)
-          bulk_g2s(ring + head + lane * wrow, tk.W + (r0 + lane) * row_bytes + (int64_t)seg * tk.ks * 64,
-                   (uint32_t)(nks * 64), &full[d]);
-        if (seg_bulk && lane >= 16 && lane - 16 < rows)
-          bulk_g2s(sdst + (lane - 16) * srow_f, tk.S + (r0 + lane - 16) * tk.G + seg * srow_f, (uint32_t)(gs * 4),
-                   &full[d]);
+        if (lane == 0) item_off[d] = head;
+        if (B.any_cp_async) fence_proxy_async_smem();  // earlier cp.async writes into the ring precede bulk writes
+        float* sdst = reinterpret_cast<float*>(ring + head + round128(wb));
+        const int gs = segd ? nks / tk.cpg : tk.G;  // scale columns of the item's rows
+        // segment scales as one bulk copy per row when every piece is whole 16 bytes
+        const bool seg_bulk = segd && (tk.G % 4) == 0 && (srow_f % 4) == 0 && (gs % 4) == 0;
+        if (!seg_bulk) {
+          // scale rows not in 16-byte pieces: 4-byte cp.async copies; each
+          // lane's arrive-on (counted before lane 0's arrive below) completes
+          // when its copies have landed, so the producer never waits on them
+          const float* src = tk.S + r0 * tk.G + (segd ? seg * srow_f : 0);
+          for (int i = lane; i < rows * gs; i += 32) {
+            const int rr = i / gs, c = i - rr * gs;
+            cp_async_4(sdst + rr * srow_f + c, src + (int64_t)rr * tk.G + c);
+          }
+          cp_async_arrive(&full[d]);
+          __syncwarp();
+        }
+        if (!segd) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[d], (uint32_t)wb);
+            bulk_g2s(ring + head, tk.W + r0 * row_bytes, (uint32_t)wb, &full[d]);
+          }
+        } else {
+          if (lane == 0) mbar_arrive_expect_tx(&full[d], (uint32_t)(rows * (nks * 64 + (seg_bulk ? gs * 4 : 0))));
+          if (lane < rows)
+            bulk_g2s(ring + head + lane * wrow, tk.W + (r0 + lane) * row_bytes + (int64_t)seg * tk.ks * 64,
+                     (uint32_t)(nks * 64), &full[d]);
+          if (seg_bulk && lane >= 16 && lane - 16 < rows)
+            bulk_g2s(sdst + (lane - 16) * srow_f, tk.S + (r0 + lane - 16) * tk.G + seg * srow_f, (uint32_t)(gs * 4),
+                     &full[d]);
+        }
       }
       __syncwarp();
       head += bytes;
@@ -372,7 +382,8 @@ __device__ __forceinline__ void producer_loop(const GemvBatchParams& B, int cta,
 }
 
 // The epilogue warp's loop.
-__device__ __forceinline__ void epilogue_loop(const GemvBatchParams& B, int cta, int lane, const float* red,
+template <class Params>
+__device__ __forceinline__ void epilogue_loop(const Params& B, int cta, int lane, const float* red,
                                            uint64_t* rfull, uint64_t* rempty, uint8_t* const* s_inbox,
                                            int* counters, volatile int* abort_flag) {
   // ------------------------------------------------------------ epilogue
@@ -439,8 +450,9 @@ __device__ __forceinline__ void epilogue_loop(const GemvBatchParams& B, int cta,
 
 // 19 warps put 5 warps on some of the SM's four 16K-register partitions:
 // at most 96 registers per thread.
+template <class Params>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemv_batch_kernel(const __grid_constant__ GemvBatchParams B, int* __restrict__ counters) {
+    gemv_batch_kernel(const __grid_constant__ Params B, int* __restrict__ counters) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;                                                  // [ring_bytes]
   uint8_t* xbuf = smem + B.ring_bytes;                                   // [2][x_bytes]
@@ -713,10 +725,14 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
   return true;
 }
 
-cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream) {
+namespace {
+
+template <class Params>
+cudaError_t launch_params(const Params& B, int* counters, cudaStream_t stream) {
   static int attr_bytes = 0;  // callers serialise launches (the C ABI holds a mutex)
+  auto kernel = gemv_batch_kernel<Params>;
   if (B.smem_bytes > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B.smem_bytes);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B.smem_bytes);
     if (e != cudaSuccess) return e;
     attr_bytes = B.smem_bytes;
   }
@@ -730,7 +746,26 @@ cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStrea
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_batch_kernel, B, counters);
+  return cudaLaunchKernelEx(&cfg, kernel, B, counters);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream) {
+  if (B.num <= kSmallBatchTasks) {
+    // a decode layer's batch: the same kernel with a ~1 KB parameter block
+    static GemvBatchParamsT<kSmallBatchTasks> S;  // callers serialise launches
+    S.num = B.num;
+    S.grid = B.grid;
+    S.x_bytes = B.x_bytes;
+    S.ring_bytes = B.ring_bytes;
+    S.smem_bytes = B.smem_bytes;
+    S.any_cp_async = B.any_cp_async;
+    S.peers = B.peers;
+    for (int i = 0; i < B.num; ++i) S.tasks[i] = B.tasks[i];
+    return launch_params(S, counters, stream);
+  }
+  return launch_params(B, counters, stream);
 }
 
 cudaError_t read_and_clear_gemv_batch_error(int* out) {

@@ -87,12 +87,15 @@ struct GemvBatchTask {
   int peer;           // y == nullptr: rows go to every rank's exchange inbox (PeerSet), the last CTA signals
 };
 constexpr int kMaxBatchTasks = 256;
-struct GemvBatchParams {
+constexpr int kSmallBatchTasks = 8;  // decode-layer batches: a small kernel-parameter block launches faster
+template <int MaxTasks>
+struct GemvBatchParamsT {
   int num, grid, x_bytes, ring_bytes, smem_bytes;
   int any_cp_async;  // some task stages scales with cp.async (proxy fence before later bulk copies)
   PeerSet peers;  // used by a peer task (at most one per batch)
-  GemvBatchTask tasks[kMaxBatchTasks];
+  GemvBatchTask tasks[MaxTasks];
 };
+using GemvBatchParams = GemvBatchParamsT<kMaxBatchTasks>;
 int64_t gemv_batch_workspace_bytes(int64_t num_tasks);
 // Fills the derived fields; false when the batch needs the per-task fallback.
 bool plan_gemv_batch(GemvBatchParams& B, int sms);

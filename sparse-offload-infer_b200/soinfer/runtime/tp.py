@@ -342,6 +342,68 @@ def run_decoder_layer_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cac
     return out
 
 
+def run_decoder_layer_dip_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, dip_k: int, plan: ShardPlan,
+                             exchange: PeerExchange, trace: dict | None = None):
+    """DIP layer under tensor parallelism, reference selection semantics: the
+    rank's gate shard (column-parallel rows) is all-gathered, every rank runs
+    the same deterministic top-dip_k |gate| selector over all I channels, and
+    each rank computes only the selected channels inside its own up / down_T
+    shard (rows [lo, hi)); the down partials go through the exchange
+    (all-reduce + residual + next RMSNorm).  One host read per layer (the
+    number of selected channels this rank owns sizes the row kernels).
+    The pipeline is the DIP one (q / k / v / o / gate).  trace (optional)
+    receives h3, the gathered gate and the global selection."""
+    from .. import ops
+    from ..offload.load_hf_checkpoint import DOWN_PROJ_T_SUFFIX
+    from .generate import _attention_block
+
+    g = model.group_size
+
+    def o_block(attn, x, post_w, eps):
+        W, m = pipeline.next_resident()
+        h3, h2 = exchange.row_parallel(W, m.scale, attn, model.hidden_size, g, residual=x, weight=post_w, eps=eps)
+        return h2, h3
+
+    prev = exchange._next_normed
+    h_in = prev[1] if prev is not None and prev[0] is x_flat else None
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, h_in=h_in, o_block=o_block)
+    gate_loc = pipeline.next_gemv(h3)
+    gate = exchange.allgather(gate_loc).view(-1)
+    idx = ops.topk_threshold_select_abs(gate, dip_k)          # global channels, ascending
+    lo, hi = plan.inter_rows
+    bounds = torch.searchsorted(idx, torch.tensor([lo, hi], dtype=torch.int32, device=idx.device))
+    a, b = (int(v) for v in bounds.tolist())                   # this rank's share of the selection
+    if trace is not None:
+        trace.update(h2=h2, h3=h3, gate=gate, idx=idx)
+    if b > a:
+        loc = (idx[a:b] - lo).contiguous()
+        up = model.matrix(layer_idx, "mlp.up_proj.weight")
+        down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
+        u_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, loc, h3, up.packed_k, g)
+        h_sel = ops.swiglu(gate_loc, u_sel, loc)
+        part = ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, loc, h_sel,
+                                          model.hidden_size, g)
+    else:
+        part = torch.zeros(model.hidden_size, dtype=torch.float16, device=h3.device)
+    nxt = layer_idx + 1
+    w_next = model.layer_norms[nxt]["input_layernorm"] if nxt < model.num_layers else None
+    h_next, out = exchange.allreduce_add_rmsnorm(part, residual=h2, weight=w_next, eps=model.rms_norm_eps)
+    exchange._next_normed = (out, h_next) if h_next is not None else None
+    return out
+
+
+def generate_dip_tp(model, plan: ShardPlan, prompt_ids: list[int], n_new: int, dip_k: int, exchange: PeerExchange,
+                    max_seq_len: int = 512):
+    """Eager greedy decode of the TP model with DIP MLPs (every rank returns the same ids)."""
+    from .generate import DIP_DENSE_SUFFIXES, WeightPipeline, _greedy
+
+    pipeline = WeightPipeline(model, suffixes=DIP_DENSE_SUFFIXES)
+    return _greedy(model, prompt_ids, n_new,
+                   lambda li, x, p, kc, vc: run_decoder_layer_dip_tp(pipeline, model, li, x, p, kc, vc, dip_k, plan,
+                                                                     exchange),
+                   None, max_seq_len, token_fn=lambda m, xn: tp_next_token(m, xn, plan, None, exchange))
+
+
 def tp_next_token(model, xn: torch.Tensor, plan: ShardPlan, group=None, exchange=None) -> torch.Tensor:
     """Greedy token over the vocabulary-parallel LM head: each rank's fused
     argmax of its rows, then the ranks agree (exchange kernel, or
@@ -377,4 +439,5 @@ def graph_decoder_tp(model, plan: ShardPlan, group=None, max_seq_len: int = 2048
 
 
 __all__ = ["ShardPlan", "shard_packed", "agree_argmax", "build_tp_model", "PeerExchange", "all_reduce_sum",
-           "run_decoder_layer_tp", "tp_next_token", "generate_tp", "graph_decoder_tp"]
+           "run_decoder_layer_tp", "run_decoder_layer_dip_tp", "generate_dip_tp", "tp_next_token", "generate_tp",
+           "graph_decoder_tp"]

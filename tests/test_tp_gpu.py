@@ -15,7 +15,11 @@ also holding the unsharded model on its own device:
   ranks: a + b is order-free) with its RMSNorm within an fp16 ulp of the
   unfused kernel, the greedy-token agreement breaks ties to the lowest global
   index, the fused row-parallel GEMV + all-reduce equals the same GEMV + NCCL, and
-  decode through the exchange (eager and graph) matches the NCCL decode.
+  decode through the exchange (eager and graph) matches the NCCL decode;
+* DIP under TP: the all-gathered gate matches the unsharded gate GEMV, the
+  global selection on it equals the oracle's reference selector bit for bit
+  on every rank, and the layer output matches the oracle's DIP block
+  evaluated on the same gate; DIP decode gives the same tokens on every rank.
 
 Each world size is skipped when fewer GPUs are visible."""
 import os
@@ -49,8 +53,10 @@ def _worker(rank, world, port_no, results):
     from soinfer.runtime import generate as gen
     from soinfer.runtime.loader import Architecture, synthetic_streaming_model
     from soinfer import _C, ops
-    from soinfer.runtime.tp import (PeerExchange, ShardPlan, all_reduce_sum, build_tp_model, generate_tp,
-                                    graph_decoder_tp, run_decoder_layer_tp, tp_next_token)
+    from oracle import reference_port as port
+    from soinfer.runtime.tp import (PeerExchange, ShardPlan, all_reduce_sum, build_tp_model, generate_dip_tp,
+                                    generate_tp, graph_decoder_tp, run_decoder_layer_dip_tp, run_decoder_layer_tp,
+                                    tp_next_token)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -61,8 +67,8 @@ def _worker(rank, world, port_no, results):
         arch = Architecture(**ARCH_ARGS)
         plan = ShardPlan(rank, world, arch.num_attention_heads, arch.num_key_value_heads, arch.head_dim,
                          arch.hidden_size, arch.intermediate_size, arch.vocab_size)
-        full = synthetic_streaming_model(arch, seed=3, resident=True, offload=False, include_dip=False, device=dev)
-        tp = build_tp_model(arch, plan, seed=3, device=dev)
+        full = synthetic_streaming_model(arch, seed=3, resident=True, offload=False, include_dip=True, device=dev)
+        tp = build_tp_model(arch, plan, seed=3, include_dip=True, device=dev)
 
         # shards are slices of the full matrices
         exact = True
@@ -171,6 +177,26 @@ def _worker(rank, world, port_no, results):
         out["ex_graph2"] = gdx.generate([7, 7], 5)
         out["ex_eager2"] = generate_tp(tp, plan, [7, 7], 5, max_seq_len=64, exchange=ex)
         del gdx
+
+        # ---- DIP under TP
+        dip_k = arch.intermediate_size // 2
+        pdp = gen.WeightPipeline(tp, gen.DIP_DENSE_SUFFIXES)
+        kd, vd = gen._kv_caches(tp, 16)
+        tr = {}
+        y = run_decoder_layer_dip_tp(pdp, tp, 0, tp.embed_tokens[11], 0, kd[0], vd[0], dip_k, plan, ex, trace=tr)
+        npf = lambda name: (full.resident[f"model.layers.0.{name}"].cpu().numpy(),
+                            full.matrices[f"model.layers.0.{name}"].scale.cpu().numpy())
+        h3n = tr["h3"].cpu().numpy()
+        blk = port.dip_mlp_block(h3n, npf("mlp.gate_proj.weight"), npf("mlp.up_proj.weight"),
+                                 npf(gen.DOWN_PROJ_T_SUFFIX), dip_k, 128, H, gate_out=tr["gate"].cpu().numpy())
+        import numpy as np
+        ref = (tr["h2"].cpu().numpy().astype(np.float32) + blk["y"].astype(np.float16).astype(np.float32))
+        out["dip_rel_l2"] = _rel_l2(y, torch.from_numpy(ref.astype(np.float16)).to(dev))
+        out["dip_idx_exact"] = bool(np.array_equal(tr["idx"].cpu().numpy(), blk["idx"]))
+        gm = full.matrices["model.layers.0.mlp.gate_proj.weight"]
+        gate_full = ops.gemv_w4a16_group_lop3(full.resident[gm.handle.name], gm.scale, tr["h3"], gm.packed_k, 128)
+        out["dip_gate_rel_l2"] = _rel_l2(tr["gate"], gate_full)
+        out["dip_tokens"] = generate_dip_tp(tp, plan, prompt, 5, dip_k, ex, max_seq_len=64)
         torch.cuda.synchronize()
         out["device_errors"] = _C.device_errors()
         ex.close()
@@ -204,6 +230,11 @@ def test_tensor_parallel(world):
         assert o["exchange_layer_rel_l2"] < 2e-3, o["exchange_layer_rel_l2"]
         assert o["ex_graph"] == o["ex_eager"] and o["ex_graph2"] == o["ex_eager2"], o
     assert all(res[r]["ex_eager"] == res[0]["ex_eager"] for r in range(world))
+    for r in range(world):
+        o = res[r]
+        assert o["dip_idx_exact"], f"rank {r}: DIP selection differs from the reference selector"
+        assert o["dip_gate_rel_l2"] < 1e-3 and o["dip_rel_l2"] < 2e-3, o
+    assert all(res[r]["dip_tokens"] == res[0]["dip_tokens"] for r in range(world))
     # not asserted equal (fp16 partial rounding), recorded for the failure message of a gross error
     same = sum(a == b for a, b in zip(res[0]["eager"], res[0]["full"]))
     assert same >= len(res[0]["full"]) - 3, (res[0]["eager"], res[0]["full"])
