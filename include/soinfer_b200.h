@@ -379,6 +379,17 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                                 const int32_t* pos_dev, void* workspace, int64_t workspace_bytes,
                                 void* stream);
 
+/* Load-time INT4 quantization + packing on the GPU (reference
+ * python/soinfer/quant/formats.py:77-110 with calibrate.min_max:22-27 and
+ * quant/pack.py:31-69): w [N, K] with row stride ld (dtype 0 fp32, 1 fp16,
+ * 2 bf16) -> packed uint8 [N, ceil(Kp/8)*4] (AWQ nibble order) and scale fp32
+ * [N, Kp/group_size], Kp = K rounded up to group_size (a power of two in
+ * [8, 256]); scale = max(amax/7, FLT_MIN), q = clamp(rint(w/scale), -7, 7)
+ * with IEEE division -- bit-exact with the reference's CPU quantizer, in one
+ * pass over the weights. */
+int soinfer_quantize_pack_int4(const void* w, int32_t dtype, int64_t N, int64_t K, int64_t ld,
+                               int64_t group_size, uint8_t* packed, float* scale, void* stream);
+
 /* ---- Tensor-parallel exchange over peer memory (no reference counterpart:
  * the reference runs on one GPU; this is the row-parallel all-reduce, the
  * all-gather and the greedy-token agreement of tensor-parallel decode across

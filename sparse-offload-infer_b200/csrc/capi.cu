@@ -634,6 +634,20 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                      name);
 }
 
+int soinfer_quantize_pack_int4(const void* w, int32_t dtype, int64_t N, int64_t K, int64_t ld, int64_t group_size,
+                               uint8_t* packed, float* scale, void* stream) {
+  const char* name = "quantize_pack_int4";
+  REQUIRE(dtype >= 0 && dtype <= 2, "%s: dtype must be 0 (fp32), 1 (fp16) or 2 (bf16)", name);
+  REQUIRE(group_size >= 8 && group_size <= 256 && (group_size & (group_size - 1)) == 0,
+          "%s: group_size must be a power of two in [8, 256]", name);
+  REQUIRE(N >= 0 && K >= 1 && ld >= K && N < (1ll << 40) && K < (1ll << 31), "%s: invalid shape or row stride", name);
+  if (N == 0) return SOINFER_OK;
+  REQUIRE(w && packed && scale, "%s: null pointer", name);
+  REQUIRE(aligned(packed, 4) && aligned(scale, 4), "%s: packed and scale must be 4-byte aligned", name);
+  return cuda_result(launch_quantize_pack_int4(w, dtype, N, K, ld, group_size, packed, scale, as_stream(stream)),
+                     name);
+}
+
 // ---------------------------------------------------------------- tensor-parallel exchange
 
 static_assert(sizeof(cudaIpcMemHandle_t) == SOINFER_IPC_HANDLE_BYTES, "IPC handle size");

@@ -43,6 +43,12 @@ struct LaunchOpts {
 cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, half* y, int64_t nrows,
                            int64_t K, int64_t group_size, cudaStream_t stream, LaunchOpts opts = {});
 
+// Group-wise INT4 quantization + AWQ packing of w [N, K] (row stride ld; dtype 0 fp32, 1 fp16,
+// 2 bf16): packed uint8 [N, ceil(Kp/8)*4], scale fp32 [N, Kp/g], Kp = K rounded up to g
+// (g a power of two in [8, 256]).  Bit-exact with the reference's CPU torch quantizer.
+cudaError_t launch_quantize_pack_int4(const void* w, int dtype, int64_t N, int64_t K, int64_t ld, int64_t group_size,
+                                      uint8_t* packed, float* scale, cudaStream_t stream);
+
 // Reads and clears the INT4 GEMV module's device error bits (DeviceError).
 cudaError_t read_and_clear_gemv_w4_error(int* out);
 

@@ -69,6 +69,7 @@ _SIGNATURES = {
     "soinfer_rope_apply_at": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
+    "soinfer_quantize_pack_int4": (_INT, [_P, ctypes.c_int32, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "soinfer_peer_buffer_bytes": (_I64, [_I64, ctypes.c_int32]),
     "soinfer_peer_buffer_create": (_INT, [_I64, _P, _P]),
     "soinfer_peer_buffer_open": (_INT, [_P, _P]),
@@ -840,6 +841,29 @@ def decode_attention(q, k_cache, v_cache, cur_len: int, out: torch.Tensor | None
         _call("soinfer_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(y), nq, nkv, max_seq, hd,
               cur_len, ws.data_ptr(), ws.numel(), _stream(dev))
     return y
+
+
+# ------------------------------------------------------------ load-time quantization
+_QUANT_DTYPES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def quantize_pack_int4(w, group_size: int):
+    """GPU group-wise INT4 quantize + AWQ pack of w [N, K] (fp32 / fp16 / bf16
+    CUDA, unit stride along K): (packed uint8 [N, ceil(Kp/8)*4], scale fp32
+    [N, Kp/g], Kp), bit-exact with soinfer.quant.formats.quantize +
+    pack.pack_int4 on the CPU."""
+    name = "quantize_pack_int4"
+    _check(w.is_cuda and w.dim() == 2 and w.stride(1) == 1, name, "(w): must be a 2D CUDA tensor with unit K stride")
+    _check(w.dtype in _QUANT_DTYPES, name, "(w): dtype must be float32, float16 or bfloat16")
+    _check(group_size in (8, 16, 32, 64, 128, 256), name, ": group_size must be a power of two in [8, 256]")
+    N, K = w.shape
+    Kp = _cdiv(K, group_size) * group_size
+    packed = torch.empty(N, Kp // 2, dtype=torch.uint8, device=w.device)
+    scale = torch.empty(N, Kp // group_size, dtype=torch.float32, device=w.device)
+    with torch.cuda.device(w.device):
+        _call("soinfer_quantize_pack_int4", _ptr(w), _QUANT_DTYPES[w.dtype], N, K, w.stride(0), group_size,
+              _ptr(packed), _ptr(scale), _stream(w.device))
+    return packed, scale, Kp
 
 
 # ------------------------------------------------------------ tensor-parallel exchange

@@ -5,8 +5,14 @@ Each decoder-layer linear weight is read one tensor at a time, quantized to
 group-wise INT4 (min-max scales) and AWQ-packed, registered in the arena, and
 its fp32 scales kept resident on the GPU.  With include_down_proj_t the
 down_proj is also stored transposed ([intermediate, hidden]) so DIP can
-select its rows.  Quantization can run on the GPU (torch ops, bit-identical
-to the CPU result) to cut load time.
+select its rows.  Quantization can run on the GPU: one fused quantize + pack
+kernel (soinfer_quantize_pack_int4), bit-exact with the CPU quantizer --
+unlike torch's GPU path, whose division by a scalar multiplies by the
+reciprocal and can move a scale by one ulp.
+
+save_quantized / load_quantized serialize the quantized arena (raw packed
+bytes + fp32 scales + a JSON index), so a model is quantized once and later
+loads are one sequential read into the pinned arena.
 """
 from __future__ import annotations
 
@@ -41,11 +47,21 @@ class LoadedMatrix:
 
 
 def quantize_and_pack(w: torch.Tensor, group_size: int, device=None) -> tuple[torch.Tensor, torch.Tensor, int]:
-    """w [N, K] -> (packed uint8 [N, ceil(Kp/8)*4] on CPU, scale fp32 [N, G], packed_k)."""
+    """w [N, K] -> (packed uint8 [N, ceil(Kp/8)*4] on CPU, scale fp32 [N, G], packed_k).
+    On a CUDA device (and a power-of-two group size <= 256) the fused kernel
+    does it in one pass; otherwise the reference's torch path on the CPU."""
     src = w.to(device) if device is not None else w
-    qt = formats.quantize(src.float(), formats.QuantConfig(bits=4, granularity="group", group_size=group_size))
+    if src.is_cuda and group_size in (8, 16, 32, 64, 128, 256):
+        from .. import _C
+
+        if src.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            src = src.float()
+        packed, scale, packed_k = _C.quantize_pack_int4(src.contiguous(), group_size)
+        return packed.cpu(), scale, packed_k
+    qt = formats.quantize(src.cpu().float(), formats.QuantConfig(bits=4, granularity="group", group_size=group_size))
     packed, packed_k = pack.pack_int4(qt.qweight)
-    return packed.cpu(), qt.scale.contiguous(), packed_k
+    scale = qt.scale.contiguous()
+    return packed, scale.to(device) if device is not None else scale, packed_k
 
 
 def packed_int4_bytes(n: int, k: int, group_size: int = 8) -> int:
@@ -110,3 +126,55 @@ def stream_load_layers(model_dir: str, num_layers: int, group_size: int = 128, l
         if log_every and ((layer + 1) % log_every == 0 or layer == num_layers - 1):
             print(f"  loaded layer {layer + 1}/{num_layers} ({store.bytes_used / 1e9:.2f} GB in arena)")
     return store, matrices
+
+
+# --------------------------------------------------------------- serialized arena
+ARENA_FORMAT = "soinfer-b200-int4-arena-v1"
+
+
+def save_quantized(path: str, store: PinnedWeightStore, matrices: dict[str, LoadedMatrix], group_size: int) -> None:
+    """Writes path/arena.bin (the used arena bytes, registration order),
+    path/scales.bin (every matrix's fp32 scales, same order) and
+    path/index.json (format, group size, per matrix: name, arena offset,
+    rows, row bytes, n, k, packed_k, scale columns, scale offset)."""
+    os.makedirs(path, exist_ok=True)
+    entries, soff = [], 0
+    with open(os.path.join(path, "scales.bin"), "wb") as fs:
+        for name, m in sorted(matrices.items(), key=lambda kv: kv[1].handle.offset):
+            sc = m.scale.detach().to("cpu", torch.float32).contiguous()
+            fs.write(sc.numpy().tobytes())
+            entries.append({"name": name, "offset": m.handle.offset, "num_rows": m.handle.num_rows,
+                            "row_nbytes": m.handle.row_nbytes, "n": m.n, "k": m.k, "packed_k": m.packed_k,
+                            "scale_cols": int(sc.shape[1]), "scale_offset": soff})
+            soff += sc.numel() * 4
+    with open(os.path.join(path, "arena.bin"), "wb") as fa:
+        fa.write(store.arena[:store.bytes_used].numpy().tobytes())
+    with open(os.path.join(path, "index.json"), "w") as fi:
+        json.dump({"format": ARENA_FORMAT, "group_size": group_size, "arena_bytes": store.bytes_used,
+                   "matrices": entries}, fi)
+
+
+def load_quantized(path: str, device=None, pin: bool = True):
+    """Inverse of save_quantized: (store, {name: LoadedMatrix}, group_size);
+    the arena is read straight into the (pinned) host allocation, the scales
+    go to `device`."""
+    import numpy as np
+
+    with open(os.path.join(path, "index.json")) as fi:
+        idx = json.load(fi)
+    if idx.get("format") != ARENA_FORMAT:
+        raise ValueError(f"{path}: not a {ARENA_FORMAT} directory")
+    store = PinnedWeightStore(idx["arena_bytes"], pin=pin)
+    with open(os.path.join(path, "arena.bin"), "rb") as fa:
+        if fa.readinto(memoryview(store.arena.numpy())) != idx["arena_bytes"]:
+            raise ValueError(f"{path}/arena.bin is shorter than its index says")
+    scales = np.fromfile(os.path.join(path, "scales.bin"), dtype=np.float32)
+    matrices = {}
+    for e in idx["matrices"]:
+        h = store.adopt(e["name"], e["offset"], e["num_rows"], e["row_nbytes"])
+        n_sc = e["num_rows"] * e["scale_cols"]
+        sc = torch.from_numpy(scales[e["scale_offset"] // 4:e["scale_offset"] // 4 + n_sc].copy())
+        sc = sc.view(e["num_rows"], e["scale_cols"])
+        matrices[e["name"]] = LoadedMatrix(h, sc.to(device) if device is not None else sc, e["packed_k"], e["n"],
+                                           e["k"])
+    return store, matrices, idx["group_size"]

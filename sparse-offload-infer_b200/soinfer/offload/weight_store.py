@@ -29,10 +29,12 @@ class WeightHandle:
 
 
 class PinnedWeightStore:
-    def __init__(self, total_bytes: int):
+    def __init__(self, total_bytes: int, pin: bool = True):
+        """pin=False: pageable memory (host-only use, e.g. preparing or
+        inspecting an arena on a machine without a GPU)."""
         if total_bytes <= 0:
             raise ValueError("total_bytes must be positive")
-        self.arena = torch.empty(total_bytes, dtype=torch.uint8, pin_memory=True)
+        self.arena = torch.empty(total_bytes, dtype=torch.uint8, pin_memory=pin)
         self._next = 0
         self._handles: dict[str, WeightHandle] = {}
 
@@ -51,6 +53,19 @@ class PinnedWeightStore:
                              f"{self.arena.numel() - self._next} remain")
         self.arena[self._next:end].view(rows, rb).copy_(data)
         h = WeightHandle(name, self._next, rows, rb)
+        self._handles[name] = h
+        self._next = end
+        return h
+
+    def adopt(self, name: str, offset: int, num_rows: int, row_nbytes: int) -> WeightHandle:
+        """Registers a span whose bytes are already in the arena (a loaded
+        serialized arena); spans must come in increasing offset order."""
+        if name in self._handles:
+            raise ValueError(f"weight {name!r} already registered")
+        end = offset + num_rows * row_nbytes
+        if offset < self._next or end > self.arena.numel():
+            raise ValueError(f"adopt({name!r}): span [{offset}, {end}) overlaps or leaves the arena")
+        h = WeightHandle(name, offset, num_rows, row_nbytes)
         self._handles[name] = h
         self._next = end
         return h

@@ -17,8 +17,8 @@ from dataclasses import dataclass
 
 import torch
 
-from ..offload.load_hf_checkpoint import (DOWN_PROJ_T_SUFFIX, LINEAR_SUFFIXES, LoadedMatrix, packed_int4_bytes,
-                                          quantize_and_pack, stream_load_layers)
+from ..offload.load_hf_checkpoint import (DOWN_PROJ_T_SUFFIX, LINEAR_SUFFIXES, LoadedMatrix, load_quantized,
+                                          packed_int4_bytes, quantize_and_pack, save_quantized, stream_load_layers)
 from ..offload.weight_store import PinnedWeightStore, WeightHandle
 from ..quant import formats, pack
 from .generate import StreamingModel
@@ -33,17 +33,26 @@ def _load_small(model_dir: str, weight_map: dict[str, str], name: str, device) -
 
 
 def load_streaming_model(model_dir: str, group_size: int = 128, include_dip: bool = False,
-                         resident: bool = False, device=None) -> StreamingModel:
+                         resident: bool = False, device=None, arena_dir: str | None = None) -> StreamingModel:
     """Quantize every decoder layer's linear weights into a pinned INT4 arena
     (plus each down_proj transposed with include_dip), load embeddings, LM
     head and norms to the GPU as fp16.  resident=True also keeps every packed
-    matrix in HBM (no streaming)."""
+    matrix in HBM (no streaming).  arena_dir: a serialized arena
+    (save_quantized) -- loaded when it exists, written after quantizing when
+    it does not."""
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     with open(os.path.join(model_dir, "config.json")) as f:
         cfg = json.load(f)
     n_layers = cfg["num_hidden_layers"]
-    store, matrices = stream_load_layers(model_dir, n_layers, group_size=group_size,
-                                         include_down_proj_t=include_dip, quant_device=device)
+    if arena_dir is not None and os.path.exists(os.path.join(arena_dir, "index.json")):
+        store, matrices, saved_g = load_quantized(arena_dir, device=device)
+        if saved_g != group_size or (include_dip and not any(k.endswith(DOWN_PROJ_T_SUFFIX) for k in matrices)):
+            raise ValueError(f"{arena_dir}: saved with group size {saved_g} / without the DIP transposes")
+    else:
+        store, matrices = stream_load_layers(model_dir, n_layers, group_size=group_size,
+                                             include_down_proj_t=include_dip, quant_device=device)
+        if arena_dir is not None:
+            save_quantized(arena_dir, store, matrices, group_size)
     with open(os.path.join(model_dir, "model.safetensors.index.json")) as f:
         wm = json.load(f)["weight_map"]
     lm_name = "lm_head.weight" if "lm_head.weight" in wm else "model.embed_tokens.weight"  # tied embeddings
@@ -115,6 +124,11 @@ def synthetic_weights(arch: Architecture, seed: int, group_size: int, include_di
 
 
 def _quantized(layer, suffix, w, group_size):
+    if w.is_cuda and group_size in (8, 16, 32, 64, 128, 256):
+        from .. import _C
+
+        packed, scale, packed_k = _C.quantize_pack_int4(w, group_size)  # one fused pass on the GPU
+        return layer, suffix, packed, scale, packed_k, w.shape[0], w.shape[1]
     qt = formats.quantize(w, formats.QuantConfig(bits=4, granularity="group", group_size=group_size))
     packed, packed_k = pack.pack_int4(qt.qweight)
     return layer, suffix, packed.contiguous(), qt.scale.contiguous(), packed_k, w.shape[0], w.shape[1]
