@@ -326,6 +326,8 @@ def run_ours(args) -> None:
     assert _C.device_errors() == 0, "device error flag set by the chained batched GEMV"
     chained_gbs = csteps * bytes_per_step / (cs.elapsed_time(ce) / 1e3) / 1e9
 
+    gemm_m8 = run_gemm_m8(layers, device) if args.gemm_m8 else None
+
     # ---- e2e through the public streaming API (weights from the pinned arena)
     e2e = run_e2e(args, layers, device, world, dist)
     del layers
@@ -358,6 +360,7 @@ def run_ours(args) -> None:
                    "l2": "inputs larger than L2 (weights far above the 126 MB L2), no flush",
                    "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "steps": csteps,
                                          "note": "each down_proj reads its gate_proj output (in-kernel dependency)"},
+                   "gemm_m8": gemm_m8,
                    "decode": decode,
                    "decode_14b_tp": decode_tp,
                    "parallelism": f"{world} independent replicas (no collective)"},
@@ -371,6 +374,53 @@ def run_ours(args) -> None:
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def run_gemm_m8(layers, device, reps: int = 20) -> dict:
+    """configs[4]'s batch-8 variant on the headline stream: the same 64 layer
+    copies x (gate, down), each GEMM multiplying 8 token rows in one pass over
+    the weights (soinfer_gemm_w4a16), 128 launches captured in one CUDA graph."""
+    from soinfer import _C
+
+    M = 8
+    gen = torch.Generator(device=device).manual_seed(99)
+    Xg = torch.randn(M, H, generator=gen, device=device).half()
+    Xd = torch.randn(M, I, generator=gen, device=device).half()
+    Yg = [torch.empty(M, I, dtype=torch.float16, device=device) for _ in layers]
+    Yd = [torch.empty(M, H, dtype=torch.float16, device=device) for _ in layers]
+
+    def step():
+        for li, (gw, gs, dw, ds) in enumerate(layers):
+            _C.gemm_w4a16(gw, gs, Xg, H, G, out=Yg[li])
+            _C.gemm_w4a16(dw, ds, Xd, I, G, out=Yd[li])
+
+    st = torch.cuda.Stream(device)
+    st.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(st):
+        step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            step()
+        for _ in range(3):
+            graph.replay()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        for _ in range(reps):
+            graph.replay()
+        e.record(st)
+    torch.cuda.synchronize(device)
+    assert _C.device_errors() == 0, "device error flag set by the multi-token GEMM"
+    ms = s.elapsed_time(e) / reps
+    L = len(layers)
+    w_bytes = 2 * L * (I * H // 2 + I * H // 128 * 4)
+    act_bytes = L * M * 2 * (H + I) * 2
+    del graph
+    return {"m": M, "value": round((w_bytes + act_bytes) / (ms / 1e3) / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "gemms_per_step": 2 * L,
+            "token_gemvs_per_s": round(2 * L * M / (ms / 1e3), 1),
+            "note": "each launch = 8 tokens x one INT4 g128 matrix (mma.sync columns carry the tokens), "
+                    "128 launches in one CUDA graph"}
 
 
 def run_e2e(args, layers, device, world, dist) -> dict:
@@ -546,6 +596,7 @@ def main() -> None:
     ap.add_argument("--decode", type=int, default=1, help="also measure configs[3] decode tok/s (reported in config)")
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
+    ap.add_argument("--gemm-m8", type=int, default=1, help="also measure the batch-8 GEMM stream (in config)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
     ap.add_argument("--tp-tokens", type=int, default=256)
     ap.add_argument("--tp-nccl", type=int, default=0, help="TP collectives through NCCL instead of the peer exchange")

@@ -92,6 +92,8 @@ int soinfer_device_errors(int* flags) {
   *flags |= f;
   if (int st = cuda_result(read_and_clear_tp_error(&f), "device_errors")) return st;
   *flags |= f;
+  if (int st = cuda_result(read_and_clear_gemm_w4_error(&f), "device_errors")) return st;
+  *flags |= f;
   return SOINFER_OK;
 }
 
@@ -632,6 +634,40 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                                                 num_q_heads, num_kv_heads, max_seq_len, head_dim, pos_dev, workspace,
                                                 as_stream(stream)),
                      name);
+}
+
+int soinfer_gemm_w4a16(const uint8_t* Wq, const float* scale, const soinfer_half* X, int64_t ldx, soinfer_half* Y,
+                       int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t num_groups,
+                       void* stream) {
+  const char* name = "gemm_w4a16";
+  if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
+  REQUIRE(M >= 0 && M <= 8, "%s: M (tokens) must be in [0, 8]", name);
+  REQUIRE(N >= 0, "%s: N must be >= 0", name);
+  if (M == 0 || N == 0) return SOINFER_OK;
+  REQUIRE(Wq && scale && X && Y, "%s: null pointer", name);
+  REQUIRE(ldx >= K && ldy >= N, "%s: row strides must cover K / N", name);
+  REQUIRE(aligned(Wq, 4) && aligned(scale, 4) && aligned(X, 2) && aligned(Y, 2), "%s: misaligned pointer", name);
+  cudaStream_t st = as_stream(stream);
+  const bool fast = plan_gemm_w4(M, N, K, group_size, num_groups) && aligned(Wq, 16) && aligned(scale, 16) &&
+                    aligned(X, 16) && ldx % 8 == 0;
+  if (fast) {
+    const cudaError_t e = launch_gemm_w4(Wq, scale, as_half(X), ldx, as_half(Y), ldy, M, N, K, group_size,
+                                         num_groups, st);
+    if (e != cudaErrorNotSupported) return cuda_result(e, name);
+  }
+  // per-token fallback: the single-token GEMV on each row of X
+  RowSource src;
+  src.W = Wq;
+  src.S = scale;
+  src.rows1 = N;
+  src.row_bytes = int4_row_bytes(K);
+  src.num_groups = num_groups;
+  for (int64_t m = 0; m < M; ++m)
+    if (int rc = cuda_result(launch_gemv_w4(RowMode::kPlain, src, as_half(X) + m * ldx, as_half(Y) + m * ldy, N, K,
+                                            group_size, st),
+                             name))
+      return rc;
+  return SOINFER_OK;
 }
 
 int soinfer_quantize_pack_int4(const void* w, int32_t dtype, int64_t N, int64_t K, int64_t ld, int64_t group_size,

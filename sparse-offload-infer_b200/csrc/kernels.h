@@ -43,6 +43,13 @@ struct LaunchOpts {
 cudaError_t launch_gemv_w4(RowMode mode, const RowSource& src, const half* x, half* y, int64_t nrows,
                            int64_t K, int64_t group_size, cudaStream_t stream, LaunchOpts opts = {});
 
+// Multi-token INT4 GEMM (gemm_w4.cu): Y[m, :] = W X[m, :] for m < M <= 8 in one pass over W.
+// plan_gemm_w4: whether the one-pass kernel takes the shape (else run per token).
+bool plan_gemm_w4(int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t G);
+cudaError_t launch_gemm_w4(const uint8_t* W, const float* S, const half* X, int64_t ldx, half* Y, int64_t ldy,
+                           int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t G, cudaStream_t stream);
+cudaError_t read_and_clear_gemm_w4_error(int* out);
+
 // Group-wise INT4 quantization + AWQ packing of w [N, K] (row stride ld; dtype 0 fp32, 1 fp16,
 // 2 bf16): packed uint8 [N, ceil(Kp/8)*4], scale fp32 [N, Kp/g], Kp = K rounded up to g
 // (g a power of two in [8, 256]).  Bit-exact with the reference's CPU torch quantizer.

@@ -70,6 +70,7 @@ _SIGNATURES = {
     "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
     "soinfer_quantize_pack_int4": (_INT, [_P, ctypes.c_int32, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "soinfer_gemm_w4a16": (_INT, [_P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "soinfer_peer_buffer_bytes": (_I64, [_I64, ctypes.c_int32]),
     "soinfer_peer_buffer_create": (_INT, [_I64, _P, _P]),
     "soinfer_peer_buffer_open": (_INT, [_P, _P]),
@@ -841,6 +842,29 @@ def decode_attention(q, k_cache, v_cache, cur_len: int, out: torch.Tensor | None
         _call("soinfer_decode_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(y), nq, nkv, max_seq, hd,
               cur_len, ws.data_ptr(), ws.numel(), _stream(dev))
     return y
+
+
+# ------------------------------------------------------------ multi-token GEMM
+def gemm_w4a16(Wq_packed, scale, X, K: int, group_size: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Y [M, N] fp16 = X [M, K] (fp16, M <= 8 tokens) times the INT4 weights'
+    transpose -- every token's reference GEMV, one pass over the weights."""
+    name = "gemm_w4a16"
+    _check(Wq_packed.is_cuda and Wq_packed.dtype == torch.uint8 and Wq_packed.is_contiguous() and Wq_packed.dim() == 2,
+           name, "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
+    _check(Wq_packed.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
+    _f32(scale, name + "(scale)")
+    _check(scale.dim() == 2 and scale.size(0) == Wq_packed.size(0), name, ": scale must be 2D [N, num_groups]")
+    _f16(X, name + "(X)")
+    _check(X.dim() == 2 and X.size(1) == K and X.stride(1) == 1 and 1 <= X.size(0) <= 8, name,
+           ": X must be [M <= 8, K] with unit K stride")
+    dev = _same_device(Wq_packed, scale, X)
+    M, N = X.size(0), Wq_packed.size(0)
+    Y = out if out is not None else torch.empty(M, N, dtype=torch.float16, device=dev)
+    _check(Y.shape == (M, N) and Y.stride(1) == 1 and Y.dtype == torch.float16, name, ": out must be fp16 [M, N]")
+    with torch.cuda.device(dev):
+        _call("soinfer_gemm_w4a16", _ptr(Wq_packed), _ptr(scale), _ptr(X), X.stride(0), _ptr(Y), Y.stride(0), M, N,
+              K, group_size, scale.size(1), _stream(dev))
+    return Y
 
 
 # ------------------------------------------------------------ load-time quantization

@@ -214,3 +214,9 @@ def head_norm_rope(q, k, v, q_norm, k_norm, cos_vals, sin_vals, k_cache, v_cache
     """B200 addition: qk_norm of q and k, RoPE of both, q in place, k / v appended to the caches at pos (or the
     device position pos_dev with cos / sin tables) -- one kernel for reference ops.py:238-250's sequence."""
     _C.head_norm_rope(q, k, v, q_norm, k_norm, cos_vals, sin_vals, k_cache, v_cache, pos, pos_dev, eps)
+
+
+def gemm_w4a16(Wq_packed: torch.Tensor, scale: torch.Tensor, X: torch.Tensor, K: int, group_size: int) -> torch.Tensor:
+    """B200 addition: batched decode -- Y [M, N] = X [M, K] W^T for M <= 8 tokens in one pass over the INT4
+    weights (each row of Y is the reference's gemv_w4a16_group_lop3 of that token)."""
+    return _C.gemm_w4a16(Wq_packed, scale, X, K, group_size)

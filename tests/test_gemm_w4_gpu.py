@@ -1,0 +1,72 @@
+"""Multi-token INT4 GEMM (soinfer_gemm_w4a16: M <= 8 tokens, one pass over
+the weights) on the GPU: every token row against the float64 oracle GEMV at
+the configs' shapes (1.7B and 14B matrices, 14B TP shards), group sizes 128
+and 256, M = 1..8, strided X / Y rows, the per-token fallback shapes, exact
+basis-vector probes, determinism across launches, and argument checks."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import reference_port as port
+from soinfer import _C, ops
+from soinfer.quant import formats, pack
+from tests.helpers import assert_close, int4_weights
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _case(n, k, g, m, seed):
+    p, s, pk = int4_weights(n, k, g, seed=seed)
+    gen = torch.Generator().manual_seed(seed + 1)
+    X = torch.randn(m, pk, generator=gen).half()
+    return p, s, pk, X
+
+
+@pytest.mark.parametrize("n,k,g", [(6144, 2048, 128), (2048, 6144, 128), (3072, 2048, 128), (17408, 5120, 128),
+                                   (5120, 2560, 128), (4352, 5120, 128), (1024, 4096, 256), (33, 256, 128),
+                                   (5120, 17408, 128), (40, 300, 32)])
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_tokens_match_oracle(n, k, g, m):
+    p, s, pk, X = _case(n, k, g, m, seed=n + k + m)
+    Y = ops.gemm_w4a16(p.to(DEV), s.to(DEV), X.to(DEV), pk, g)
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    for i in range(m):
+        ref = port.gemv_w4a16(p.numpy(), s.numpy(), X[i].numpy(), pk, g)
+        assert_close(Y[i], ref, f"gemm {n}x{k} g{g} token {i}/{m}")
+
+
+def test_strided_rows_deterministic_and_out():
+    p, s, pk, X = _case(6144, 2048, 128, 8, seed=3)
+    big = torch.zeros(8, 2048 + 64, dtype=torch.float16, device=DEV)
+    big[:, :2048] = X.to(DEV)
+    Xs = big[:, :2048]                       # row stride 2112
+    out = torch.empty(8, 6144 + 8, dtype=torch.float16, device=DEV)[:, :6144]
+    a = _C.gemm_w4a16(p.to(DEV), s.to(DEV), Xs, pk, 128, out=out)
+    b = ops.gemm_w4a16(p.to(DEV), s.to(DEV), X.to(DEV), pk, 128)
+    assert torch.equal(a, b), "strided X / Y or a second launch changed the result"
+
+
+def test_basis_vectors_exact():
+    torch.manual_seed(2)
+    N, K = 64, 1024
+    W = torch.randn(N, K) * 3.0
+    qt = formats.quantize(W, formats.QuantConfig(bits=4, granularity="group", group_size=128))
+    packed, pk = pack.pack_int4(qt.qweight)
+    deq = formats.dequantize(qt)
+    cols = [0, 7, 129, 513, 1000, 1023, 640, 77]
+    X = torch.zeros(8, K, dtype=torch.float16)
+    for i, c in enumerate(cols):
+        X[i, c] = 1.0
+    Y = ops.gemm_w4a16(packed.to(DEV), qt.scale.to(DEV), X.to(DEV), pk, 128).cpu()
+    for i, c in enumerate(cols):
+        assert torch.equal(Y[i], deq[:, c].half()), f"column {c}"
+
+
+def test_argument_checks():
+    p, s, pk, X = _case(64, 256, 128, 9, seed=1)
+    with pytest.raises(RuntimeError):
+        ops.gemm_w4a16(p.to(DEV), s.to(DEV), X.to(DEV), pk, 128)  # 9 tokens
+    lib = _C.lib()
+    assert lib.soinfer_gemm_w4a16(None, None, None, 256, None, 64, 9, 64, 256, 128, 2, None) == 1
