@@ -109,6 +109,13 @@ typedef struct soinfer_gemv_task {
    * task of the batch with the same N. */
   const soinfer_half* residual;
   const soinfer_half* glu_gate;
+  /* Optional prologue (NULL = off): the task multiplies RMSNorm(x) * norm_weight
+   * (fp16 [K], eps norm_eps) instead of x -- each CTA normalises x in shared
+   * memory as soinfer_rmsnorm computes it (v * rsqrt(mean(v^2) + eps) * w,
+   * rounded to fp16), so the normalised vector is never written.  Needs the
+   * persistent path (K and group_size multiples of 128). */
+  const soinfer_half* norm_weight;
+  float norm_eps;
 } soinfer_gemv_task;
 
 /* Bytes of zero-initialised device workspace soinfer_gemv_w4a16_batch needs

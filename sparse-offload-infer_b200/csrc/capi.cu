@@ -108,7 +108,7 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
   if (num_tasks == 0) return SOINFER_OK;
   REQUIRE(tasks, "%s: null task list", name);
   bool fast = true;
-  int npeer = 0;
+  int npeer = 0, nnorm = 0;
   for (int64_t i = 0; i < num_tasks; ++i) {
     const soinfer_gemv_task& t = tasks[i];
     char tn[64];
@@ -125,6 +125,12 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
       REQUIRE(t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.Wq, 16) && aligned(t.x, 16) &&
                   aligned(t.scale, 4),
               "%s: a peer task needs K and group_size multiples of 128 and 16-byte aligned rows / x", tn);
+    }
+    if (t.norm_weight) {
+      REQUIRE(t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.norm_weight, 16) && t.norm_eps >= 0.f,
+              "%s: a norm prologue needs K and group_size multiples of 128, a 16-byte aligned weight and eps >= 0",
+              tn);
+      ++nnorm;
     }
     for (int64_t j = 0; j < i; ++j) {  // an epilogue input made in this batch must share the row split
       if (tasks[j].y && (tasks[j].y == t.glu_gate || tasks[j].y == t.residual))
@@ -161,6 +167,8 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
       d.resid = as_half(t.residual);
       d.glu = as_half(t.glu_gate);
       d.peer = t.y ? 0 : 1;
+      d.norm_w = as_half(t.norm_weight);
+      d.eps = t.norm_eps;
     }
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -171,6 +179,8 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
     }
   }
   // fallback: ordered single-GEMV launches (stream order satisfies every dep)
+  REQUIRE(nnorm == 0, "%s: a norm prologue needs the persistent path (K, group size multiples of 128; rows per "
+                      "CTA <= 128)", name);
   for (int64_t i = 0; i < num_tasks; ++i) {
     const soinfer_gemv_task& t = tasks[i];
     RowSource src;

@@ -457,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem;                                                  // [ring_bytes]
   uint8_t* xbuf = smem + B.ring_bytes;                                   // [2][x_bytes]
   float* red = reinterpret_cast<float*>(xbuf + 2 * B.x_bytes);          // [2][kGroupWarps][kRedRows]
+  uint8_t* nscr = reinterpret_cast<uint8_t*>(red) + kRedBytes;          // [norm_bytes] norm weights
   __shared__ uint64_t full[kMaxItems], empty[kMaxItems];
   __shared__ uint64_t xfull[2], xempty[2], rfull[2], rempty[2];
   __shared__ int item_off[kMaxItems];
@@ -531,8 +532,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint4* src = reinterpret_cast<const uint4*>(tk.x);
       uint4* dst = reinterpret_cast<uint4*>(xbuf + xs * B.x_bytes);
       const int n16 = tk.K / 8;
-      for (int u = lane; u < n16; u += 32) cp_async_16(dst + u, src + u);
-      cp_async_arrive_noinc(&xfull[xs]);
+      if (tk.norm_w == nullptr) {
+        for (int u = lane; u < n16; u += 32) cp_async_16(dst + u, src + u);
+        cp_async_arrive_noinc(&xfull[xs]);
+      } else {
+        // RMSNorm prologue: x and the norm weights land, then the warp
+        // normalises x in place -- f * inv * w in fp32, rounded to fp16, as
+        // the rmsnorm kernel does -- and arrives (32 arrivals, like the copies)
+        uint4* wsc = reinterpret_cast<uint4*>(nscr);
+        const uint4* wsrc = reinterpret_cast<const uint4*>(tk.norm_w);
+        for (int u = lane; u < n16; u += 32) {
+          cp_async_16(dst + u, src + u);
+          cp_async_16(wsc + u, wsrc + u);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+        float ss = 0.f;
+        for (int u = lane; u < n16; u += 32) {
+          const uint4 v = dst[u];
+          const half2* h = reinterpret_cast<const half2*>(&v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss / (float)tk.K + tk.eps);
+        for (int u = lane; u < n16; u += 32) {
+          const uint4 v = dst[u], wv = wsc[u];
+          const half2* h = reinterpret_cast<const half2*>(&v);
+          const half2* wh = reinterpret_cast<const half2*>(&wv);
+          uint4 o;
+          half2* oh = reinterpret_cast<half2*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(h[j]), gw = __half22float2(wh[j]);
+            oh[j] = __floats2half2_rn(f.x * inv * gw.x, f.y * inv * gw.y);
+          }
+          dst[u] = o;
+        }
+        __syncwarp();
+        mbar_arrive(&xfull[xs]);
+      }
       ++a;
     }
     if (stop) raise_abort(abort_flag);
@@ -684,6 +727,7 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
     if (B.tasks[i].dep >= 0) B.tasks[B.tasks[i].dep].publish = 1;
   int npeer = 0;
   B.any_cp_async = 0;
+  int norm_k = 0;
   for (int i = 0; i < B.num; ++i) {
     GemvBatchTask& tk = B.tasks[i];
     tk.rows_per_cta = (tk.N + sms - 1) / sms;
@@ -710,6 +754,7 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
       tk.scale_plain = 1;
     }
     if (tk.peer) ++npeer;
+    if (tk.norm_w != nullptr) norm_k = tk.K > norm_k ? tk.K : norm_k;
     if (tk.scale_plain && !(tk.nsegs > 1 && tk.G % 4 == 0 && (tk.ks / tk.cpg) % 4 == 0 &&
                             ((chunks - (tk.nsegs - 1) * tk.ks) / tk.cpg) % 4 == 0))
       B.any_cp_async = 1;  // the producer's seg_bulk test fails for some item of this task
@@ -719,9 +764,10 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
   B.grid = sms;
   B.x_bytes = round128(max_k * 2);
   const int static_smem = 3072;  // mbarriers, item offsets, per-warp biases, flags (~2 KB used)
-  B.ring_bytes = ((kSmemLimit - static_smem - 2 * B.x_bytes - kRedBytes - 256) / 128) * 128;
+  B.norm_bytes = norm_k > 0 ? round128(norm_k * 2) : 0;
+  B.ring_bytes = ((kSmemLimit - static_smem - 2 * B.x_bytes - kRedBytes - B.norm_bytes - 256) / 128) * 128;
   if (B.ring_bytes < kMaxItemBytes + 128) return false;
-  B.smem_bytes = B.ring_bytes + 2 * B.x_bytes + kRedBytes;
+  B.smem_bytes = B.ring_bytes + 2 * B.x_bytes + kRedBytes + B.norm_bytes;
   return true;
 }
 
@@ -761,6 +807,7 @@ cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStrea
     S.ring_bytes = B.ring_bytes;
     S.smem_bytes = B.smem_bytes;
     S.any_cp_async = B.any_cp_async;
+    S.norm_bytes = B.norm_bytes;
     S.peers = B.peers;
     for (int i = 0; i < B.num; ++i) S.tasks[i] = B.tasks[i];
     return launch_params(S, counters, stream);

@@ -98,6 +98,8 @@ struct GemvBatchTask {
   const half* resid;  // optional epilogue: y = fp16(resid + fp16(dot))
   const half* glu;    // optional epilogue: y = fp16(silu(glu) * fp16(dot)), applied before resid
   int peer;           // y == nullptr: rows go to every rank's exchange inbox (PeerSet), the last CTA signals
+  const half* norm_w; // optional prologue: x -> fp16(x * rsqrt(mean(x^2) + eps) * norm_w) in shared memory
+  float eps;
 };
 constexpr int kMaxBatchTasks = 256;
 constexpr int kSmallBatchTasks = 8;  // decode-layer batches: a small kernel-parameter block launches faster
@@ -105,6 +107,7 @@ template <int MaxTasks>
 struct GemvBatchParamsT {
   int num, grid, x_bytes, ring_bytes, smem_bytes;
   int any_cp_async;  // some task stages scales with cp.async (proxy fence before later bulk copies)
+  int norm_bytes;    // shared scratch for the norm weights of prologue tasks (0: none)
   PeerSet peers;  // used by a peer task (at most one per batch)
   GemvBatchTask tasks[MaxTasks];
 };

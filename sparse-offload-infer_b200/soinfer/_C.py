@@ -274,7 +274,8 @@ def gemv_fp16_argmax(W, x, logits: bool = False, out_idx=None):
 
 class _GemvTask(ctypes.Structure):
     _fields_ = [("Wq", _P), ("scale", _P), ("x", _P), ("y", _P), ("N", _I64), ("K", _I64), ("group_size", _I64),
-                ("num_groups", _I64), ("dep", _I64), ("residual", _P), ("glu_gate", _P)]
+                ("num_groups", _I64), ("dep", _I64), ("residual", _P), ("glu_gate", _P), ("norm_weight", _P),
+                ("norm_eps", _F32)]
 
 
 MAX_BATCH_TASKS = 256
@@ -283,10 +284,12 @@ MAX_BATCH_TASKS = 256
 class GemvBatch:
     """A prepared list of INT4 GEMVs run as one persistent kernel
     (soinfer_gemv_w4a16_batch).  tasks: sequence of
-    (Wq_packed, scale, x, y, K, group_size, dep[, residual[, glu_gate]]) with
-    dep = index of an earlier task whose output feeds this task's x, or -1;
-    residual / glu_gate (fp16 [N] or None) add the epilogues
-    y = residual + fp16(silu(glu_gate) * fp16(W x)) of the C ABI.  The tensors
+    (Wq_packed, scale, x, y, K, group_size, dep[, residual[, glu_gate[, (norm_weight, eps)]]])
+    with dep = index of an earlier task whose output feeds this task's x, or
+    -1; residual / glu_gate (fp16 [N] or None) add the epilogues
+    y = residual + fp16(silu(glu_gate) * fp16(W x)) of the C ABI; a
+    (norm_weight fp16 [K], eps) pair multiplies RMSNorm(x) * norm_weight
+    instead of x (computed in the kernel).  The tensors
     must stay alive and keep their storage while the batch is used.
     peers (a PeerSetStruct): tensor-parallel batch (soinfer_gemv_w4a16_batch_tp)
     in which one task may have y = None -- its rows go to every rank's
@@ -301,6 +304,10 @@ class GemvBatch:
             W, scale, x, y, K, group_size, dep = task[:7]
             residual = task[7] if len(task) > 7 else None
             glu = task[8] if len(task) > 8 else None
+            norm = task[9] if len(task) > 9 else None
+            if norm is not None:
+                _f16(norm[0], f"gemv_w4a16_batch[task {i}](norm_weight)")
+                _check(norm[0].numel() == K, f"gemv_w4a16_batch[task {i}]", ": norm_weight must hold K values")
             name = f"gemv_w4a16_batch[task {i}]"
             _check(W.is_cuda and W.dtype == torch.uint8 and W.is_contiguous() and W.dim() == 2, name,
                    "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
@@ -323,7 +330,9 @@ class GemvBatch:
             _check(dev is None or d == dev, name, ": all tasks must be on one device")
             dev = d
             arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), _ptr(y), W.size(0), K, group_size,
-                               scale.size(1), dep, _ptr(residual), _ptr(glu))
+                               scale.size(1), dep, _ptr(residual), _ptr(glu),
+                               _ptr(norm[0]) if norm is not None else None,
+                               float(norm[1]) if norm is not None else 0.0)
         self._arr, self.n, self.device = arr, n, dev
         self._keep = [tuple(t) for t in tasks]
         self.peers = peers
@@ -854,7 +863,7 @@ def gemm_w4a16(Wq_packed, scale, X, K: int, group_size: int, out: torch.Tensor |
     _check(Wq_packed.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
     _f32(scale, name + "(scale)")
     _check(scale.dim() == 2 and scale.size(0) == Wq_packed.size(0), name, ": scale must be 2D [N, num_groups]")
-    _f16(X, name + "(X)")
+    _check(X.is_cuda and X.dtype == torch.float16, name, "(X): must be a float16 CUDA tensor")
     _check(X.dim() == 2 and X.size(1) == K and X.stride(1) == 1 and 1 <= X.size(0) <= 8, name,
            ": X must be [M <= 8, K] with unit K stride")
     dev = _same_device(Wq_packed, scale, X)

@@ -150,22 +150,44 @@ class WeightPipeline:
         self._prefetch_into(self.cur_buf, self.cur_name)
         return self.model.resident[name], self.model.matrices[name]
 
-    def next_gemvs(self, x_in: torch.Tensor, count: int) -> list[torch.Tensor]:
+    def _batched(self, count: int) -> list[str] | None:
+        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(count)]
+        return names if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names) else None
+
+    def next_gemvs(self, x_in: torch.Tensor, count: int, norm: tuple | None = None) -> list[torch.Tensor]:
         """The next `count` GEMVs, all on the same input.  When they are all
         HBM-resident they run as one persistent batched launch (one kernel for
-        q / k / v or gate / up); otherwise one after another."""
-        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(count)]
-        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+        q / k / v or gate / up); otherwise one after another.  norm =
+        (weight, eps): the GEMVs take rmsnorm(x_in) * weight -- computed inside
+        the batched kernel, or by the rmsnorm op before the unbatched GEMVs."""
+        names = self._batched(count)
+        if names is not None:
             tasks = []
             for name in names:
                 m = self.model.matrices[name]
                 y = torch.empty(m.n, dtype=torch.float16, device=x_in.device)
-                tasks.append((self.model.resident[name], m.scale, x_in, y, m.packed_k, self.model.group_size, -1))
+                tasks.append((self.model.resident[name], m.scale, x_in, y, m.packed_k, self.model.group_size, -1,
+                              None, None, norm))
             for _ in range(count):
                 self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
             _C.gemv_w4a16_batch(tasks)
             return [t[3] for t in tasks]
+        if norm is not None:
+            x_in = ops.rmsnorm(x_in.unsqueeze(0), norm[0], norm[1]).squeeze(0)
         return [self.next_gemv(x_in) for _ in range(count)]
+
+    def next_gemv_residual(self, x_in: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """residual + (next weight) x_in: one batched launch with the residual
+        epilogue when resident, else the GEMV and an add."""
+        names = self._batched(1)
+        if names is not None:
+            m = self.model.matrices[names[0]]
+            y = torch.empty(m.n, dtype=torch.float16, device=x_in.device)
+            self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
+            _C.gemv_w4a16_batch([(self.model.resident[names[0]], m.scale, x_in, y, m.packed_k, self.model.group_size,
+                                  -1, residual)])
+            return y
+        return residual + self.next_gemv(x_in)
 
     def next_glu(self, h3: torch.Tensor) -> torch.Tensor:
         """The next gate / up weights as fp16(silu(gate(h3)) * up(h3)): one batched
@@ -184,26 +206,34 @@ class WeightPipeline:
         gate, up = self.next_gemvs(h3, 2)
         return ops.swiglu(gate, up)
 
-    def next_mlp(self, h3: torch.Tensor, h2: torch.Tensor) -> torch.Tensor:
+    def next_mlp(self, h3: torch.Tensor | None, h2: torch.Tensor, norm: tuple | None = None) -> torch.Tensor:
         """The next gate / up / down weights as a dense SwiGLU MLP plus the
-        residual: h2 + down(fp16(silu(gate(h3)) * up(h3))).  Resident weights:
-        one persistent launch (up's epilogue applies SwiGLU, down depends on up
-        and adds the residual); otherwise three GEMVs, swiglu and an add."""
-        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(3)]
-        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+        residual: h2 + down(fp16(silu(gate(h3)) * up(h3))), with h3 =
+        rmsnorm(h2) * norm[0] computed inside the kernel when h3 is None.
+        Resident weights: one persistent launch (up's epilogue applies SwiGLU,
+        down depends on up and adds the residual); otherwise three GEMVs,
+        swiglu and an add."""
+        if h3 is None and norm is None:
+            raise ValueError("next_mlp needs h3 or the norm to compute it")
+        names = self._batched(3)
+        if names is not None:
             mg, mu, md = (self.model.matrices[n] for n in names)
             res, g = self.model.resident, self.model.group_size
-            dev = h3.device
+            dev = h2.device
+            xin = h3 if h3 is not None else h2
+            nrm = None if h3 is not None else norm
             gate = torch.empty(mg.n, dtype=torch.float16, device=dev)
             hidden = torch.empty(mu.n, dtype=torch.float16, device=dev)
             out = torch.empty(md.n, dtype=torch.float16, device=dev)
-            tasks = [(res[names[0]], mg.scale, h3, gate, mg.packed_k, g, -1),
-                     (res[names[1]], mu.scale, h3, hidden, mu.packed_k, g, -1, None, gate),
+            tasks = [(res[names[0]], mg.scale, xin, gate, mg.packed_k, g, -1, None, None, nrm),
+                     (res[names[1]], mu.scale, xin, hidden, mu.packed_k, g, -1, None, gate, nrm),
                      (res[names[2]], md.scale, hidden, out, md.packed_k, g, 1, h2)]
             for _ in range(3):
                 self.cur_buf, self.cur_name = 1 - self.cur_buf, self._advance()
             _C.gemv_w4a16_batch(tasks)
             return out
+        if h3 is None:
+            h3 = ops.rmsnorm(h2.unsqueeze(0), norm[0], norm[1]).squeeze(0)
         gate, up = self.next_gemvs(h3, 2)
         return h2 + self.next_gemv(ops.swiglu(gate, up))
 
@@ -223,7 +253,7 @@ class DevicePosition:
 
 def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos: int,
                      k_cache: torch.Tensor, v_cache: torch.Tensor, reduce_o=None, h_in: torch.Tensor | None = None,
-                     o_block=None) -> tuple[torch.Tensor, torch.Tensor]:
+                     o_block=None, fuse_norms: bool = False) -> tuple[torch.Tensor, torch.Tensor | None]:
     """rmsnorm -> q/k/v GEMVs -> q/k norm + RoPE + KV append (one kernel) ->
     GQA decode attention -> o GEMV -> residual add + post-attention rmsnorm
     (one kernel).  Returns (h2 = x + o, h3 = rmsnorm(h2)).  Tensor-parallel
@@ -231,12 +261,17 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
     sum of row-parallel partials); h_in is rmsnorm(x) when already computed;
     o_block(attn, x, post_norm_weight, eps) -> (h2, h3) replaces the o GEMV,
     the residual add and the rmsnorm (it consumes the o weight from the
-    pipeline itself)."""
+    pipeline itself).  fuse_norms: the input rmsnorm runs inside the q/k/v
+    batched kernel, the o GEMV adds the residual in its epilogue, and h3 is
+    returned as None (the MLP normalises h2 in its own kernel)."""
     NQ, NKV, HD = model.num_attention_heads, model.num_key_value_heads, model.head_dim
     eps = model.rms_norm_eps
     norms = model.layer_norms[layer_idx]
-    h = h_in if h_in is not None else ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
-    q, k, v = pipeline.next_gemvs(h, 3)
+    if fuse_norms and h_in is None:
+        q, k, v = pipeline.next_gemvs(x_flat, 3, norm=(norms["input_layernorm"], eps))
+    else:
+        h = h_in if h_in is not None else ops.rmsnorm(x_flat.unsqueeze(0), norms["input_layernorm"], eps).squeeze(0)
+        q, k, v = pipeline.next_gemvs(h, 3)
     q, k, v = q.view(NQ, HD), k.view(NKV, HD), v.view(NKV, HD)
     if isinstance(pos, DevicePosition):
         ops.head_norm_rope(q, k, v, norms["q_norm"], norms["k_norm"], pos.cos_table, pos.sin_table, k_cache, v_cache,
@@ -249,6 +284,8 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
         attn = ops.decode_attention(q, k_cache, v_cache, pos + 1).reshape(NQ * HD)
     if o_block is not None:
         return o_block(attn, x_flat, norms["post_attention_layernorm"], eps)
+    if fuse_norms and reduce_o is None:
+        return pipeline.next_gemv_residual(attn, x_flat), None
     o = pipeline.next_gemv(attn)
     if reduce_o is not None:
         o = reduce_o(o)
@@ -259,9 +296,11 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
 def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
                                 x_flat: torch.Tensor, pos: int, k_cache: torch.Tensor,
                                 v_cache: torch.Tensor) -> torch.Tensor:
-    """Dense layer: all 7 linear weights through the pipeline (reference generate.py:141-182)."""
-    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
-    return pipeline.next_mlp(h3, h2)
+    """Dense layer: all 7 linear weights through the pipeline (reference generate.py:141-182).
+    Both rmsnorms run inside the batched GEMV kernels (q/k/v and gate/up)."""
+    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, fuse_norms=True)
+    return pipeline.next_mlp(h3, h2, norm=(model.layer_norms[layer_idx]["post_attention_layernorm"],
+                                            model.rms_norm_eps))
 
 
 # --------------------------------------------------------------------- DIP

@@ -168,3 +168,31 @@ def test_glu_and_residual_epilogues_equal_unfused():
     _C.gemv_w4a16_batch([(p.to(DEV), s.to(DEV), x, y, pk, 8, -1, r, gv)])
     plain = ops.gemv_w4a16_group_lop3(p.to(DEV), s.to(DEV), x, pk, 8)
     assert torch.equal(y, r + ops.swiglu(gv, plain))
+
+
+@pytest.mark.parametrize("k", [2048, 5120, 6144])
+def test_norm_prologue_matches_rmsnorm_then_gemv(k):
+    """Tasks with a norm prologue multiply rmsnorm(x) * w (computed inside the
+    kernel) -- against the oracle on the oracle's rmsnorm, and against the
+    separate rmsnorm op followed by the plain batched GEMV (the same fp16
+    vector up to the sum-of-squares order: within one fp16 ulp per element)."""
+    n = 3072
+    p, s, pk = int4_weights(n, k, 128, seed=k)
+    gen = torch.Generator().manual_seed(k + 1)
+    x = (torch.randn(k, generator=gen) * 3).half()
+    w = (torch.rand(k, generator=gen) + 0.5).half()
+    eps = 1e-6
+    y = torch.empty(n, dtype=torch.float16, device=DEV)
+    y2 = torch.empty(n, dtype=torch.float16, device=DEV)
+    P, S, X, Wn = p.to(DEV), s.to(DEV), x.to(DEV), w.to(DEV)
+    _C.gemv_w4a16_batch([(P, S, X, y, pk, 128, -1, None, None, (Wn, eps)),
+                         (P, S, X, y2, pk, 128, -1, None, None, (Wn, eps))])
+    h = ops.rmsnorm(X.unsqueeze(0), Wn, eps).squeeze(0)
+    ref_sep = torch.empty(n, dtype=torch.float16, device=DEV)
+    _C.gemv_w4a16_batch([(P, S, h, ref_sep, pk, 128, -1)])
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    assert torch.equal(y, y2), "two tasks with the same prologue differ"
+    hn = port.rmsnorm(x.numpy()[None], w.numpy(), eps)[0]
+    assert_close(y, port.gemv_w4a16(p.numpy(), s.numpy(), hn, pk, 128), f"norm prologue K={k}", max_abs=None)
+    assert_close(y, ref_sep.double(), f"norm prologue vs rmsnorm op K={k}", max_abs=None)
