@@ -333,6 +333,7 @@ def run_ours(args) -> None:
     del layers
     decode = run_decode(args, device) if args.decode and rank == 0 and world == 1 else None
     decode_tp = run_decode_tp(args, device, world, rank, dist) if args.tp_decode else None
+    decode_int8 = run_decode_int8(args, device) if args.int8_decode and world == 1 else None
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -363,6 +364,7 @@ def run_ours(args) -> None:
                    "gemm_m8": gemm_m8,
                    "decode": decode,
                    "decode_14b_tp": decode_tp,
+                   "decode_14b_int8": decode_int8,
                    "parallelism": f"{world} independent replicas (no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -583,6 +585,35 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
                 "sums + residual + RMSNorm (soinfer.runtime.tp.PeerExchange)" if world > 1 else "single GPU")}
 
 
+def run_decode_int8(args, device) -> dict:
+    """configs[4]'s INT8 per-channel variant: the 14B-shaped model with int8
+    rows and one fp32 scale per row (the reference's gemv_w8a16 per GEMV),
+    batch-1 greedy decode on one GPU, same prompt / token counts as the TP run."""
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import QWEN3_14B, synthetic_streaming_model
+
+    arch = QWEN3_14B
+    model = synthetic_streaming_model(arch, seed=2, resident=True, offload=False, include_dip=False, device=device,
+                                      bits=8)
+    weight_bytes = sum(t.numel() for t in model.resident.values()) + sum(
+        m.scale.numel() * 4 for m in model.matrices.values())
+    gd = gen.GraphDecoder(model, max_seq_len=4096)
+    prompt = torch.randint(0, arch.vocab_size, (args.tp_prompt,), generator=torch.Generator().manual_seed(1)).tolist()
+    gd.generate(prompt[:8], 4)
+    tm = {}
+    gd.generate(prompt, args.tp_tokens, timings=tm)
+    del gd, model
+    torch.cuda.empty_cache()
+    n = args.tp_tokens - 1
+    ms = tm["decode_ms"] / n
+    kv = 2 * arch.num_key_value_heads * arch.head_dim * 2 * arch.num_layers * (args.tp_prompt + args.tp_tokens / 2)
+    floor_bytes = weight_bytes + arch.vocab_size * arch.hidden_size * 2 + kv
+    return {"model": "Qwen3-14B-shaped, INT8 per-channel weights (int8 rows + fp32 row scale), resident in HBM",
+            "prompt_tokens": args.tp_prompt, "new_tokens": args.tp_tokens, "tok_s": round(n / (tm["decode_ms"] / 1e3), 1),
+            "ms_per_token": round(ms, 4), "weight_bytes": int(weight_bytes),
+            "hbm_floor_ms": round(floor_bytes / (measured_peaks().get("hbm_gbs") or 6650.0) / 1e6, 4)}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -597,6 +628,7 @@ def main() -> None:
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
     ap.add_argument("--gemm-m8", type=int, default=1, help="also measure the batch-8 GEMM stream (in config)")
+    ap.add_argument("--int8-decode", type=int, default=1, help="also measure the 14B INT8 per-channel decode (N=1)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
     ap.add_argument("--tp-tokens", type=int, default=256)
     ap.add_argument("--tp-nccl", type=int, default=0, help="TP collectives through NCCL instead of the peer exchange")

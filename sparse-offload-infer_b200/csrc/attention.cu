@@ -220,7 +220,7 @@ cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* ou
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  return launch_ex(kernel, dim3(nkv, nsplit, groups), dim3(kThreads), smem, stream, 1, false, q, kc, vc, out, ws_acc,
+  return launch_ex(kernel, dim3(nkv, nsplit, groups), dim3(kThreads), smem, stream, 1, true /* programmatic dependent: both kernels wait first */, q, kc, vc, out, ws_acc,
                    ws_ml, nq, nkv, max_seq, hd, cur_len, L, scale_log2, pos_dev);
 }
 
@@ -285,7 +285,7 @@ cudaError_t decode_attention_impl(const half* q, const half* kc, const half* vc,
   }
   if (e != cudaSuccess || nsplit == 1) return e;
   const int threads = ihd < 32 ? 32 : (ihd > 256 ? 256 : ihd);
-  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, false, ws_acc, ws_ml, out, ihd, nsplit,
+  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, true /* programmatic dependent: both kernels wait first */, ws_acc, ws_ml, out, ihd, nsplit,
                    L, max_seq, pos_dev);
 }
 

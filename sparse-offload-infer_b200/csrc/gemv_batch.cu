@@ -497,6 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
+  // let the next kernel (launched as a programmatic dependent; it waits for
+  // this grid's completion before touching memory) be scheduled early
+  pdl_launch_dependents();
 
   if (warp == kProducerWarp) {
     producer_loop(B, cta, lane, ring, full, empty, item_off, abort_flag);
@@ -702,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (stop) raise_abort(abort_flag);
   }
   __syncthreads();
-  if (tid == 0 && !s_abort) {
+  if (B.need_counters && tid == 0 && !s_abort) {
     __threadfence();
     const int done = atomicAdd(counters + B.num, 1);
     if (done == grid - 1) {  // every CTA is past every dependency wait: reset for the next launch
@@ -761,6 +764,8 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
     max_k = tk.K > max_k ? tk.K : max_k;
   }
   if (npeer > 1 || (npeer == 1 && B.peers.world < 1)) return false;
+  B.need_counters = npeer > 0 ? 1 : 0;
+  for (int i = 0; i < B.num; ++i) B.need_counters |= B.tasks[i].publish;
   B.grid = sms;
   B.x_bytes = round128(max_k * 2);
   const int static_smem = 3072;  // mbarriers, item offsets, per-warp biases, flags (~2 KB used)
@@ -808,6 +813,7 @@ cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStrea
     S.smem_bytes = B.smem_bytes;
     S.any_cp_async = B.any_cp_async;
     S.norm_bytes = B.norm_bytes;
+    S.need_counters = B.need_counters;
     S.peers = B.peers;
     for (int i = 0; i < B.num; ++i) S.tasks[i] = B.tasks[i];
     return launch_params(S, counters, stream);

@@ -12,6 +12,10 @@
 namespace soinfer {
 namespace {
 
+// Every kernel here starts with griddepcontrol.wait (before touching any
+// activation memory), so each is launched as a programmatic dependent: its
+// launch overlaps the tail of the kernel before it.
+constexpr bool kPdl = true;
 constexpr int kNormThreads = 256;
 
 // ADD: the normalised row is v = fp16(x + x2) (fp32 add, one rounding -- the
@@ -213,13 +217,13 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ matrix, const int
 
 cudaError_t launch_rmsnorm(const half* x, const half* w, half* out, int64_t rows, int64_t hidden, float eps,
                            cudaStream_t stream) {
-  return launch_ex(rmsnorm_kernel<false>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, false, x,
+  return launch_ex(rmsnorm_kernel<false>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, kPdl, x,
                    (const half*)nullptr, w, out, (half*)nullptr, hidden, eps);
 }
 
 cudaError_t launch_add_rmsnorm(const half* x, const half* x2, const half* w, half* out, half* sum_out, int64_t rows,
                                int64_t hidden, float eps, cudaStream_t stream) {
-  return launch_ex(rmsnorm_kernel<true>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, false, x, x2, w, out,
+  return launch_ex(rmsnorm_kernel<true>, dim3((unsigned)rows), dim3(kNormThreads), 0, stream, 1, kPdl, x, x2, w, out,
                    sum_out, hidden, eps);
 }
 
@@ -229,7 +233,7 @@ cudaError_t launch_swiglu(const half* gate, const half* up, const int32_t* idx, 
   int64_t blocks = (n + threads - 1) / threads;
   if (blocks > 1184) blocks = 1184;
   if (blocks < 1) blocks = 1;
-  return launch_ex(swiglu_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, false, gate, up, idx, out, n);
+  return launch_ex(swiglu_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, kPdl, gate, up, idx, out, n);
 }
 
 cudaError_t launch_add_half(const half* a, const half* b, half* out, int64_t n, cudaStream_t stream) {
@@ -237,7 +241,7 @@ cudaError_t launch_add_half(const half* a, const half* b, half* out, int64_t n, 
   int64_t blocks = (n + threads - 1) / threads;
   if (blocks > 1184) blocks = 1184;
   if (blocks < 1) blocks = 1;
-  return launch_ex(add_half_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, false, a, b, out, n);
+  return launch_ex(add_half_kernel, dim3((unsigned)blocks), dim3(threads), 0, stream, 1, kPdl, a, b, out, n);
 }
 
 cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const half* qw, const half* kw,
@@ -246,7 +250,7 @@ cudaError_t launch_head_norm_rope(half* q, const half* k, const half* v, const h
                                   int64_t table_rows, float eps, cudaStream_t stream) {
   const int64_t rows = nq + 2 * nkv;
   const unsigned blocks = (unsigned)((rows + kHeadRowsPerBlock - 1) / kHeadRowsPerBlock);
-  return launch_ex(head_norm_rope_kernel, dim3(blocks), dim3(kHeadRowsPerBlock * 32), 0, stream, 1, false, q, k, v,
+  return launch_ex(head_norm_rope_kernel, dim3(blocks), dim3(kHeadRowsPerBlock * 32), 0, stream, 1, kPdl, q, k, v,
                    qw, kw, cv, sv, kc, vc, (int)nq, (int)nkv, (int)hd, max_seq, pos, pos_dev, table_rows, eps);
 }
 
@@ -254,7 +258,7 @@ cudaError_t launch_rope(half* x, const float* cv, const float* sv, int64_t heads
                         cudaStream_t stream) {
   int threads = (int)(head_dim / 2);
   threads = threads < 32 ? 32 : (threads > 1024 ? 1024 : threads);
-  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, false, x, cv, sv, head_dim,
+  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, kPdl, x, cv, sv, head_dim,
                    (const int32_t*)nullptr, (int64_t)0);
 }
 
@@ -262,21 +266,21 @@ cudaError_t launch_rope_at(half* x, const float* cos_table, const float* sin_tab
                            int64_t head_dim, const int32_t* pos_dev, cudaStream_t stream) {
   int threads = (int)(head_dim / 2);
   threads = threads < 32 ? 32 : (threads > 1024 ? 1024 : threads);
-  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, false, x, cos_table, sin_table,
+  return launch_ex(rope_kernel, dim3((unsigned)heads), dim3(threads), 0, stream, 1, kPdl, x, cos_table, sin_table,
                    head_dim, pos_dev, table_rows);
 }
 
 cudaError_t launch_kv_append(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                              int64_t hd, int64_t pos, cudaStream_t stream) {
   int threads = hd < 32 ? 32 : (hd > 256 ? 256 : (int)hd);
-  return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, false, kc, vc, kn, vn, max_seq,
+  return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, kPdl, kc, vc, kn, vn, max_seq,
                    hd, pos, (const int32_t*)nullptr);
 }
 
 cudaError_t launch_kv_append_at(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                                 int64_t hd, const int32_t* pos_dev, cudaStream_t stream) {
   int threads = hd < 32 ? 32 : (hd > 256 ? 256 : (int)hd);
-  return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, false, kc, vc, kn, vn, max_seq,
+  return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, kPdl, kc, vc, kn, vn, max_seq,
                    hd, (int64_t)0, pos_dev);
 }
 
@@ -289,9 +293,9 @@ cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, i
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   if (vec)
-    return launch_ex(gather_rows_kernel<true>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, false, matrix,
+    return launch_ex(gather_rows_kernel<true>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, kPdl, matrix,
                      num_rows, row_nbytes, rows, k, dst);
-  return launch_ex(gather_rows_kernel<false>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, false, matrix,
+  return launch_ex(gather_rows_kernel<false>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, kPdl, matrix,
                    num_rows, row_nbytes, rows, k, dst);
 }
 

@@ -108,6 +108,7 @@ struct GemvBatchParamsT {
   int num, grid, x_bytes, ring_bytes, smem_bytes;
   int any_cp_async;  // some task stages scales with cp.async (proxy fence before later bulk copies)
   int norm_bytes;    // shared scratch for the norm weights of prologue tasks (0: none)
+  int need_counters; // some task is depended on or sends to peers: count CTAs / reset at the end
   PeerSet peers;  // used by a peer task (at most one per batch)
   GemvBatchTask tasks[MaxTasks];
 };

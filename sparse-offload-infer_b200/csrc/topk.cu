@@ -251,7 +251,7 @@ cudaError_t launch_topk_impl(bool exact, const void* v, int64_t n, int64_t k, in
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
   }
-  return launch_ex(kernel, dim3(1), dim3(kThreads), bytes, stream, 1, false, v, (int)n, (int)k, out_idx, out_count);
+  return launch_ex(kernel, dim3(1), dim3(kThreads), bytes, stream, 1, true /* programmatic dependent: waits first */, v, (int)n, (int)k, out_idx, out_count);
 }
 
 }  // namespace
@@ -268,7 +268,7 @@ cudaError_t launch_topk_abs_half(bool exact, const half* v, int64_t n, int64_t k
 
 cudaError_t launch_build_descriptors(const int32_t* sel, int64_t k, const int32_t* slot_of, int64_t I, int32_t* desc,
                                      int32_t* miss, int32_t* miss_count, cudaStream_t stream) {
-  return launch_ex(descriptors_kernel, dim3(1), dim3(kThreads), 0, stream, 1, false, sel, (int)k, slot_of, (int)I,
+  return launch_ex(descriptors_kernel, dim3(1), dim3(kThreads), 0, stream, 1, true /* programmatic dependent: waits first */, sel, (int)k, slot_of, (int)I,
                    desc, miss, miss_count);
 }
 

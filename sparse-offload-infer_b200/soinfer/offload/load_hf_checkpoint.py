@@ -44,6 +44,7 @@ class LoadedMatrix:
     packed_k: int
     n: int
     k: int
+    bits: int = 4        # 4: group-wise INT4 (AWQ-packed rows); 8: INT8 rows (one int8 per value), per-channel scales
 
 
 def quantize_and_pack(w: torch.Tensor, group_size: int, device=None) -> tuple[torch.Tensor, torch.Tensor, int]:

@@ -128,11 +128,10 @@ class WeightPipeline:
         name = self.cur_name
         m = self.model.matrices[name]
         if self.model.is_resident(name):
-            y = ops.gemv_w4a16_group_lop3(self.model.resident[name], m.scale, x_in, m.packed_k, self.model.group_size)
+            y = self._gemv(self.model.resident[name], m, x_in)
         else:
             self.sm.wait(self.cur_buf)
-            y = ops.gemv_w4a16_group_lop3(self._view(self.cur_buf, m), m.scale, x_in, m.packed_k,
-                                          self.model.group_size)
+            y = self._gemv(self._view(self.cur_buf, m), m, x_in)
             self.sm.mark_read_done(self.cur_buf)
         nxt = 1 - self.cur_buf
         name_next = self._advance()
@@ -150,9 +149,18 @@ class WeightPipeline:
         self._prefetch_into(self.cur_buf, self.cur_name)
         return self.model.resident[name], self.model.matrices[name]
 
+    def _gemv(self, rows: torch.Tensor, m: LoadedMatrix, x_in: torch.Tensor) -> torch.Tensor:
+        if m.bits == 8:  # INT8 rows, per-channel scales (the reference's gemv_w8a16)
+            return ops.gemv_w8a16(rows.view(torch.int8), m.scale, x_in, m.k)
+        return ops.gemv_w4a16_group_lop3(rows, m.scale, x_in, m.packed_k, self.model.group_size)
+
     def _batched(self, count: int) -> list[str] | None:
+        """The next `count` names when they can run as one persistent batched
+        INT4 launch (resident, INT4), else None."""
         names = [self._seq[(self._i + j) % len(self._seq)] for j in range(count)]
-        return names if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names) else None
+        ok = self.model.batch_gemvs and all(self.model.is_resident(n) and self.model.matrices[n].bits == 4
+                                            for n in names)
+        return names if ok else None
 
     def next_gemvs(self, x_in: torch.Tensor, count: int, norm: tuple | None = None) -> list[torch.Tensor]:
         """The next `count` GEMVs, all on the same input.  When they are all
@@ -192,8 +200,8 @@ class WeightPipeline:
     def next_glu(self, h3: torch.Tensor) -> torch.Tensor:
         """The next gate / up weights as fp16(silu(gate(h3)) * up(h3)): one batched
         launch with the SwiGLU epilogue when resident, else two GEMVs and swiglu."""
-        names = [self._seq[(self._i + j) % len(self._seq)] for j in range(2)]
-        if self.model.batch_gemvs and all(self.model.is_resident(n) for n in names):
+        names = self._batched(2)
+        if names is not None:
             mg, mu = (self.model.matrices[n] for n in names)
             res, g = self.model.resident, self.model.group_size
             gate = torch.empty(mg.n, dtype=torch.float16, device=h3.device)

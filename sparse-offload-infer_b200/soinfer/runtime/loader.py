@@ -106,16 +106,23 @@ def _linear_shapes(arch: Architecture) -> dict[str, tuple[int, int]]:
     }
 
 
-def synthetic_weights(arch: Architecture, seed: int, group_size: int, include_dip: bool, std: float, device):
+def synthetic_weights(arch: Architecture, seed: int, group_size: int, include_dip: bool, std: float, device,
+                      bits: int = 4):
     """Yields (layer, suffix, packed uint8 CUDA, scale fp32 CUDA, packed_k, n, k) for every decoder
     linear weight in load order -- the seeded random-init matrices quantized to group-wise INT4 (the
-    transposed down_proj right after its down_proj) -- then returns the generator for the embeddings."""
+    transposed down_proj right after its down_proj), or with bits=8 to per-channel INT8 (rows of int8
+    values viewed as uint8, scale [N, 1]) -- then returns the generator for the embeddings."""
     gen = torch.Generator(device=device).manual_seed(seed)
     shapes = _linear_shapes(arch)
     for layer in range(arch.num_layers):
         for suffix in LINEAR_SUFFIXES:
             n, k = shapes[suffix]
             w = torch.randn(n, k, generator=gen, device=device) * std
+            if bits == 8:
+                qt = formats.quantize(w, formats.QuantConfig(bits=8, granularity="per_channel"))
+                yield layer, suffix, qt.qweight.contiguous().view(torch.uint8), qt.scale.contiguous(), k, n, k
+                del w
+                continue
             yield _quantized(layer, suffix, w, group_size)
             if include_dip and suffix == "mlp.down_proj.weight":
                 yield _quantized(layer, DOWN_PROJ_T_SUFFIX, w.t().contiguous(), group_size)
@@ -149,12 +156,15 @@ def synthetic_small_tensors(arch: Architecture, gen: torch.Generator, std: float
 
 def synthetic_streaming_model(arch: Architecture, seed: int = 0, group_size: int = 128, include_dip: bool = True,
                               resident: bool = True, offload: bool = True, std: float = 0.02,
-                              embed_std: float = 1.0, device=None) -> StreamingModel:
+                              embed_std: float = 1.0, device=None, bits: int = 4) -> StreamingModel:
     """Seeded random-init model of `arch`.  resident: packed matrices kept in
     HBM; offload: packed matrices also registered in the pinned arena (needed
-    for streaming and for building hot caches from host memory)."""
+    for streaming and for building hot caches from host memory).  bits=8: the
+    INT8 per-channel variant (dense layers only: DIP reads INT4 rows)."""
     if not (resident or offload):
         raise ValueError("a model needs its weights resident, in the arena, or both")
+    if bits not in (4, 8) or (bits == 8 and include_dip):
+        raise ValueError("bits must be 4, or 8 without the DIP transposes")
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     shapes = _linear_shapes(arch)
     store = None
@@ -162,13 +172,14 @@ def synthetic_streaming_model(arch: Architecture, seed: int = 0, group_size: int
         total = 0
         for _layer in range(arch.num_layers):
             for suffix in LINEAR_SUFFIXES:
-                total += packed_int4_bytes(*shapes[suffix], group_size)
+                total += packed_int4_bytes(*shapes[suffix], group_size) if bits == 4 else shapes[suffix][0] * shapes[
+                    suffix][1]
                 if include_dip and suffix == "mlp.down_proj.weight":
                     total += packed_int4_bytes(*shapes[suffix][::-1], group_size)
         store = PinnedWeightStore(total)
     matrices: dict[str, LoadedMatrix] = {}
     res: dict[str, torch.Tensor] | None = {} if resident else None
-    weights = synthetic_weights(arch, seed, group_size, include_dip, std, device)
+    weights = synthetic_weights(arch, seed, group_size, include_dip, std, device, bits=bits)
     while True:
         try:
             layer, suffix, packed, scale, packed_k, n, k = next(weights)
@@ -182,7 +193,7 @@ def synthetic_streaming_model(arch: Architecture, seed: int = 0, group_size: int
             handle = WeightHandle(name, -1, packed.shape[0], packed.shape[1])
         if res is not None:
             res[name] = packed
-        matrices[name] = LoadedMatrix(handle, scale, packed_k, n, k)
+        matrices[name] = LoadedMatrix(handle, scale, packed_k, n, k, bits)
     norms, embed, lm_head, ones = synthetic_small_tensors(arch, gen, std, embed_std, device)
     return StreamingModel(store=store, matrices=matrices, num_layers=arch.num_layers, embed_tokens=embed,
                           lm_head=lm_head, final_norm=ones, layer_norms=norms, hidden_size=arch.hidden_size,

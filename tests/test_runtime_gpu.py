@@ -187,3 +187,43 @@ def test_teacher_forced_nll_is_finite(models):
         model, lambda m, li, x, p, kc, vc: gen.run_decoder_layer_streaming(pipe, m, li, x, p, kc, vc), [1, 2, 3, 4],
         max_seq_len=8)
     assert np.isfinite(nll) and nll > 0
+
+
+def test_int8_per_channel_variant():
+    """The INT8 per-channel weight format (configs[4]'s variant): a dense layer
+    vs the float64 composition with the oracle's INT8 GEMV, and the graph
+    decoder's tokens equal the eager loop's."""
+    model = synthetic_streaming_model(ARCH, seed=8, include_dip=False, resident=True, offload=False, bits=8)
+    assert all(m.bits == 8 and m.scale.shape[1] == 1 for m in model.matrices.values())
+    H, I = model.hidden_size, ARCH.intermediate_size
+    NQ, NKV, HD, eps = model.num_attention_heads, model.num_key_value_heads, model.head_dim, model.rms_norm_eps
+    kcs, vcs = gen._kv_caches(model, 8)
+    x = model.embed_tokens[3]
+    y = gen.run_decoder_layer_streaming(gen.WeightPipeline(model), model, 0, x, 0, kcs[0], vcs[0])
+    norms = {k: _np(v) for k, v in model.layer_norms[0].items()}
+
+    def gemv(suffix, v):
+        m = model.matrix(0, suffix)
+        return port.gemv_w8a16(_np(model.resident[m.handle.name].view(torch.int8)), _np(m.scale), v,
+                               m.k).astype(np.float16)
+
+    xn = _np(x)
+    h = port.rmsnorm(xn[None], norms["input_layernorm"], eps)[0]
+    q = port.rmsnorm(gemv("self_attn.q_proj.weight", h).reshape(NQ, HD), norms["q_norm"], eps)
+    k = port.rmsnorm(gemv("self_attn.k_proj.weight", h).reshape(NKV, HD), norms["k_norm"], eps)
+    v = gemv("self_attn.v_proj.weight", h).reshape(NKV, HD)
+    cos_v, sin_v = (_np(t) for t in ops.precompute_rope_cos_sin(HD, model.rope_theta, 0, device="cuda"))
+    q, k = port.rope(q, cos_v, sin_v), port.rope(k, cos_v, sin_v)
+    kc = np.zeros((NKV, 8, HD), np.float16)
+    vc = np.zeros((NKV, 8, HD), np.float16)
+    kc[:, 0], vc[:, 0] = k, v
+    attn = port.decode_attention(q, kc, vc, 1).astype(np.float16).reshape(-1)
+    h2 = (xn.astype(np.float32) + gemv("self_attn.o_proj.weight", attn).astype(np.float32)).astype(np.float16)
+    h3 = port.rmsnorm(h2[None], norms["post_attention_layernorm"], eps)[0]
+    g_, u_ = gemv("mlp.gate_proj.weight", h3), gemv("mlp.up_proj.weight", h3)
+    mh = (port.silu(g_.astype(np.float32)) * u_.astype(np.float32)).astype(np.float16)
+    ref = (h2.astype(np.float32) + gemv("mlp.down_proj.weight", mh).astype(np.float32)).astype(np.float16)
+    assert_close(y, ref.astype(np.float64), "int8 dense layer", max_abs=None, rel_l2=3e-3)
+    prompt = [5, 6, 7]
+    assert gen.GraphDecoder(model, max_seq_len=32).generate(prompt, 4) == gen.generate_streaming(model, prompt, 4,
+                                                                                                 max_seq_len=32)
