@@ -14,6 +14,13 @@
 // accumulated in fp32, and the split writes (m, l, acc[hd]) to the workspace.
 // A combine kernel rescales and sums the splits in a fixed order.  With a
 // single split the CTA writes the output directly.
+//
+// Split layout: for the attended length c, want = min(cap, ceil(c/16))
+// splits of L = ceil(c/want) positions (cap: enough CTAs to fill the GPU).
+// Both forms compute it in the kernel from c, so the device-position form
+// (launched once for max_seq, c read from device memory at run time) uses
+// exactly the layout of the host-length form at the same c -- every split
+// busy at any length, and bit-identical results between the two forms.
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -32,12 +39,17 @@ __device__ __forceinline__ int device_cur_len(const int32_t* pos_dev, int64_t ma
   return (int)(len < 1 ? 1 : (len > max_seq ? max_seq : len));
 }
 
+__host__ __device__ __forceinline__ int split_want(int c, int cap) {
+  const int w = (c + 15) / 16;
+  return w < 1 ? 1 : (w > cap ? cap : w);
+}
+
 template <int TEAM, int REP>
 __global__ void __launch_bounds__(kThreads)
     attn_split_kernel(const half* __restrict__ q, const half* __restrict__ kc, const half* __restrict__ vc,
                       half* __restrict__ out, float* __restrict__ ws_acc, float* __restrict__ ws_ml, const int nq,
                       const int nkv, const int64_t max_seq, const int hd, const int cur_len_host, const int L,
-                      const float scale_log2, const int32_t* __restrict__ pos_dev) {
+                      const int cap, const float scale_log2, const int32_t* __restrict__ pos_dev) {
   constexpr int kTeams = kThreads / TEAM;
   extern __shared__ float smem[];
   float* s_p = smem;                        // [REP][L] scores, then probabilities
@@ -46,10 +58,8 @@ __global__ void __launch_bounds__(kThreads)
 
   const int kvh = blockIdx.x;
   const int split = blockIdx.y;
-  const int nsplit = gridDim.y;
   const int n_rep = nq / nkv;
   const int qh0 = kvh * n_rep + blockIdx.z * REP;
-  const int t0 = split * L;
   const int team = threadIdx.x / TEAM;
   const int tl = threadIdx.x % TEAM;
   const int d0 = tl * 8;
@@ -60,11 +70,14 @@ __global__ void __launch_bounds__(kThreads)
   pdl_launch_dependents();
   pdl_wait();
   // device-position form: cur_len = *pos_dev + 1, read after the producer of
-  // pos_dev has finished; the launch was planned for max_seq, so splits past
-  // the live length have nothing to do
+  // pos_dev has finished (the launch holds enough splits for any length)
   const int cur_len = pos_dev ? device_cur_len(pos_dev, max_seq) : cur_len_host;
-  if (t0 >= cur_len) return;
-  const int t1 = (t0 + L < cur_len) ? t0 + L : cur_len;
+  const int want = split_want(cur_len, cap);
+  const int Ld = (cur_len + want - 1) / want;      // positions per split (<= L, the score-row stride)
+  const int nsplit = (cur_len + Ld - 1) / Ld;
+  const int t0 = split * Ld;
+  if (split >= nsplit) return;
+  const int t1 = (t0 + Ld < cur_len) ? t0 + Ld : cur_len;
 
   float qf[REP][8];
 #pragma unroll
@@ -185,15 +198,16 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ ws_acc, const float* __restrict__ ws_ml,
-                                    half* __restrict__ out, const int hd, const int nsplit_launched, const int L,
+                                    half* __restrict__ out, const int hd, const int cur_len_host, const int cap,
                                     const int64_t max_seq, const int32_t* __restrict__ pos_dev) {
   pdl_launch_dependents();
   pdl_wait();
-  int nsplit = nsplit_launched;
-  if (pos_dev) {  // only the splits the live length reached wrote partials
-    const int active = (device_cur_len(pos_dev, max_seq) + L - 1) / L;
-    nsplit = active < nsplit ? active : nsplit;
-  }
+  // the split layout of this length (see the file comment)
+  const int cur_len = pos_dev ? device_cur_len(pos_dev, max_seq) : cur_len_host;
+  const int want = split_want(cur_len, cap);
+  const int Ld = (cur_len + want - 1) / want;
+  const int nsplit = (cur_len + Ld - 1) / Ld;
+  if (nsplit == 1) return;  // the single split wrote the output itself
   const int qh = blockIdx.x;
   const float* ml = ws_ml + (int64_t)qh * kMaxSplits * 2;
   float M = -INFINITY;
@@ -211,8 +225,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_acc, const floa
 
 template <int TEAM, int REP>
 cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* out, float* ws_acc, float* ws_ml,
-                         int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L, float scale_log2,
-                         int groups, const int32_t* pos_dev, cudaStream_t stream) {
+                         int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L, int cap,
+                         float scale_log2, int groups, const int32_t* pos_dev, cudaStream_t stream) {
   constexpr int kTeams = kThreads / TEAM;
   const size_t smem = (size_t)(REP * L + kTeams * REP * hd) * sizeof(float);
   auto kernel = attn_split_kernel<TEAM, REP>;
@@ -221,19 +235,19 @@ cudaError_t launch_split(const half* q, const half* kc, const half* vc, half* ou
     if (e != cudaSuccess) return e;
   }
   return launch_ex(kernel, dim3(nkv, nsplit, groups), dim3(kThreads), smem, stream, 1, true /* programmatic dependent: both kernels wait first */, q, kc, vc, out, ws_acc,
-                   ws_ml, nq, nkv, max_seq, hd, cur_len, L, scale_log2, pos_dev);
+                   ws_ml, nq, nkv, max_seq, hd, cur_len, L, cap, scale_log2, pos_dev);
 }
 
 template <int TEAM>
 cudaError_t dispatch_rep(int rep, const half* q, const half* kc, const half* vc, half* out, float* ws_acc,
                          float* ws_ml, int nq, int nkv, int64_t max_seq, int hd, int cur_len, int nsplit, int L,
-                         float sl2, int groups, const int32_t* pd, cudaStream_t st) {
+                         int cap, float sl2, int groups, const int32_t* pd, cudaStream_t st) {
   switch (rep) {
-    case 1: return launch_split<TEAM, 1>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
-    case 2: return launch_split<TEAM, 2>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
-    case 4: return launch_split<TEAM, 4>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
-    case 5: return launch_split<TEAM, 5>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
-    case 8: return launch_split<TEAM, 8>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, sl2, groups, pd, st);
+    case 1: return launch_split<TEAM, 1>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, cap, sl2, groups, pd, st);
+    case 2: return launch_split<TEAM, 2>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, cap, sl2, groups, pd, st);
+    case 4: return launch_split<TEAM, 4>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, cap, sl2, groups, pd, st);
+    case 5: return launch_split<TEAM, 5>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, cap, sl2, groups, pd, st);
+    case 8: return launch_split<TEAM, 8>(q, kc, vc, out, ws_acc, ws_ml, nq, nkv, max_seq, hd, cur_len, nsplit, L, cap, sl2, groups, pd, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -261,13 +275,14 @@ cudaError_t decode_attention_impl(const half* q, const half* kc, const half* vc,
   else
     rep = 1;
   const int groups = n_rep / rep;
-  int64_t want = (kTargetCtas + nkv * groups - 1) / (nkv * groups);
-  if (want > kMaxSplits) want = kMaxSplits;
-  const int64_t by_len = (plan_len + 15) / 16;
-  if (want > by_len) want = by_len;
-  if (want < 1) want = 1;
-  const int L = (int)((plan_len + want - 1) / want);
-  const int nsplit = (int)((plan_len + L - 1) / L);
+  int64_t cap64 = (kTargetCtas + nkv * groups - 1) / (nkv * groups);
+  const int cap = (int)(cap64 > kMaxSplits ? kMaxSplits : cap64);
+  const int want = split_want((int)plan_len, cap);
+  const int L_plan = (int)((plan_len + want - 1) / want);
+  // score-row stride: the longest split of any length <= plan_len (<= max(L_plan, 16))
+  const int L = L_plan > 16 ? L_plan : 16;
+  // splits launched: the host form's own count; the device form enough for any length
+  const int nsplit = pos_dev ? want : (int)((plan_len + L_plan - 1) / L_plan);
   float* ws_acc = reinterpret_cast<float*>(workspace);
   float* ws_ml = ws_acc + nq * kMaxSplits * hd;
   const float sl2 = (1.0f / sqrtf((float)hd)) * kLog2e;
@@ -277,16 +292,16 @@ cudaError_t decode_attention_impl(const half* q, const half* kc, const half* vc,
   cudaError_t e;
   const int inq = (int)nq, inkv = (int)nkv, ihd = (int)hd, icl = (int)plan_len;
   switch (team) {
-    case 4: e = dispatch_rep<4>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
-    case 8: e = dispatch_rep<8>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
-    case 16: e = dispatch_rep<16>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
-    case 32: e = dispatch_rep<32>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, sl2, groups, pos_dev, stream); break;
+    case 4: e = dispatch_rep<4>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, cap, sl2, groups, pos_dev, stream); break;
+    case 8: e = dispatch_rep<8>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, cap, sl2, groups, pos_dev, stream); break;
+    case 16: e = dispatch_rep<16>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, cap, sl2, groups, pos_dev, stream); break;
+    case 32: e = dispatch_rep<32>(rep, q, kc, vc, out, ws_acc, ws_ml, inq, inkv, max_seq, ihd, icl, nsplit, L, cap, sl2, groups, pos_dev, stream); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess || nsplit == 1) return e;
   const int threads = ihd < 32 ? 32 : (ihd > 256 ? 256 : ihd);
-  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, true /* programmatic dependent: both kernels wait first */, ws_acc, ws_ml, out, ihd, nsplit,
-                   L, max_seq, pos_dev);
+  return launch_ex(attn_combine_kernel, dim3(inq), dim3(threads), 0, stream, 1, true /* programmatic dependent: both kernels wait first */, ws_acc, ws_ml, out, ihd, icl,
+                   cap, max_seq, pos_dev);
 }
 
 }  // namespace
