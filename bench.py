@@ -334,6 +334,7 @@ def run_ours(args) -> None:
     decode = run_decode(args, device) if args.decode and rank == 0 and world == 1 else None
     decode_tp = run_decode_tp(args, device, world, rank, dist) if args.tp_decode else None
     decode_int8 = run_decode_int8(args, device) if args.int8_decode and world == 1 else None
+    dip_blocks = run_dip_blocks(args, device) if args.dip_blocks and world == 1 else None
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -365,6 +366,7 @@ def run_ours(args) -> None:
                    "decode": decode,
                    "decode_14b_tp": decode_tp,
                    "decode_14b_int8": decode_int8,
+                   "dip_blocks": dip_blocks,
                    "parallelism": f"{world} independent replicas (no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -585,6 +587,128 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
                 "sums + residual + RMSNorm (soinfer.runtime.tp.PeerExchange)" if world > 1 else "single GPU")}
 
 
+def pcie_h2d_peak(device, nbytes: int = 256 << 20, reps: int = 5) -> float:
+    """Pinned host -> device copy bandwidth (GB/s), best of `reps`."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(reps + 1):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        dst.copy_(src, non_blocking=True)
+        e.record()
+        torch.cuda.synchronize(device)
+        best = max(best, nbytes / (s.elapsed_time(e) / 1e3) / 1e9)
+    return best
+
+
+def run_dip_blocks(args, device, reps: int = 20) -> dict:
+    """configs[1] and configs[2] on the Qwen3-1.7B MLP shapes (H 2048, I 6144,
+    k = I/2), 28 layer copies per step (weights far above L2):
+    * DIP block: gate GEMV, |gate| top-k, up_proj on the selected rows,
+      SwiGLU, down_proj_T sparse accumulate -- all on the device, one CUDA
+      graph per step; algorithmic bytes per block 13,443,072;
+    * cache-aware DIP block: 20% hot cache (Zipf s=1.1 ranking over a seeded
+      permutation), the misses' rows streamed from the pinned arena by the
+      device-driven gather (one host read of the miss count per block, as the
+      reference); H2D bytes = misses x (up + down_T row bytes), against the
+      measured pinned H2D peak."""
+    import copy
+
+    from soinfer import ops
+    from soinfer.offload.hot_cache import HotCache, StaticFrequencyPolicy
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import QWEN3_1_7B, synthetic_streaming_model
+
+    arch = QWEN3_1_7B
+    L, Hh, Ii = arch.num_layers, arch.hidden_size, arch.intermediate_size
+    k = Ii // 2
+    model = synthetic_streaming_model(arch, seed=3, resident=True, offload=True, include_dip=True, device=device)
+    g = model.group_size
+    gen_x = torch.Generator(device=device).manual_seed(17)
+    h3 = [torch.randn(Hh, generator=gen_x, device=device).half() for _ in range(L)]
+    bufs = gen.DipBuffers.make(model, k)
+    outs = [None] * L
+
+    def gate_and_select(li):
+        m = model.matrix(li, "mlp.gate_proj.weight")
+        gate = ops.gemv_w4a16_group_lop3(model.resident[m.handle.name], m.scale, h3[li], m.packed_k, g)
+        return gate, ops.topk_threshold_select_abs(gate, k)
+
+    def dip_step():
+        for li in range(L):
+            gate, idx = gate_and_select(li)
+            outs[li] = gen.dip_mlp_tail(model, li, h3[li], gate, idx, k, bufs)
+
+    st = torch.cuda.Stream(device)
+    st.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(st):
+        dip_step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            dip_step()
+        for _ in range(3):
+            graph.replay()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        for _ in range(reps):
+            graph.replay()
+        e.record(st)
+    torch.cuda.synchronize(device)
+    dip_ms = s.elapsed_time(e) / reps
+    ref0 = outs[0].clone()
+    del graph
+    block_bytes = 13_443_072
+
+    # cache-aware DIP: hot rows resident, misses from the pinned arena
+    rng = np.random.default_rng(0)
+    perm = rng.permutation(Ii)
+    freq = np.empty(Ii, dtype=np.int64)
+    freq[perm] = (1e9 / np.arange(1, Ii + 1) ** 1.1).astype(np.int64)
+    hot = StaticFrequencyPolicy(freq, round(0.2 * Ii)).hot_list
+    caches = [HotCache.build(model, li, hot) for li in range(L)]
+    host_model = copy.copy(model)  # same matrices; up / down_T rows read from the arena
+    host_model.resident = {n: t for n, t in model.resident.items()
+                           if not (n.endswith("mlp.up_proj.weight") or n.endswith(gen.DOWN_PROJ_T_SUFFIX))}
+    miss = [0] * L
+
+    def cached_step(count):
+        for li in range(L):
+            gate, idx = gate_and_select(li)
+            outs[li] = gen.cached_dip_mlp_tail(host_model, li, h3[li], gate, idx, bufs, caches[li],
+                                               miss if count else None)
+
+    cached_step(False)
+    torch.cuda.synchronize(device)
+    assert torch.equal(outs[0], ref0), "cache-aware DIP differs from DIP"
+    creps = 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(creps):
+        cached_step(True)
+    e.record()
+    torch.cuda.synchronize(device)
+    cached_ms = s.elapsed_time(e) / creps
+    miss_bytes = sum(miss) / creps
+    peak = pcie_h2d_peak(device)
+    del model, host_model, caches, bufs
+    torch.cuda.empty_cache()
+    return {"shapes": "Qwen3-1.7B MLP: H 2048, I 6144, k 3072, INT4 g128; 28 layer copies per step",
+            "dip_block": {"us_per_block": round(dip_ms * 1e3 / L, 2),
+                          "value": round(L * block_bytes / (dip_ms / 1e3) / 1e9, 1), "unit": UNIT,
+                          "bytes_per_block": block_bytes, "steps": reps,
+                          "note": "CUDA graph per step; the fraction of HBM peak is value / roofline.peak"},
+            "cached_dip_block": {"us_per_block": round(cached_ms * 1e3 / L, 2), "hot_channels": len(hot),
+                                 "h2d_bytes_per_block": int(miss_bytes / L),
+                                 "h2d_gbs": round(miss_bytes / (cached_ms / 1e3) / 1e9, 2),
+                                 "pcie_h2d_peak_gbs": round(peak, 2),
+                                 "h2d_frac_of_peak": round(miss_bytes / (cached_ms / 1e3) / 1e9 / peak, 4),
+                                 "bit_identical_to_dip": True, "steps": creps,
+                                 "note": "eager (one miss-count read per block); misses gathered over PCIe "
+                                         "from the pinned arena by the device"}}
+
+
 def run_decode_int8(args, device) -> dict:
     """configs[4]'s INT8 per-channel variant: the 14B-shaped model with int8
     rows and one fp32 scale per row (the reference's gemv_w8a16 per GEMV),
@@ -629,6 +753,7 @@ def main() -> None:
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
     ap.add_argument("--gemm-m8", type=int, default=1, help="also measure the batch-8 GEMM stream (in config)")
     ap.add_argument("--int8-decode", type=int, default=1, help="also measure the 14B INT8 per-channel decode (N=1)")
+    ap.add_argument("--dip-blocks", type=int, default=1, help="also measure configs[1] / configs[2] blocks (N=1)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
     ap.add_argument("--tp-tokens", type=int, default=256)
     ap.add_argument("--tp-nccl", type=int, default=0, help="TP collectives through NCCL instead of the peer exchange")

@@ -547,7 +547,7 @@ int soinfer_decode_attention(const soinfer_half* q, const soinfer_half* k_cache,
   REQUIRE(head_dim >= 8 && head_dim % 8 == 0 && head_dim <= 256, "%s: head_dim must be a multiple of 8 in [8, 256]",
           name);
   REQUIRE(cur_len >= 1 && cur_len <= max_seq_len, "%s: cur_len out of range for max_seq_len", name);
-  REQUIRE(num_q_heads < (1 << 20) && max_seq_len < (1ll << 31), "%s: sizes too large", name);
+  REQUIRE(num_q_heads <= 1024 && max_seq_len < (1ll << 31), "%s: sizes too large (num_q_heads <= 1024)", name);
   REQUIRE(q && k_cache && v_cache && out, "%s: null pointer", name);
   REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16), "%s: q and caches must be 16-byte aligned",
           name);
@@ -634,7 +634,7 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
   REQUIRE(num_q_heads % num_kv_heads == 0, "%s: num_q_heads must be a multiple of num_kv_heads", name);
   REQUIRE(head_dim >= 8 && head_dim % 8 == 0 && head_dim <= 256, "%s: head_dim must be a multiple of 8 in [8, 256]",
           name);
-  REQUIRE(max_seq_len >= 1 && num_q_heads < (1 << 20) && max_seq_len < (1ll << 31), "%s: sizes out of range", name);
+  REQUIRE(max_seq_len >= 1 && num_q_heads <= 1024 && max_seq_len < (1ll << 31), "%s: sizes out of range (num_q_heads <= 1024)", name);
   REQUIRE(q && k_cache && v_cache && out && pos_dev, "%s: null pointer", name);
   REQUIRE(aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16), "%s: q and caches must be 16-byte aligned",
           name);

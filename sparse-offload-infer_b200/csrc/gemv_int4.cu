@@ -219,9 +219,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   // every row stored: the last CTA signals the exchange (PEER only)
   auto finish = [&]() {
     if constexpr (PEER) {
+      __threadfence_system();  // every thread's row stores, before the CTA counts itself done
       __syncthreads();
       if (tid == 0) {
-        __threadfence_system();
         const unsigned prev = atomicAdd(peer_ticket(ps), 1u);
         if (prev == gridDim.x - 1) {
           *peer_ticket(ps) = 0u;

@@ -70,13 +70,13 @@ __device__ __forceinline__ uint32_t peer_next_epoch(const PeerSet& ps) {
   return (uint32_t)(*reinterpret_cast<volatile int*>(peer_epoch(ps))) + 1u;
 }
 
-// Flag stores to every rank; the caller's threads have pushed their data and
-// pass a barrier first.  Threads [0, world) each signal one rank.
+// Flag stores to every rank.  Every thread of the CTA calls it after its own
+// pushes: each fences them at system scope, the barrier gathers the CTA, and
+// threads [0, world) then each signal one rank.
 __device__ __forceinline__ void peer_signal_all(const PeerSet& ps, int parity, uint32_t e) {
-  if ((int)threadIdx.x < ps.world) {
-    __threadfence_system();
-    st_release_sys_u32(peer_flag(ps, threadIdx.x, parity, ps.rank), e);
-  }
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < ps.world) st_release_sys_u32(peer_flag(ps, threadIdx.x, parity, ps.rank), e);
 }
 
 // Bounded wait (whole CTA) until every rank signalled exchange e here.

@@ -36,7 +36,6 @@ __global__ void __launch_bounds__(kThreads)
       const uint4 v = __ldcg(reinterpret_cast<const uint4*>(partial) + i);
       for (int r = 0; r < ps.world; ++r) reinterpret_cast<uint4*>(peer_slot(ps, r, par, ps.rank))[i] = v;
     }
-    __syncthreads();
     peer_signal_all(ps, par, e);
   }
   if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout)) {
@@ -115,7 +114,6 @@ __global__ void __launch_bounds__(kThreads)
     const uint4 v = __ldcg(local + i);
     for (int r = 0; r < ps.world; ++r) reinterpret_cast<uint4*>(peer_slot(ps, r, par, ps.rank))[i] = v;
   }
-  __syncthreads();
   peer_signal_all(ps, par, e);
   if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout)) {
     for (int r = 0; r < ps.world; ++r) {
@@ -148,7 +146,6 @@ __global__ void tp_argmax_kernel(const PeerSet ps, const half* __restrict__ logi
     const unsigned long long key = ((unsigned long long)half_order_key(h) << 32) | (0xFFFFFFFFu - gi);
     *reinterpret_cast<unsigned long long*>(peer_slot(ps, tid, par, ps.rank)) = key;
   }
-  __syncthreads();
   peer_signal_all(ps, par, e);
   if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout) && tid == 0) {
     unsigned long long best = 0;

@@ -363,9 +363,20 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
         channel_counts[layer_idx].scatter_add_(0, idx_long, torch.ones_like(idx_long))
     if selected_out is not None:
         selected_out[layer_idx].append(idx_long.cpu().tolist())
+    return h2 + dip_mlp_tail(model, layer_idx, h3, gate, idx, dip_k, bufs, idx_long)
+
+
+def dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor, idx: torch.Tensor,
+                 dip_k: int, bufs: DipBuffers, idx_long: torch.Tensor | None = None) -> torch.Tensor:
+    """The DIP MLP after the selection (configs[1] block minus the gate GEMV
+    and selector): up_proj on the selected rows, h = fp16(silu(g) * u),
+    down_proj_T sparse accumulate -- resident rows read in place, arena rows
+    gathered on the device.  Returns the down output (no residual)."""
     up = model.matrix(layer_idx, "mlp.up_proj.weight")
     down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
     g = model.group_size
+    if idx_long is None and not (model.is_resident(up.handle.name) and model.is_resident(down_t.handle.name)):
+        idx_long = idx.long()
     if model.is_resident(up.handle.name):
         u_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, idx, h3, up.packed_k, g)
     else:
@@ -374,14 +385,12 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
         u_sel = ops.gemv_w4a16_group_lop3(rows, up.scale.index_select(0, idx_long), h3, up.packed_k, g)
     h_sel = ops.swiglu(gate, u_sel, idx)
     if model.is_resident(down_t.handle.name):
-        down = ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, idx, h_sel,
+        return ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, idx, h_sel,
                                           model.hidden_size, g)
-    else:
-        rows = bufs.down_rows(dip_k)
-        ops.gather_rows_device(model.weight_source(down_t), idx, rows)
-        down = ops.gemv_w4a16_sparse_accumulate(rows, down_t.scale.index_select(0, idx_long), h_sel,
-                                                model.hidden_size, g)
-    return h2 + down
+    rows = bufs.down_rows(dip_k)
+    ops.gather_rows_device(model.weight_source(down_t), idx, rows)
+    return ops.gemv_w4a16_sparse_accumulate(rows, down_t.scale.index_select(0, idx_long), h_sel, model.hidden_size,
+                                            g)
 
 
 def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
@@ -396,7 +405,17 @@ def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel
     h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     gate = pipeline.next_gemv(h3)
     idx = _select(gate, dip_k)
-    cache = caches[layer_idx]
+    return h2 + cached_dip_mlp_tail(model, layer_idx, h3, gate, idx, bufs, caches[layer_idx], miss_bytes)
+
+
+def cached_dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor,
+                        idx: torch.Tensor, bufs: DipBuffers, cache: HotCache,
+                        miss_bytes: list[int] | None = None) -> torch.Tensor:
+    """The cache-aware DIP MLP after the selection (configs[2] block minus the
+    gate GEMV and selector): selected channels resolve to hot-cache slots or
+    misses; the misses' up / down_T rows are gathered from the pinned arena by
+    the device (zero-copy over PCIe); one fused GEMV per direction reads both.
+    One host read (the miss count).  Returns the down output (no residual)."""
     up = model.matrix(layer_idx, "mlp.up_proj.weight")
     down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
     g = model.group_size
@@ -413,9 +432,8 @@ def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel
     u_sel = ops.gemv_dip_fused_up(cache.up_Wq, cache.up_scale, up_rows, up.scale.index_select(0, miss_long), desc,
                                   h3, up.packed_k, g)
     h_sel = ops.swiglu(gate, u_sel, idx)
-    down = ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows,
+    return ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows,
                                    down_t.scale.index_select(0, miss_long), desc, h_sel, model.hidden_size, g)
-    return h2 + down
 
 
 def dip_bytes_per_token(model: StreamingModel, dip_k: int, dense: bool = False) -> int:
