@@ -116,6 +116,9 @@ typedef struct soinfer_gemv_task {
    * persistent path (K and group_size multiples of 128). */
   const soinfer_half* norm_weight;
   float norm_eps;
+  /* With norm_weight: if not NULL, the normalised x (fp16 [K]) is also written
+   * here, complete when the launch is (for kernels that need it later). */
+  soinfer_half* norm_out;
 } soinfer_gemv_task;
 
 /* Bytes of zero-initialised device workspace soinfer_gemv_w4a16_batch needs

@@ -126,6 +126,8 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
                   aligned(t.scale, 4),
               "%s: a peer task needs K and group_size multiples of 128 and 16-byte aligned rows / x", tn);
     }
+    REQUIRE(!t.norm_out || (t.norm_weight && aligned(t.norm_out, 16)), "%s: norm_out needs norm_weight and 16-byte "
+            "alignment", tn);
     if (t.norm_weight) {
       REQUIRE(t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.norm_weight, 16) && t.norm_eps >= 0.f,
               "%s: a norm prologue needs K and group_size multiples of 128, a 16-byte aligned weight and eps >= 0",
@@ -169,6 +171,7 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
       d.peer = t.y ? 0 : 1;
       d.norm_w = as_half(t.norm_weight);
       d.eps = t.norm_eps;
+      d.norm_out = as_half(t.norm_out);
     }
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

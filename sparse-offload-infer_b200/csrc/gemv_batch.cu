@@ -575,6 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             oh[j] = __floats2half2_rn(f.x * inv * gw.x, f.y * inv * gw.y);
           }
           dst[u] = o;
+          if (tk.norm_out != nullptr && blockIdx.x == 0) reinterpret_cast<uint4*>(tk.norm_out)[u] = o;
         }
         __syncwarp();
         mbar_arrive(&xfull[xs]);

@@ -90,15 +90,16 @@ struct GemvBatchTask {
   const float* S;
   const half* x;
   half* y;
+  const half* resid;  // optional epilogue: y = fp16(resid + fp16(dot))
+  const half* glu;    // optional epilogue: y = fp16(silu(glu) * fp16(dot)), applied before resid
+  const half* norm_w; // optional prologue: x -> fp16(x * rsqrt(mean(x^2) + eps) * norm_w) in shared memory
+  half* norm_out;     // with the prologue: CTA 0 also writes the normalised x here (for later kernels)
   int N, K, G, cpg, dep;
   // filled by plan_gemv_batch: rows per CTA, 16-row tiles per item, publish (a later task depends on it),
   // ks / nsegs (K split into segments of ks 128-chunks when a 16-row tile is too long for one item),
   // scale_plain (scale rows staged by plain loads: not 16-byte rows, or segmented)
   int rows_per_cta, tiles_per_item, publish, ks, nsegs, scale_plain;
-  const half* resid;  // optional epilogue: y = fp16(resid + fp16(dot))
-  const half* glu;    // optional epilogue: y = fp16(silu(glu) * fp16(dot)), applied before resid
   int peer;           // y == nullptr: rows go to every rank's exchange inbox (PeerSet), the last CTA signals
-  const half* norm_w; // optional prologue: x -> fp16(x * rsqrt(mean(x^2) + eps) * norm_w) in shared memory
   float eps;
 };
 constexpr int kMaxBatchTasks = 256;

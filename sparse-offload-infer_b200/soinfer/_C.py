@@ -275,7 +275,7 @@ def gemv_fp16_argmax(W, x, logits: bool = False, out_idx=None):
 class _GemvTask(ctypes.Structure):
     _fields_ = [("Wq", _P), ("scale", _P), ("x", _P), ("y", _P), ("N", _I64), ("K", _I64), ("group_size", _I64),
                 ("num_groups", _I64), ("dep", _I64), ("residual", _P), ("glu_gate", _P), ("norm_weight", _P),
-                ("norm_eps", _F32)]
+                ("norm_eps", _F32), ("norm_out", _P)]
 
 
 MAX_BATCH_TASKS = 256
@@ -284,12 +284,13 @@ MAX_BATCH_TASKS = 256
 class GemvBatch:
     """A prepared list of INT4 GEMVs run as one persistent kernel
     (soinfer_gemv_w4a16_batch).  tasks: sequence of
-    (Wq_packed, scale, x, y, K, group_size, dep[, residual[, glu_gate[, (norm_weight, eps)]]])
+    (Wq_packed, scale, x, y, K, group_size, dep[, residual[, glu_gate[, (norm_weight, eps[, norm_out])]]])
     with dep = index of an earlier task whose output feeds this task's x, or
     -1; residual / glu_gate (fp16 [N] or None) add the epilogues
     y = residual + fp16(silu(glu_gate) * fp16(W x)) of the C ABI; a
     (norm_weight fp16 [K], eps) pair multiplies RMSNorm(x) * norm_weight
-    instead of x (computed in the kernel).  The tensors
+    instead of x (computed in the kernel; a third element, fp16 [K], receives
+    the normalised x).  The tensors
     must stay alive and keep their storage while the batch is used.
     peers (a PeerSetStruct): tensor-parallel batch (soinfer_gemv_w4a16_batch_tp)
     in which one task may have y = None -- its rows go to every rank's
@@ -308,6 +309,9 @@ class GemvBatch:
             if norm is not None:
                 _f16(norm[0], f"gemv_w4a16_batch[task {i}](norm_weight)")
                 _check(norm[0].numel() == K, f"gemv_w4a16_batch[task {i}]", ": norm_weight must hold K values")
+                if len(norm) > 2 and norm[2] is not None:
+                    _f16(norm[2], f"gemv_w4a16_batch[task {i}](norm_out)")
+                    _check(norm[2].numel() == K, f"gemv_w4a16_batch[task {i}]", ": norm_out must hold K values")
             name = f"gemv_w4a16_batch[task {i}]"
             _check(W.is_cuda and W.dtype == torch.uint8 and W.is_contiguous() and W.dim() == 2, name,
                    "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
@@ -332,7 +336,8 @@ class GemvBatch:
             arr[i] = _GemvTask(W.data_ptr(), scale.data_ptr(), x.data_ptr(), _ptr(y), W.size(0), K, group_size,
                                scale.size(1), dep, _ptr(residual), _ptr(glu),
                                _ptr(norm[0]) if norm is not None else None,
-                               float(norm[1]) if norm is not None else 0.0)
+                               float(norm[1]) if norm is not None else 0.0,
+                               _ptr(norm[2]) if norm is not None and len(norm) > 2 else None)
         self._arr, self.n, self.device = arr, n, dev
         self._keep = [tuple(t) for t in tasks]
         self.peers = peers

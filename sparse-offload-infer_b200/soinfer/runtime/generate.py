@@ -181,7 +181,10 @@ class WeightPipeline:
             _C.gemv_w4a16_batch(tasks)
             return [t[3] for t in tasks]
         if norm is not None:
-            x_in = ops.rmsnorm(x_in.unsqueeze(0), norm[0], norm[1]).squeeze(0)
+            h = ops.rmsnorm(x_in.unsqueeze(0), norm[0], norm[1]).squeeze(0)
+            if len(norm) > 2 and norm[2] is not None:
+                norm[2].copy_(h)
+            x_in = h
         return [self.next_gemv(x_in) for _ in range(count)]
 
     def next_gemv_residual(self, x_in: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
@@ -301,6 +304,23 @@ def _attention_block(pipeline: WeightPipeline, model: StreamingModel, layer_idx:
     return h2.squeeze(0), h3.squeeze(0)
 
 
+def _attention_and_gate(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int, x_flat: torch.Tensor, pos,
+                        k_cache: torch.Tensor, v_cache: torch.Tensor):
+    """Attention half + the dense gate GEMV of a DIP layer: (h2, h3, gate).
+    Resident weights: the norms run inside the batched kernels (q/k/v; gate,
+    which also writes h3 for the selected-row kernels) and o adds the
+    residual in its epilogue."""
+    names = pipeline._batched(5)  # q, k, v, o, gate
+    if names is None:
+        h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
+        return h2, h3, pipeline.next_gemv(h3)
+    h2, _ = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache, fuse_norms=True)
+    h3 = torch.empty_like(h2)
+    norm = (model.layer_norms[layer_idx]["post_attention_layernorm"], model.rms_norm_eps, h3)
+    gate = pipeline.next_gemvs(h2, 1, norm=norm)[0]
+    return h2, h3, gate
+
+
 def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
                                 x_flat: torch.Tensor, pos: int, k_cache: torch.Tensor,
                                 v_cache: torch.Tensor) -> torch.Tensor:
@@ -353,8 +373,7 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
     sparse accumulate over the same rows.  channel_counts[layer] (int64 [I]
     CUDA) accumulates selections; selected_out[layer] collects the index lists
     (this one syncs)."""
-    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
-    gate = pipeline.next_gemv(h3)
+    h2, h3, gate = _attention_and_gate(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     idx = _select(gate, dip_k)
     idx_long = idx.long() if (channel_counts is not None or selected_out is not None
                               or not model.is_resident(model.matrix(layer_idx, "mlp.up_proj.weight").handle.name)
@@ -402,8 +421,7 @@ def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel
     from the arena); one fused GEMV per direction reads both.  Bit-identical
     to run_decoder_layer_dip on the same inputs.  miss_bytes[layer] counts
     the streamed bytes."""
-    h2, h3 = _attention_block(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
-    gate = pipeline.next_gemv(h3)
+    h2, h3, gate = _attention_and_gate(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     idx = _select(gate, dip_k)
     return h2 + cached_dip_mlp_tail(model, layer_idx, h3, gate, idx, bufs, caches[layer_idx], miss_bytes)
 
