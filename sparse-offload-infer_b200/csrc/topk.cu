@@ -15,6 +15,13 @@
 // mode reuses the radix select and resolves ties at the k-th value by the
 // lower index.  One CTA of 1024 threads; keys stay in shared memory when n
 // fits (n <= 49152), otherwise every pass re-reads v from L2.
+//
+// The DIP decode path selects on |fp16 gate| (reference: gate.float().abs()):
+// those values are exact fp16 magnitudes, so their order is the order of the
+// 15-bit |h| patterns -- topk_abs_half_kernel radix-selects on 16-bit keys in
+// two 8-bit passes, replays the same bisection, and compacts with one
+// block-wide scan (each warp owns a contiguous run of indices), in a fraction
+// of the general kernel's barriers.
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -202,6 +209,128 @@ __global__ void __launch_bounds__(kThreads)
   if (tid == 0) *out_count = count;
 }
 
+// |fp16| keys: the magnitude bits; NaN ranks below every number (key 0), as
+// float_key does for the general kernel.
+__device__ __forceinline__ uint32_t abs_half_key(uint16_t bits) {
+  const uint32_t m = bits & 0x7fffu;
+  return m > 0x7c00u ? 0u : m;
+}
+
+// Selects bin b with sum(counts of bins > b) < remaining <= sum(counts of bins >= b)
+// over hist[256] (warp 0); writes s_bin / s_rem (remaining within the bin).
+__device__ __forceinline__ void pick_bin(const uint32_t* hist, int remaining, uint32_t* s_bin, int* s_rem) {
+  const int lane = threadIdx.x & 31;
+  int c[8];
+  int lsum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = (int)hist[lane * 8 + j];
+    lsum += c[j];
+  }
+  int suf = lsum;  // inclusive suffix sum over lanes >= lane
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += u;
+  }
+  int cum = suf - lsum;
+#pragma unroll
+  for (int j = 7; j >= 0; --j) {
+    if (cum < remaining && cum + c[j] >= remaining) {
+      *s_bin = (uint32_t)(lane * 8 + j);
+      *s_rem = remaining - cum;
+    }
+    cum += c[j];
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    topk_abs_half_kernel(const half* __restrict__ v, const int n, const int k, int32_t* __restrict__ out_idx,
+                         int32_t* __restrict__ out_count) {
+  extern __shared__ uint16_t sbits[];  // [n] raw fp16 bits
+  __shared__ uint32_t hist[256];
+  __shared__ int s_warp[kWarpsPerBlock];
+  __shared__ int s_total;
+  __shared__ float s_wmax[kWarpsPerBlock];
+  __shared__ uint32_t s_bin;
+  __shared__ int s_rem;
+  __shared__ float s_tau;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint16_t* vb = reinterpret_cast<const uint16_t*>(v);
+  float lmax = 0.f;  // reference: local_max starts at 0 (topk_select.cu:19)
+  for (int i = tid; i < n; i += kThreads) {
+    const uint16_t b = vb[i];
+    sbits[i] = b;
+    lmax = fmaxf(lmax, fabsf(__half2float(__ushort_as_half(b))));
+  }
+  for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
+  lmax = warp_max(lmax);
+  if (lane == 0) s_wmax[warp] = lmax;
+  __syncthreads();
+  // pass 1: high byte of the 16-bit key
+  for (int i = tid; i < n; i += kThreads) atomicAdd(&hist[abs_half_key(sbits[i]) >> 8], 1u);
+  __syncthreads();
+  if (warp == 0) pick_bin(hist, k, &s_bin, &s_rem);
+  __syncthreads();
+  const uint32_t hi = s_bin;
+  const int rem1 = s_rem;
+  for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
+  __syncthreads();
+  // pass 2: low byte among the keys in that bin
+  for (int i = tid; i < n; i += kThreads) {
+    const uint32_t key = abs_half_key(sbits[i]);
+    if ((key >> 8) == hi) atomicAdd(&hist[key & 255u], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) pick_bin(hist, rem1, &s_bin, &s_rem);
+  __syncthreads();
+  const uint32_t kth = (hi << 8) | s_bin;  // the k-th largest |h| (NaN-free: key 0 == +0)
+  // the reference threshold: replay the bisection on the k-th value
+  if (tid == 0) {
+    float m = 0.f;
+    for (int w = 0; w < kWarpsPerBlock; ++w) m = fmaxf(m, s_wmax[w]);
+    const float kv = __half2float(__ushort_as_half((uint16_t)kth));
+    float lo = 0.f, hi_b = m + 1e-3f;
+#pragma unroll 1
+    for (int it = 0; it < kBisectionSteps; ++it) {
+      const float mid = 0.5f * (lo + hi_b);
+      if (kv >= mid)
+        lo = mid;
+      else
+        hi_b = mid;
+    }
+    s_tau = lo;
+  }
+  __syncthreads();
+  const float tau = s_tau;
+  // ordered compaction: warp w owns indices [w * chunk, (w + 1) * chunk)
+  const int chunk = ((n + kWarpsPerBlock - 1) / kWarpsPerBlock + 31) & ~31;
+  const int c0 = warp * chunk, c1 = min(n, c0 + chunk);
+  int wcount = 0;
+  for (int i0 = c0; i0 < c1; i0 += 32) {
+    const int i = i0 + lane;
+    const bool sel = i < c1 && fabsf(__half2float(__ushort_as_half(sbits[i]))) >= tau;
+    wcount += __popc(__ballot_sync(0xffffffffu, sel));
+  }
+  const int wbase = block_warp_scan(wcount, s_warp, &s_total);
+  int run = wbase;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int i0 = c0; i0 < c1 && run < k; i0 += 32) {
+    const int i = i0 + lane;
+    const bool sel = i < c1 && fabsf(__half2float(__ushort_as_half(sbits[i]))) >= tau;
+    const unsigned bs = __ballot_sync(0xffffffffu, sel);
+    const int pos = run + __popc(bs & lt_mask);
+    if (sel && pos < k) out_idx[pos] = i;
+    run += __popc(bs);
+  }
+  const int total = s_total;
+  const int count = total < k ? total : k;
+  for (int p = count + tid; p < k; p += kThreads) out_idx[p] = -1;
+  if (tid == 0) *out_count = count;
+}
+
 __global__ void __launch_bounds__(kThreads)
     descriptors_kernel(const int32_t* __restrict__ sel, const int k, const int32_t* __restrict__ slot_of, const int I,
                        int32_t* __restrict__ desc, int32_t* __restrict__ miss, int32_t* __restrict__ miss_count) {
@@ -263,6 +392,16 @@ cudaError_t launch_topk(bool exact, const float* v, int64_t n, int64_t k, int32_
 
 cudaError_t launch_topk_abs_half(bool exact, const half* v, int64_t n, int64_t k, int32_t* out_idx,
                                  int32_t* out_count, cudaStream_t stream) {
+  if (!exact && n <= 2 * kSmemKeysMax) {
+    const size_t bytes = (size_t)n * sizeof(uint16_t);
+    if (bytes > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(topk_abs_half_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)bytes);
+      if (e != cudaSuccess) return e;
+    }
+    return launch_ex(topk_abs_half_kernel, dim3(1), dim3(kThreads), bytes, stream, 1, true, v, (int)n, (int)k,
+                     out_idx, out_count);
+  }
   return launch_topk_impl<true>(exact, v, n, k, out_idx, out_count, stream);
 }
 

@@ -97,3 +97,29 @@ def test_rejects_bad_arguments():
         ops.topk_threshold_select(torch.rand(4, 256, device=DEV), 10)
     with pytest.raises(RuntimeError):
         ops.topk_select_exact(abs_g.half(), 10)
+
+
+@pytest.mark.parametrize("n,k", [(6144, 3072), (17408, 8704), (2176, 1088), (1000, 1), (77, 77), (300, 150)])
+@pytest.mark.parametrize("dist", ["normal", "ties", "special"])
+def test_fp16_abs_selector_bit_exact_with_reference(n, k, dist):
+    """The |fp16 gate| selector (16-bit keys, two radix passes) against the
+    reference semantics on gate.float().abs(): indices and count bit-exact,
+    including heavy ties, zeros, +-inf and NaN (NaN never qualifies)."""
+    gen = torch.Generator().manual_seed(n + k)
+    if dist == "normal":
+        g = torch.randn(n, generator=gen).half()
+    elif dist == "ties":
+        g = (torch.randint(-6, 7, (n,), generator=gen).float() * 0.25).half()
+    else:
+        g = torch.randn(n, generator=gen).half()
+        g[:: 7] = 0.0
+        g[3:: 11] = -0.0
+        g[5:: 13] = float("inf")
+        g[2:: 17] = float("nan")
+        g[1:: 19] = -float("inf")
+    idx, count = _C.topk_threshold_select_abs_f16(g.to(DEV), k)
+    e_idx, e_count = port.topk_threshold_select_ref(g.float().abs().numpy(), k)
+    got = idx.cpu().numpy()
+    assert int(count.item()) == int(e_count), (int(count.item()), int(e_count))
+    assert np.array_equal(got[: int(e_count)], e_idx[: int(e_count)])
+    assert np.all(got[int(e_count):] == -1)
