@@ -144,10 +144,13 @@ int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, 
  * rows: int32 [num_sel] device, each in [0, N).
  * Replaces the pair at runtime/generate.py:286-302 (gather_rows_staged of the
  * selected up_proj rows + gemv_w4a16_group_lop3 with N = k) when the matrix is
- * resident in device memory. */
+ * resident in device memory.  glu_gate (optional, fp16 [N]): y[r] =
+ * fp16(silu(glu_gate[rows[r]]) * y[r]) -- DIP's SwiGLU on the selected
+ * channels (generate.py:300-302), equal to soinfer_swiglu after the GEMV. */
 int soinfer_gemv_w4a16_rows(const uint8_t* Wq, const float* scale, int64_t N, const int32_t* rows,
                             int64_t num_sel, const soinfer_half* x, soinfer_half* y, int64_t K,
-                            int64_t group_size, int64_t num_groups, void* stream);
+                            int64_t group_size, int64_t num_groups, const soinfer_half* glu_gate,
+                            void* stream);
 
 /* y = dequant(Wq, scale) @ x for symmetric INT8 weights.
  * Wq: int8 [N, K]; scale: fp32 [N or 1, num_groups]; scale_row_stride = 0
@@ -265,11 +268,14 @@ int soinfer_gemv_w4a16_sparse_accumulate_noalloc(const uint8_t* Wq_sel, const fl
 /* Row-indirect form of the sparse 'down' GEMV over a resident transposed
  * matrix: row j of the sum is Wq_T[rows[j]] with scale_T[rows[j]].
  * Bit-identical to gathering those rows and calling
- * soinfer_gemv_w4a16_sparse_accumulate.  rows: int32 [k] in [0, I). */
+ * soinfer_gemv_w4a16_sparse_accumulate.  rows: int32 [k] in [0, I).
+ * residual (optional, fp16 [H]): y = fp16(residual + fp16(sum)) -- the
+ * layer's residual add (generate.py:310), equal to adding after the GEMV. */
 int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, int64_t I,
                                    const int32_t* rows, const soinfer_half* h, soinfer_half* y,
                                    int64_t H, int64_t k, int64_t group_size, int64_t num_groups,
-                                   void* workspace, int64_t workspace_bytes, void* stream);
+                                   void* workspace, int64_t workspace_bytes, const soinfer_half* residual,
+                                   void* stream);
 
 /* Cache-or-stream 'down' direction: same as the sparse accumulate with each
  * row resolved through desc (see soinfer_gemv_dip_fused_up).  Bit-identical

@@ -256,7 +256,7 @@ int soinfer_gemv_w4a16_group_lop3(const uint8_t* Wq, const float* scale, const s
 
 int soinfer_gemv_w4a16_rows(const uint8_t* Wq, const float* scale, int64_t N, const int32_t* rows, int64_t num_sel,
                             const soinfer_half* x, soinfer_half* y, int64_t K, int64_t group_size, int64_t num_groups,
-                            void* stream) {
+                            const soinfer_half* glu_gate, void* stream) {
   const char* name = "gemv_w4a16_rows";
   if (int st = check_int4_layout(name, K, group_size, num_groups)) return st;
   REQUIRE(num_sel >= 0 && N >= 0, "%s: sizes must be >= 0", name);
@@ -271,8 +271,15 @@ int soinfer_gemv_w4a16_rows(const uint8_t* Wq, const float* scale, int64_t N, co
   src.rows1 = N;
   src.row_bytes = int4_row_bytes(K);
   src.num_groups = num_groups;
-  return cuda_result(
-      launch_gemv_w4(RowMode::kIndexed, src, as_half(x), as_half(y), num_sel, K, group_size, as_stream(stream)), name);
+  LaunchOpts opts;
+  opts.glu = as_half(glu_gate);
+  cudaError_t e = launch_gemv_w4(RowMode::kIndexed, src, as_half(x), as_half(y), num_sel, K, group_size,
+                                 as_stream(stream), opts);
+  if (e == cudaErrorNotSupported && glu_gate) {  // shape outside the bulk path: GEMV, then the SwiGLU kernel
+    e = launch_gemv_w4(RowMode::kIndexed, src, as_half(x), as_half(y), num_sel, K, group_size, as_stream(stream));
+    if (e == cudaSuccess) e = launch_swiglu(as_half(glu_gate), as_half(y), rows, as_half(y), num_sel, as_stream(stream));
+  }
+  return cuda_result(e, name);
 }
 
 int soinfer_gemv_w8a16(const int8_t* Wq, const float* scale, const soinfer_half* x, soinfer_half* y, int64_t N,
@@ -393,17 +400,23 @@ int64_t soinfer_sparse_workspace_bytes(int64_t H, int64_t k) {
 
 static int sparse_common(const char* name, RowMode mode, const RowSource& src, const soinfer_half* h, soinfer_half* y,
                          int64_t H, int64_t k, int64_t group_size, int64_t num_groups, void* ws, int64_t ws_bytes,
-                         void* stream) {
+                         void* stream, const soinfer_half* residual = nullptr) {
   if (int st = check_int4_layout(name, H, group_size, num_groups)) return st;
   REQUIRE(k >= 0, "%s: k must be >= 0", name);
   REQUIRE(y, "%s: null output", name);
-  if (k == 0) return cuda_result(cudaMemsetAsync(y, 0, (size_t)H * 2, as_stream(stream)), name);
+  if (k == 0) {
+    if (residual) return cuda_result(cudaMemcpyAsync(y, residual, (size_t)H * 2, cudaMemcpyDeviceToDevice,
+                                                     as_stream(stream)), name);
+    return cuda_result(cudaMemsetAsync(y, 0, (size_t)H * 2, as_stream(stream)), name);
+  }
   REQUIRE(h, "%s: null h", name);
   REQUIRE(ws && ws_bytes >= sparse_workspace_bytes(H, k), "%s: workspace too small (need %lld bytes)", name,
           (long long)sparse_workspace_bytes(H, k));
   REQUIRE(aligned(ws, 16), "%s: workspace must be 16-byte aligned", name);
-  return cuda_result(launch_sparse_down(mode, src, as_half(h), as_half(y), H, k, group_size, ws, as_stream(stream)),
-                     name);
+  LaunchOpts opts;
+  opts.resid = as_half(residual);
+  return cuda_result(
+      launch_sparse_down(mode, src, as_half(h), as_half(y), H, k, group_size, ws, as_stream(stream), opts), name);
 }
 
 int soinfer_gemv_w4a16_sparse_accumulate(const uint8_t* Wq_sel, const float* scale_sel, const soinfer_half* h,
@@ -451,7 +464,8 @@ int soinfer_gemv_w4a16_sparse_accumulate_noalloc(const uint8_t* Wq_sel, const fl
 
 int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, int64_t I, const int32_t* rows,
                                    const soinfer_half* h, soinfer_half* y, int64_t H, int64_t k, int64_t group_size,
-                                   int64_t num_groups, void* workspace, int64_t workspace_bytes, void* stream) {
+                                   int64_t num_groups, void* workspace, int64_t workspace_bytes,
+                                   const soinfer_half* residual, void* stream) {
   const char* name = "gemv_w4a16_sparse_rows";
   REQUIRE(k == 0 || (I >= 1 && Wq_T && scale_T && rows), "%s: null pointer or empty matrix", name);
   REQUIRE(aligned(Wq_T, 4), "%s: misaligned weights", name);
@@ -463,7 +477,7 @@ int soinfer_gemv_w4a16_sparse_rows(const uint8_t* Wq_T, const float* scale_T, in
   src.row_bytes = int4_row_bytes(H);
   src.num_groups = num_groups;
   return sparse_common(name, RowMode::kIndexed, src, h, y, H, k, group_size, num_groups, workspace, workspace_bytes,
-                       stream);
+                       stream, residual);
 }
 
 int soinfer_gemv_dip_fused_down(const uint8_t* cache_Wq, const float* cache_scale, int64_t C,

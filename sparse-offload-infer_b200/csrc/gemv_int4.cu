@@ -133,7 +133,7 @@ __device__ __forceinline__ void chunk_dot(const uint4 wa, const uint4 wb, const 
 template <RowMode M, bool PEER>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_w4_bulk_kernel(const RowSource src, const half* __restrict__ x, half* __restrict__ y, const int nrows,
-                        const int K, const BulkPlan p, const PeerSet ps) {
+                        const int K, const BulkPlan p, const PeerSet ps, const half* __restrict__ glu) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint4* xs = reinterpret_cast<uint4*>(smem);
   float* ss = reinterpret_cast<float*>(smem + p.smem_x);
@@ -209,7 +209,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     par = (int)(epoch & 1u);
   }
   auto put = [&](int64_t row, float v) {
-    const half h = __float2half_rn(v);
+    half h = __float2half_rn(v);
+    if (glu != nullptr) {  // SwiGLU epilogue on the selected row's gate value (x / (1 + exp(-x)) in fp32)
+      const float gv = __half2float(glu[M == RowMode::kIndexed ? src.idx[row] : row]);
+      h = __float2half_rn((gv / (1.0f + expf(-gv))) * __half2float(h));
+    }
     if constexpr (PEER) {
       for (int r = 0; r < ps.world; ++r) reinterpret_cast<half*>(peer_slot(ps, r, par, ps.rank))[row] = h;
     } else {
@@ -450,7 +454,7 @@ bool bulk_ok(const RowSource& src, const half* x, int64_t nrows, int64_t K, int6
 
 template <RowMode M, bool PEER>
 cudaError_t launch_bulk(const RowSource& src, const half* x, half* y, int64_t nrows, int64_t K, const BulkPlan& plan,
-                        int grid, const PeerSet& ps, cudaStream_t stream, bool pdl) {
+                        int grid, const PeerSet& ps, cudaStream_t stream, bool pdl, const half* glu = nullptr) {
   auto kernel = gemv_w4_bulk_kernel<M, PEER>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -459,7 +463,7 @@ cudaError_t launch_bulk(const RowSource& src, const half* x, half* y, int64_t nr
     attr_set = true;
   }
   return launch_ex(kernel, dim3(grid), dim3(kThreads), (size_t)plan.smem_total, stream, 1, pdl, src, x, y,
-                   (int)nrows, (int)K, plan, ps);
+                   (int)nrows, (int)K, plan, ps, glu);
 }
 
 template <RowMode M>
@@ -468,8 +472,9 @@ cudaError_t launch_mode(const RowSource& src, const half* x, half* y, int64_t nr
   BulkPlan plan;
   int grid = 0;
   if (bulk_ok<M>(src, x, nrows, K, gsz, plan, grid)) {
-    return launch_bulk<M, false>(src, x, y, nrows, K, plan, grid, PeerSet{}, stream, opts.pdl);
+    return launch_bulk<M, false>(src, x, y, nrows, K, plan, grid, PeerSet{}, stream, opts.pdl, opts.glu);
   }
+  if (opts.glu != nullptr) return cudaErrorNotSupported;  // the caller applies the epilogue separately
   const int64_t blocks = (nrows + 3) / 4;
   return launch_ex(gemv_w4_simt_kernel<M>, dim3((unsigned)blocks), dim3(128), 0, stream, 1, opts.pdl, src, x, y,
                    nrows, K, gsz);

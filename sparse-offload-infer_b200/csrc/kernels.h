@@ -37,6 +37,9 @@ inline int64_t peer_buffer_bytes(int64_t slot_bytes, int world) {
 
 struct LaunchOpts {
   bool pdl = false;  // programmatic dependent launch (weights not produced by the previous kernel)
+  // Optional output epilogues (the bulk INT4 GEMV / the sparse down GEMV):
+  const half* glu = nullptr;    // y[r] = fp16(silu(glu[idx[r]]) * fp16(dot))  (indexed rows: SwiGLU of DIP)
+  const half* resid = nullptr;  // y[c] = fp16(resid[c] + fp16(sum))           (sparse down: the residual add)
 };
 
 // y[r] = dot(row r of src, x) for r < nrows (INT4, AWQ order, fp32 accumulation).

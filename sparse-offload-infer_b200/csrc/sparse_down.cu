@@ -114,7 +114,7 @@ template <RowMode M, int VEC>
 __global__ void __launch_bounds__(kThreads)
     sparse_down_kernel(const RowSource src, const half* __restrict__ h, half* __restrict__ y, const int64_t H,
                        const int64_t k, const int64_t gsz, const int64_t chunks, const int64_t rows_per_slab,
-                       float* __restrict__ partials, int* __restrict__ tickets) {
+                       float* __restrict__ partials, int* __restrict__ tickets, const half* __restrict__ resid) {
   constexpr int kCols = VEC * 8;  // columns per chunk
   extern __shared__ float red[];  // [kPhases][kColChunks * kCols]
   __shared__ int is_last;
@@ -195,7 +195,9 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t slabs = gridDim.y;
 #pragma unroll 8
     for (int64_t r = 0; r < slabs; ++r) sum += __ldcg(partials + r * H + col);
-    y[col] = __float2half_rn(sum);
+    half out = __float2half_rn(sum);
+    if (resid != nullptr) out = __float2half_rn(__half2float(resid[col]) + __half2float(out));  // residual epilogue
+    y[col] = out;
   }
   if (threadIdx.x == 0) tickets[col_slab] = 0;  // leave the workspace ready for the next call
 }
@@ -216,11 +218,11 @@ cudaError_t launch_mode(const RowSource& src, const half* h, half* y, int64_t H,
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     return launch_ex(kernel, grid, dim3(kThreads), smem, stream, 1, opts.pdl, src, h, y, H, k, gsz, s.chunks,
-                     s.rows_per_slab, partials, tickets);
+                     s.rows_per_slab, partials, tickets, opts.resid);
   }
   const size_t smem = (size_t)kPhases * kColChunks * 8 * sizeof(float);
   return launch_ex(sparse_down_kernel<M, 1>, grid, dim3(kThreads), smem, stream, 1, opts.pdl, src, h, y, H, k, gsz,
-                   s.chunks, s.rows_per_slab, partials, tickets);
+                   s.chunks, s.rows_per_slab, partials, tickets, opts.resid);
 }
 
 }  // namespace

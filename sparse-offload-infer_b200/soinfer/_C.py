@@ -38,7 +38,7 @@ _SIGNATURES = {
     "soinfer_gemv_w4a16_group_ex": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, ctypes.c_uint32, _P]),
     "soinfer_gemv_batch_workspace_bytes": (_I64, [_I64]),
     "soinfer_gemv_w4a16_batch": (_INT, [_P, _I64, _P, _I64, _P]),
-    "soinfer_gemv_w4a16_rows": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P]),
+    "soinfer_gemv_w4a16_rows": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_gemv_w8a16": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "soinfer_topk_threshold_select": (_INT, [_P, _I64, _I64, _P, _P, _P]),
     "soinfer_topk_threshold_select_abs_f16": (_INT, [_P, _I64, _I64, _P, _P, _P]),
@@ -51,7 +51,7 @@ _SIGNATURES = {
     "soinfer_lm_head_argmax_workspace_bytes": (_I64, []),
     "soinfer_gemv_fp16_argmax": (_INT, [_P, _P, _P, _I64, _I64, _P, _P, _I64, _P]),
     "soinfer_gemv_w4a16_sparse_accumulate_noalloc": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
-    "soinfer_gemv_w4a16_sparse_rows": (_INT, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P]),
+    "soinfer_gemv_w4a16_sparse_rows": (_INT, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "soinfer_gemv_dip_fused_down": (_INT, [_P, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64,
                                            _P]),
     "soinfer_gather_rows_staged": (_INT, [_P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _P]),
@@ -366,7 +366,10 @@ def reset_workspaces() -> None:
         ws.zero_()
 
 
-def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: torch.Tensor | None = None):
+def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: torch.Tensor | None = None,
+                    glu_gate: torch.Tensor | None = None):
+    """Row-indirect INT4 GEMV; glu_gate (fp16 [N]): the output is
+    fp16(silu(glu_gate[rows]) * y) (DIP's SwiGLU in the epilogue)."""
     name = "gemv_w4a16_rows"
     _check(Wq_packed.is_cuda and Wq_packed.dtype == torch.uint8 and Wq_packed.is_contiguous() and Wq_packed.dim() == 2,
            name, "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
@@ -377,11 +380,14 @@ def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: tor
     _check(rows.dim() == 1, name, ": rows must be 1D")
     _f16(x, name + "(x)")
     _check(x.dim() == 1 and x.size(0) == K, name, ": x must be 1D [K]")
+    if glu_gate is not None:
+        _f16(glu_gate, name + "(glu_gate)")
+        _check(glu_gate.numel() == Wq_packed.size(0), name, ": glu_gate must hold N values")
     dev = _same_device(Wq_packed, scale, rows, x)
     y = out if out is not None else torch.empty(rows.numel(), dtype=torch.float16, device=dev)
     with torch.cuda.device(dev):
         _call("soinfer_gemv_w4a16_rows", _ptr(Wq_packed), _ptr(scale), Wq_packed.size(0), _ptr(rows), rows.numel(),
-              _ptr(x), _ptr(y), K, group_size, scale.size(1), _stream(dev))
+              _ptr(x), _ptr(y), K, group_size, scale.size(1), _ptr(glu_gate), _stream(dev))
     return y
 
 
@@ -565,7 +571,9 @@ def gemv_w4a16_sparse_accumulate_noalloc(Wq_selected, scale_selected, h_selected
 
 
 def gemv_w4a16_sparse_rows(Wq_T, scale_T, rows, h_selected, H: int, group_size: int,
-                           out: torch.Tensor | None = None):
+                           out: torch.Tensor | None = None, residual: torch.Tensor | None = None):
+    """Row-indirect sparse down GEMV; residual (fp16 [H]): the output is
+    fp16(residual + y) (the layer's residual add in the epilogue)."""
     name = "gemv_w4a16_sparse_rows"
     _check(Wq_T.is_cuda and Wq_T.dtype == torch.uint8 and Wq_T.is_contiguous() and Wq_T.dim() == 2, name,
            "(Wq_T): must be a contiguous 2D uint8 CUDA tensor")
@@ -576,12 +584,15 @@ def gemv_w4a16_sparse_rows(Wq_T, scale_T, rows, h_selected, H: int, group_size: 
     _f16(h_selected, name + "(h_selected)")
     k = rows.numel()
     _check(h_selected.dim() == 1 and h_selected.size(0) == k, name, ": h_selected must be 1D [k]")
+    if residual is not None:
+        _f16(residual, name + "(residual)")
+        _check(residual.numel() == H, name, ": residual must hold H values")
     dev = _same_device(Wq_T, scale_T, rows, h_selected)
     y = out if out is not None else torch.empty(H, dtype=torch.float16, device=dev)
     with torch.cuda.device(dev):
         ws, wsb = _sparse_ws(dev, H, k)
         _call("soinfer_gemv_w4a16_sparse_rows", _ptr(Wq_T), _ptr(scale_T), Wq_T.size(0), _ptr(rows), _ptr(h_selected),
-              _ptr(y), H, k, group_size, scale_T.size(1), ws, wsb, _stream(dev))
+              _ptr(y), H, k, group_size, scale_T.size(1), ws, wsb, _ptr(residual), _stream(dev))
     return y
 
 

@@ -53,11 +53,12 @@ def gemv_w4a16_group_lop3(Wq_packed: torch.Tensor, scale: torch.Tensor, x: torch
 
 
 def gemv_w4a16_rows(Wq_packed: torch.Tensor, scale: torch.Tensor, rows: torch.Tensor, x: torch.Tensor, K: int,
-                    group_size: int) -> torch.Tensor:
+                    group_size: int, glu_gate: torch.Tensor | None = None) -> torch.Tensor:
     """B200 addition: y[r] = (row rows[r] of dequant(Wq_packed, scale)) . x for a device-resident matrix --
     the gather of selected up_proj rows fused into the GEMV (bit-identical to
-    gemv_w4a16_group_lop3(Wq_packed[rows], scale[rows], x, K, group_size)). rows: int32 CUDA."""
-    return _C.gemv_w4a16_rows(Wq_packed, scale, rows, x, K, group_size)
+    gemv_w4a16_group_lop3(Wq_packed[rows], scale[rows], x, K, group_size)). rows: int32 CUDA.
+    glu_gate: y = swiglu(glu_gate, y, rows) computed in the epilogue (DIP's h_sel)."""
+    return _C.gemv_w4a16_rows(Wq_packed, scale, rows, x, K, group_size, glu_gate=glu_gate)
 
 
 def topk_threshold_select(abs_g: torch.Tensor, k: int) -> torch.Tensor:
@@ -101,10 +102,11 @@ def gemv_w4a16_sparse_accumulate(Wq_selected: torch.Tensor, scale_selected: torc
 
 
 def gemv_w4a16_sparse_rows(Wq_T: torch.Tensor, scale_T: torch.Tensor, rows: torch.Tensor, h_selected: torch.Tensor,
-                           H: int, group_size: int) -> torch.Tensor:
+                           H: int, group_size: int, residual: torch.Tensor | None = None) -> torch.Tensor:
     """B200 addition: sparse 'down' GEMV over rows `rows` (int32 CUDA) of a resident transposed matrix,
-    bit-identical to gemv_w4a16_sparse_accumulate(Wq_T[rows], scale_T[rows], h_selected, H, group_size)."""
-    return _C.gemv_w4a16_sparse_rows(Wq_T, scale_T, rows, h_selected, H, group_size)
+    bit-identical to gemv_w4a16_sparse_accumulate(Wq_T[rows], scale_T[rows], h_selected, H, group_size);
+    residual: residual + y computed in the epilogue."""
+    return _C.gemv_w4a16_sparse_rows(Wq_T, scale_T, rows, h_selected, H, group_size, residual=residual)
 
 
 def build_dip_descriptors(selected_indices: torch.Tensor, slot_of: torch.Tensor):

@@ -382,34 +382,37 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
         channel_counts[layer_idx].scatter_add_(0, idx_long, torch.ones_like(idx_long))
     if selected_out is not None:
         selected_out[layer_idx].append(idx_long.cpu().tolist())
-    return h2 + dip_mlp_tail(model, layer_idx, h3, gate, idx, dip_k, bufs, idx_long)
+    return dip_mlp_tail(model, layer_idx, h3, gate, idx, dip_k, bufs, idx_long, residual=h2)
 
 
 def dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor, idx: torch.Tensor,
-                 dip_k: int, bufs: DipBuffers, idx_long: torch.Tensor | None = None) -> torch.Tensor:
+                 dip_k: int, bufs: DipBuffers, idx_long: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
     """The DIP MLP after the selection (configs[1] block minus the gate GEMV
     and selector): up_proj on the selected rows, h = fp16(silu(g) * u),
-    down_proj_T sparse accumulate -- resident rows read in place, arena rows
-    gathered on the device.  Returns the down output (no residual)."""
+    down_proj_T sparse accumulate -- resident rows read in place (SwiGLU in
+    the row GEMV's epilogue, the residual in the down GEMV's), arena rows
+    gathered on the device.  Returns residual + down (or down)."""
     up = model.matrix(layer_idx, "mlp.up_proj.weight")
     down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
     g = model.group_size
     if idx_long is None and not (model.is_resident(up.handle.name) and model.is_resident(down_t.handle.name)):
         idx_long = idx.long()
     if model.is_resident(up.handle.name):
-        u_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, idx, h3, up.packed_k, g)
+        h_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, idx, h3, up.packed_k, g, glu_gate=gate)
     else:
         rows = bufs.up_rows(dip_k)
         ops.gather_rows_device(model.weight_source(up), idx, rows)
         u_sel = ops.gemv_w4a16_group_lop3(rows, up.scale.index_select(0, idx_long), h3, up.packed_k, g)
-    h_sel = ops.swiglu(gate, u_sel, idx)
+        h_sel = ops.swiglu(gate, u_sel, idx)
     if model.is_resident(down_t.handle.name):
         return ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, idx, h_sel,
-                                          model.hidden_size, g)
+                                          model.hidden_size, g, residual=residual)
     rows = bufs.down_rows(dip_k)
     ops.gather_rows_device(model.weight_source(down_t), idx, rows)
-    return ops.gemv_w4a16_sparse_accumulate(rows, down_t.scale.index_select(0, idx_long), h_sel, model.hidden_size,
+    down = ops.gemv_w4a16_sparse_accumulate(rows, down_t.scale.index_select(0, idx_long), h_sel, model.hidden_size,
                                             g)
+    return down if residual is None else residual + down
 
 
 def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,

@@ -379,8 +379,8 @@ def run_decoder_layer_dip_tp(pipeline, model, layer_idx, x_flat, pos, k_cache, v
         loc = (idx[a:b] - lo).contiguous()
         up = model.matrix(layer_idx, "mlp.up_proj.weight")
         down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
-        u_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, loc, h3, up.packed_k, g)
-        h_sel = ops.swiglu(gate_loc, u_sel, loc)
+        h_sel = ops.gemv_w4a16_rows(model.resident[up.handle.name], up.scale, loc, h3, up.packed_k, g,
+                                    glu_gate=gate_loc)
         part = ops.gemv_w4a16_sparse_rows(model.resident[down_t.handle.name], down_t.scale, loc, h_sel,
                                           model.hidden_size, g)
     else:

@@ -215,3 +215,23 @@ def test_dip_mlp_block_matches_oracle_and_cached_is_bit_identical(H, I, k):
     assert torch.equal(u_c, u_sel)
     y_c = ops.gemv_dip_fused_down(dW[hot_d], dS[hot_d], dW[m].contiguous(), dS[m].contiguous(), desc, h_sel, H, g)
     assert torch.equal(y_c, y)
+
+
+@pytest.mark.parametrize("n,K,k", [(6144, 2048, 3072), (17408, 5120, 8704), (300, 512, 37)])
+def test_fused_epilogues_equal_unfused(n, K, k):
+    """The rows GEMV with the SwiGLU epilogue equals rows GEMV then swiglu, and
+    the sparse down with the residual epilogue equals sparse down then the
+    fp16 add -- bit for bit (the DIP layer uses the fused forms)."""
+    gen = torch.Generator().manual_seed(n + k)
+    uW, uS, pk = (t.to(DEV) if torch.is_tensor(t) else t for t in int4_weights(n, K, 128, seed=n))
+    dW, dS, _ = (t.to(DEV) if torch.is_tensor(t) else t for t in int4_weights(n, K, 128, seed=n + 1))
+    x = fp16_randn(pk, seed=k).to(DEV)
+    gate = fp16_randn(n, seed=k + 1, std=2.0).to(DEV)
+    idx = torch.randperm(n, generator=gen)[:k].sort()[0].int().to(DEV)
+    fused = ops.gemv_w4a16_rows(uW, uS, idx, x, pk, 128, glu_gate=gate)
+    plain = ops.swiglu(gate, ops.gemv_w4a16_rows(uW, uS, idx, x, pk, 128), idx)
+    assert torch.equal(fused, plain)
+    res = fp16_randn(pk, seed=k + 2).to(DEV)
+    a = ops.gemv_w4a16_sparse_rows(dW, dS, idx, fused, pk, 128, residual=res)
+    b = res + ops.gemv_w4a16_sparse_rows(dW, dS, idx, fused, pk, 128)
+    assert torch.equal(a, b)
