@@ -122,7 +122,8 @@ def last_error() -> str:
 
 
 def device_errors() -> int:
-    """Reads and clears the device-side error bits (bit 0: a bounded copy wait timed out)."""
+    """Reads and clears the device-side error bits (bit 0: a bounded copy wait
+    timed out; bit 1: a peer-exchange wait timed out -- a rank never signalled)."""
     flags = ctypes.c_int(0)
     _call("soinfer_device_errors", ctypes.byref(flags))
     return flags.value

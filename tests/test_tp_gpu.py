@@ -238,3 +238,35 @@ def test_tensor_parallel(world):
     # not asserted equal (fp16 partial rounding), recorded for the failure message of a gross error
     same = sum(a == b for a, b in zip(res[0]["eager"], res[0]["full"]))
     assert same >= len(res[0]["full"]) - 3, (res[0]["eager"], res[0]["full"])
+
+
+def test_exchange_wait_times_out_and_reports():
+    """Failure detection without a fault: a two-rank exchange whose second
+    rank never signals (its buffer is a second local allocation nobody
+    drives) gives up after its bounded wait (1 s), raises the peer-timeout
+    device error bit and returns -- the context stays usable."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from soinfer import _C
+
+    dev = torch.device("cuda", 0)
+    slot = 64 * 1024
+    nbytes = _C.peer_buffer_bytes(slot, 2)
+    own, _ = _C.peer_buffer_create(nbytes, dev)
+    other, _ = _C.peer_buffer_create(nbytes, dev)
+    try:
+        peers = _C.PeerSetStruct()
+        peers.base[0], peers.base[1] = own, other
+        peers.rank, peers.world, peers.slot_bytes = 0, 2, slot
+        _C.device_errors()  # clear
+        x = torch.randn(512, device=dev).half()
+        out = torch.empty_like(x)
+        _C.tp_allreduce_add_rmsnorm(peers, x, None, None, out, None, 1e-6, dev)
+        torch.cuda.synchronize(dev)
+        assert _C.device_errors() & 2, "the timed-out wait did not report kErrPeerTimeout"
+        y = torch.ones(4, device=dev) * 2  # the context is still usable
+        assert float(y.sum().item()) == 8.0
+    finally:
+        torch.cuda.synchronize(dev)
+        _C.peer_buffer_destroy(own, dev)
+        _C.peer_buffer_destroy(other, dev)
