@@ -139,7 +139,7 @@ class ClockSampler:
 def cpu_gemv_sample(seconds: float, threads: int):
     """The reference's CPU path restated (oracle): fp32 matvec of the
     pre-dequantized INT4 weights, dequantization outside the timer
-    (tests/test_m4_kernels.py:157-168 oracle; BASELINE.md CPU plan).
+    (the reference's tests/test_m4_kernels.py:157-168 oracle).
     Returns (GB/s of algorithmic INT4 bytes, sample description, gemvs run)."""
     from oracle import reference_port as port
 

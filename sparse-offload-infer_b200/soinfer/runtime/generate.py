@@ -388,7 +388,7 @@ def run_decoder_layer_dip(pipeline: WeightPipeline, model: StreamingModel, layer
 def dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor, idx: torch.Tensor,
                  dip_k: int, bufs: DipBuffers, idx_long: torch.Tensor | None = None,
                  residual: torch.Tensor | None = None) -> torch.Tensor:
-    """The DIP MLP after the selection (configs[1] block minus the gate GEMV
+    """The DIP MLP after the selection (the DIP block minus the gate GEMV
     and selector): up_proj on the selected rows, h = fp16(silu(g) * u),
     down_proj_T sparse accumulate -- resident rows read in place (SwiGLU in
     the row GEMV's epilogue, the residual in the down GEMV's), arena rows
@@ -432,7 +432,7 @@ def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel
 def cached_dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor,
                         idx: torch.Tensor, bufs: DipBuffers, cache: HotCache,
                         miss_bytes: list[int] | None = None) -> torch.Tensor:
-    """The cache-aware DIP MLP after the selection (configs[2] block minus the
+    """The cache-aware DIP MLP after the selection (the cached-DIP block minus the
     gate GEMV and selector): selected channels resolve to hot-cache slots or
     misses; the misses' up / down_T rows are gathered from the pinned arena by
     the device (zero-copy over PCIe); one fused GEMV per direction reads both.

@@ -88,7 +88,7 @@ class Architecture:
     rope_theta: float = 1e6
 
 
-# BASELINE configs[3] / configs[4] architectures
+# the decode benchmark architectures (Qwen3-1.7B- and Qwen3-14B-shaped)
 QWEN3_1_7B = Architecture(28, 2048, 6144, 16, 8, 128, 151936)
 QWEN3_14B = Architecture(40, 5120, 17408, 40, 8, 128, 151936)
 

@@ -1,5 +1,5 @@
-"""Tensor-parallel decode across the GPUs of one node (
-the 14B-shaped model on 1/2/4/8 B200s).
+"""Tensor-parallel decode across the GPUs of one node (the 14B-shaped model
+on 1/2/4/8 B200s).
 
 Sharding (Megatron-style, one process per GPU):
 * column-parallel (output rows split): q_proj / k_proj / v_proj by heads

@@ -1,10 +1,10 @@
 """Generates tests/golden/hot_cache_golden.json from the reference implementation.
 
 Imports the reference's own python/soinfer/offload/hot_cache.py
-(sparse-offload-infer) from $SOINFER_REF_PYTHON (default
-/root/reference/python) -- its policy half is pure Python -- and records, for
+(sparse-offload-infer) from $SOINFER_REF_PYTHON (the reference checkout's
+python/ folder) -- its policy half is pure Python -- and records, for
 seeded synthetic selection traces (Zipf-skewed channel popularity, as in
-BASELINE configs[2]), the hot set of the static policy and the hit counts of
+the cache-aware DIP benchmark), the hot set of the static policy and the hit counts of
 the static, LRU and LFU-with-decay policies at several cache sizes.  The
 committed JSON pins soinfer.offload.hot_cache; this script only runs where
 the reference source is available.

@@ -190,7 +190,7 @@ def test_teacher_forced_nll_is_finite(models):
 
 
 def test_int8_per_channel_variant():
-    """The INT8 per-channel weight format (configs[4]'s variant): a dense layer
+    """The INT8 per-channel weight format (the 14B benchmark's variant): a dense layer
     vs the float64 composition with the oracle's INT8 GEMV, and the graph
     decoder's tokens equal the eager loop's."""
     model = synthetic_streaming_model(ARCH, seed=8, include_dip=False, resident=True, offload=False, bits=8)
