@@ -29,8 +29,8 @@ namespace soinfer {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kMaxSplits = 64;
-constexpr int kTargetCtas = 296;
+constexpr int kMaxSplits = 128;
+constexpr int kTargetCtas = 592;
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Attended length of the device-position form: *pos_dev + 1, clamped to [1, max_seq].
