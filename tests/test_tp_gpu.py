@@ -270,3 +270,57 @@ def test_exchange_wait_times_out_and_reports():
         torch.cuda.synchronize(dev)
         _C.peer_buffer_destroy(own, dev)
         _C.peer_buffer_destroy(other, dev)
+
+
+def test_exchange_single_rank_equals_local_ops():
+    """The exchange kernels on a one-rank peer set (one GPU, no peers): the
+    all-reduce + residual + RMSNorm equals add_rmsnorm (a sum over one rank is
+    the partial itself), the all-gather is the identity, the argmax returns
+    the local index plus the offset, and the batched peer task + finish equals
+    the GEMV with the residual epilogue followed by rmsnorm."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from soinfer import _C, ops
+    from tests.helpers import int4_weights
+
+    dev = torch.device("cuda", 0)
+    slot = 64 * 1024
+    own, _ = _C.peer_buffer_create(_C.peer_buffer_bytes(slot, 1), dev)
+    try:
+        peers = _C.PeerSetStruct()
+        peers.base[0] = own
+        peers.rank, peers.world, peers.slot_bytes = 0, 1, slot
+        g = torch.Generator(device=dev).manual_seed(3)
+        H = 5120
+        part = torch.randn(H, generator=g, device=dev).half()
+        res = torch.randn(H, generator=g, device=dev).half()
+        w = (torch.rand(H, generator=g, device=dev) + 0.5).half()
+        out_sum, out_norm = torch.empty_like(part), torch.empty_like(part)
+        _C.tp_allreduce_add_rmsnorm(peers, part, res, w, out_sum, out_norm, 1e-6, dev)
+        n3, n2 = ops.add_rmsnorm(res.unsqueeze(0), part.unsqueeze(0), w, 1e-6)
+        assert torch.equal(out_sum, n2.squeeze(0))
+        ref_norm = n3.squeeze(0).float()
+        assert bool(((out_norm.float() - ref_norm).abs() <= 1e-3 + 2e-3 * ref_norm.abs()).all())
+        loc = torch.randn(2048, generator=g, device=dev).half()
+        gathered = torch.empty_like(loc)
+        _C.tp_allgather(peers, loc, gathered)
+        assert torch.equal(gathered, loc)
+        logits = torch.randn(100, generator=g, device=dev).half()
+        idx = torch.tensor([17], dtype=torch.int32, device=dev)
+        out_idx = torch.empty(1, dtype=torch.int32, device=dev)
+        _C.tp_argmax(peers, logits, idx, 1000, out_idx)
+        assert int(out_idx.item()) == 1017
+        p, s, pk = int4_weights(H, 2560, 128, seed=5)
+        P, S = p.to(dev), s.to(dev)
+        x = torch.randn(pk, generator=g, device=dev).half()
+        _C.gemv_w4a16_batch([(P, S, x, None, pk, 128, -1)], peers)
+        fin_sum, fin_norm = torch.empty_like(res), torch.empty_like(res)
+        _C.tp_allreduce_add_rmsnorm(peers, None, res, w, fin_sum, fin_norm, 1e-6, dev)
+        ref = torch.empty(H, dtype=torch.float16, device=dev)
+        _C.gemv_w4a16_batch([(P, S, x, ref, pk, 128, -1, res)])
+        torch.cuda.synchronize(dev)
+        assert torch.equal(fin_sum, ref)
+        assert _C.device_errors() == 0
+    finally:
+        torch.cuda.synchronize(dev)
+        _C.peer_buffer_destroy(own, dev)
