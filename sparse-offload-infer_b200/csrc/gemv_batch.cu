@@ -293,8 +293,9 @@ __device__ __forceinline__ void producer_loop(const Params& B, int cta, int lane
                                            uint64_t* full, uint64_t* empty, int* item_off,
                                            volatile int* abort_flag) {
   // ------------------------------------------------------------ producer
-  // Ring allocation is FIFO: items are consumed in issue order, so the
-  // occupied bytes are [item_off[oldest], head) circularly.
+  // Ring allocation is FIFO: the producer frees items in issue order (it
+  // waits on each one's empty barrier, whichever consumer group takes it), so
+  // the occupied bytes are [item_off[oldest], head) circularly.
   int head = 0, issued = 0, oldest = 0;
   bool stop = false;
   for (int ti = 0; ti < B.num && !stop; ++ti) {
@@ -312,11 +313,28 @@ __device__ __forceinline__ void producer_loop(const Params& B, int cta, int lane
       const int nks = segd ? min(tk.ks, v.chunks - seg * tk.ks) : v.chunks;
       const int wb = rows * wrow, sb = rows * srow_f * 4;
       const int bytes = round128(wb) + round128(sb);
-      if (head + bytes > B.ring_bytes) head = 0;
-      while (issued > oldest) {
-        const int start = item_off[oldest % kMaxItems];
-        const bool overlap = head <= start && head + bytes > start;
-        if (issued - oldest < kMaxItems && !overlap) break;
+      // place the item at head, or at 0 when it does not fit before the end;
+      // the live items occupy [tail, head) -- or, once head has wrapped while
+      // the oldest item still lies beyond it, [tail, end) and [0, head), where
+      // only [head, tail) is free and wrapping again would overwrite them
+      while (true) {
+        int at = head;
+        bool ok = true;
+        if (issued == oldest) {
+          if (at + bytes > B.ring_bytes) at = 0;
+        } else {
+          const int tail = item_off[oldest % kMaxItems];
+          if (tail < head) {
+            if (at + bytes > B.ring_bytes) at = 0, ok = bytes <= tail;
+          } else {  // wrapped (tail == head: full)
+            ok = head + bytes <= tail;
+          }
+          ok = ok && issued - oldest < kMaxItems;
+        }
+        if (ok) {
+          head = at;
+          break;
+        }
         if (!warp_wait(&empty[oldest % kMaxItems], (uint32_t)((oldest / kMaxItems) & 1), abort_flag)) {
           stop = true;
           break;
@@ -765,6 +783,20 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms) {
     max_k = tk.K > max_k ? tk.K : max_k;
   }
   if (npeer > 1 || (npeer == 1 && B.peers.world < 1)) return false;
+  // A task whose glu / resid rows are an earlier task's y reads each row in
+  // the epilogue lane that wrote it, which needs the same base and row split;
+  // anything else goes to the ordered per-task fallback.
+  for (int i = 0; i < B.num; ++i) {
+    const GemvBatchTask& tk = B.tasks[i];
+    for (int j = 0; j < i; ++j) {
+      const GemvBatchTask& p = B.tasks[j];
+      if (p.y == nullptr) continue;
+      const half* lo = p.y;
+      const half* hi = p.y + p.N;
+      for (const half* e : {tk.glu, tk.resid})
+        if (e != nullptr && e < hi && e + tk.N > lo && (e != p.y || p.N != tk.N)) return false;
+    }
+  }
   B.need_counters = npeer > 0 ? 1 : 0;
   for (int i = 0; i < B.num; ++i) B.need_counters |= B.tasks[i].publish;
   B.grid = sms;

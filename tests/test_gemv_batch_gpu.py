@@ -41,6 +41,30 @@ def test_independent_tasks_match_oracle(shapes):
         assert_close(t[3], refs[i], f"batch task {i} {shapes[i]}")
 
 
+def test_mixed_item_sizes_share_the_ring():
+    """One CTA's item stream mixes large and small items in an irregular
+    order, so the ring's wrap point moves from lap to lap: every task still
+    matches the oracle, launch after launch (a placement that overwrote a live
+    item would corrupt whichever task was still being consumed)."""
+    mats = [int4_weights(n, k, 128, seed=60 + i) for i, (n, k) in enumerate([(6144, 2048), (740, 2048), (300, 4096)])]
+    dmats = [(p.to(DEV), s.to(DEV), pk) for p, s, pk in mats]
+    order = [0, 1, 0, 0, 2, 1, 1, 0, 2, 0, 1, 0, 0, 0, 2, 2, 1, 0, 1, 0, 2, 0, 0, 1]
+    tasks, refs = [], []
+    for i, m in enumerate(order):
+        p, s, pk = mats[m]
+        x = fp16_randn(pk, 70 + i)
+        y = torch.empty(p.size(0), dtype=torch.float16, device=DEV)
+        tasks.append((dmats[m][0], dmats[m][1], x.to(DEV), y, pk, 128, -1))
+        refs.append(port.gemv_w4a16(p.numpy(), s.numpy(), x.numpy(), pk, 128))
+    batch = _C.GemvBatch(tasks)
+    for rep in range(3):
+        batch.run()
+        torch.cuda.synchronize()
+        assert _C.device_errors() == 0
+        for i, t in enumerate(tasks):
+            assert_close(t[3], refs[i], f"rep {rep} task {i} (matrix {order[i]})")
+
+
 @pytest.mark.parametrize("shapes,g", [
     # tensor-parallel shards of the 14B layer: K-segmented down_proj (TP 1 / 2), scale rows of
     # 17, 10, 5 groups (not 16-byte rows: staged by plain loads)
