@@ -269,8 +269,32 @@ __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint
 #pragma unroll
       for (int i = 0; i < NM; ++i) consume_unit(xr[i], wa, w1, sa[i * kGroupWarps], s1p[i * kGroupWarps], br[i], i, acc0, acc1);
     } else {
+      // two chunks per iteration: their dot products are independent and
+      // interleave; the accumulation keeps chunk order (same rounding)
+      int i = 0;
 #pragma unroll 1
-      for (int i = 0; i < nm; ++i) {
+      for (; i + 1 < nm; i += 2) {
+        uint4 xf0[4], xf1[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          xf0[j] = ct.xq[i * (kGroupWarps * 16) + j];
+          xf1[j] = ct.xq[(i + 1) * (kGroupWarps * 16) + j];
+        }
+        const int sc0 = G128 ? i * kGroupWarps : (ct.c_first + i * kGroupWarps) / ct.cpg;
+        const int sc1 = G128 ? (i + 1) * kGroupWarps : (ct.c_first + (i + 1) * kGroupWarps) / ct.cpg;
+        const uint4 wa0 = *reinterpret_cast<const uint4*>(wa + i * (kGroupWarps * 64));
+        const uint4 wb0 = *reinterpret_cast<const uint4*>(w1 + i * (kGroupWarps * 64));
+        const uint4 wa1 = *reinterpret_cast<const uint4*>(wa + (i + 1) * (kGroupWarps * 64));
+        const uint4 wb1 = *reinterpret_cast<const uint4*>(w1 + (i + 1) * (kGroupWarps * 64));
+        float d00, d01, d10, d11;
+        chunk_dot(wa0, wb0, xf0, d00, d01);
+        chunk_dot(wa1, wb1, xf1, d10, d11);
+        acc0 = fmaf(sa[sc0], d00 - ct.sbias[i], acc0);
+        acc1 = fmaf(s1p[sc0], d01 - ct.sbias[i], acc1);
+        acc0 = fmaf(sa[sc1], d10 - ct.sbias[i + 1], acc0);
+        acc1 = fmaf(s1p[sc1], d11 - ct.sbias[i + 1], acc1);
+      }
+      if (i < nm) {
         uint4 xf[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) xf[j] = ct.xq[i * (kGroupWarps * 16) + j];
