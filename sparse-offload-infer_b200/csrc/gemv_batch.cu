@@ -60,6 +60,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "peer.cuh"
+#include "ring_place.h"
 
 namespace soinfer {
 
@@ -337,25 +338,12 @@ __device__ __forceinline__ void producer_loop(const Params& B, int cta, int lane
       const int nks = segd ? min(tk.ks, v.chunks - seg * tk.ks) : v.chunks;
       const int wb = rows * wrow, sb = rows * srow_f * 4;
       const int bytes = round128(wb) + round128(sb);
-      // place the item at head, or at 0 when it does not fit before the end;
-      // the live items occupy [tail, head) -- or, once head has wrapped while
-      // the oldest item still lies beyond it, [tail, end) and [0, head), where
-      // only [head, tail) is free and wrapping again would overwrite them
+      // place the item (ring_place.h); otherwise wait for the oldest item
       while (true) {
-        int at = head;
-        bool ok = true;
-        if (issued == oldest) {
-          if (at + bytes > B.ring_bytes) at = 0;
-        } else {
-          const int tail = item_off[oldest % kMaxItems];
-          if (tail < head) {
-            if (at + bytes > B.ring_bytes) at = 0, ok = bytes <= tail;
-          } else {  // wrapped (tail == head: full)
-            ok = head + bytes <= tail;
-          }
-          ok = ok && issued - oldest < kMaxItems;
-        }
-        if (ok) {
+        const int live = issued - oldest;
+        const int at = ring_place(head, live > 0 ? item_off[oldest % kMaxItems] : 0, live, bytes, B.ring_bytes,
+                                  kMaxItems);
+        if (at >= 0) {
           head = at;
           break;
         }
