@@ -73,3 +73,116 @@ def test_host_gather_validates_indices():
     idx = (ctypes.c_int64 * 2)(0, 9)
     st = lib.soinfer_gather_rows_staged(matrix, 4, 16, idx, 2, staging, 64, ctypes.c_void_p(1), 64, None)
     assert st == 1 and "out of range" in lib.soinfer_last_error().decode()
+
+
+# fake device addresses: the checks below fail before any pointer is touched or any CUDA call is made
+P = ctypes.c_void_p(0x10000)
+P2 = ctypes.c_void_p(0x20000)
+
+
+def _err():
+    return _C.lib().soinfer_last_error().decode()
+
+
+def test_batch_gemm_and_quantizer_arguments():
+    lib = _C.lib()
+    # batch-8 GEMM: M <= 8 tokens, strides cover K / N, alignment
+    assert lib.soinfer_gemm_w4a16(P, P, P, 2048, P, 6144, 9, 6144, 2048, 128, 16, None) == 1
+    assert "M (tokens)" in _err()
+    assert lib.soinfer_gemm_w4a16(P, P, P, 2048, P, 6144, 0, 6144, 2048, 128, 16, None) == 0
+    assert lib.soinfer_gemm_w4a16(P, P, P, 100, P, 6144, 2, 6144, 2048, 128, 16, None) == 1
+    assert "row strides" in _err()
+    assert lib.soinfer_gemm_w4a16(P, P, ctypes.c_void_p(0x10001), 2048, P, 6144, 2, 6144, 2048, 128, 16, None) == 1
+    assert "misaligned" in _err()
+    assert lib.soinfer_gemm_w4a16(P, P, P, 2048, P, 6144, 2, 6144, 2048, 128, 15, None) == 1
+    assert "num_groups" in _err()
+    # GPU quantizer: dtype, group size, shape
+    assert lib.soinfer_quantize_pack_int4(P, 3, 16, 256, 256, 128, P, P, None) == 1 and "dtype" in _err()
+    assert lib.soinfer_quantize_pack_int4(P, 0, 16, 256, 256, 12, P, P, None) == 1 and "power of two" in _err()
+    assert lib.soinfer_quantize_pack_int4(P, 0, 16, 256, 100, 128, P, P, None) == 1 and "row stride" in _err()
+    assert lib.soinfer_quantize_pack_int4(P, 0, 0, 256, 256, 128, P, P, None) == 0
+
+
+def _task(N=64, K=2048, g=128, dep=-1, y=P2, residual=None, glu=None, norm_w=None, norm_out=None):
+    return _C._GemvTask(P, P, P, y, N, K, g, (K + g - 1) // g, dep, residual, glu, norm_w, 1e-6, norm_out)
+
+
+def _tasks(*ts):
+    arr = (_C._GemvTask * len(ts))(*ts)
+    return arr, len(ts)
+
+
+def test_batched_gemv_arguments():
+    lib = _C.lib()
+    assert lib.soinfer_gemv_batch_workspace_bytes(-1) == 0
+    assert lib.soinfer_gemv_batch_workspace_bytes(_C.MAX_BATCH_TASKS + 1) == 0
+    assert lib.soinfer_gemv_batch_workspace_bytes(8) >= 9 * 4
+    assert lib.soinfer_gemv_w4a16_batch(None, 0, None, 0, None) == 0
+    assert lib.soinfer_gemv_w4a16_batch(None, _C.MAX_BATCH_TASKS + 1, None, 0, None) == 1
+    assert "num_tasks" in _err()
+    assert lib.soinfer_gemv_w4a16_batch(None, 1, None, 0, None) == 1 and "null task list" in _err()
+    cases = [
+        ((_task(dep=0),), "dep must be -1 or an earlier task"),
+        ((_task(y=None),), "null pointer"),  # y == NULL only with peers
+        ((_task(g=100),), "multiple of 8"),
+        ((_task(N=0),), "N must be >= 1"),
+        ((_task(norm_out=P),), "norm_out needs norm_weight"),
+        ((_task(norm_w=ctypes.c_void_p(0x10008)),), "norm prologue"),
+        # an epilogue input written by an earlier task of the batch must use its row split
+        ((_task(N=64, y=P2), _task(N=128, glu=P2)), "N differs"),
+        ((_task(N=64, y=P2), _task(N=128, residual=P2)), "N differs"),
+    ]
+    for ts, msg in cases:
+        arr, n = _tasks(*ts)
+        assert lib.soinfer_gemv_w4a16_batch(ctypes.addressof(arr), n, None, 0, None) == 1, msg
+        assert msg in _err(), (msg, _err())
+
+
+def _peers(world=2, rank=0, slot=4096, bases=None):
+    ps = _C.PeerSetStruct()
+    for r in range(world):
+        ps.base[r] = (bases[r] if bases is not None else 0x100000 * (r + 1))
+    ps.rank, ps.world, ps.slot_bytes = rank, world, slot
+    return ps
+
+
+def test_peer_set_and_exchange_arguments():
+    lib = _C.lib()
+    assert lib.soinfer_peer_buffer_bytes(8, 2) == 0
+    assert lib.soinfer_peer_buffer_bytes(16, 0) == 0
+    assert lib.soinfer_peer_buffer_bytes(16, _C.MAX_PEERS + 1) == 0
+    assert lib.soinfer_peer_buffer_bytes(1024, 2) == 256 + 2 * 2 * 1024  # header + two parities x world slots
+    ar = lib.soinfer_tp_allreduce_add_rmsnorm
+    assert ar(None, P, None, None, P2, None, 64, 1e-6, None) == 1 and "null peer set" in _err()
+    bad_sets = [
+        (_peers(world=0), "world size"),
+        (_peers(world=2, rank=2), "rank out of range"),
+        (_peers(slot=24), "slot_bytes"),
+        (_peers(bases=[0x100000, 0]), "peer buffer 1 null"),
+        (_peers(bases=[0x100000, 0x200010]), "256-byte aligned"),
+    ]
+    for ps, msg in bad_sets:
+        assert ar(ctypes.byref(ps), P, None, None, P2, None, 64, 1e-6, None) == 1, msg
+        assert msg in _err(), (msg, _err())
+    ps = _peers()
+    assert ar(ctypes.byref(ps), P, None, None, P2, None, 12, 1e-6, None) == 1 and "multiple of 8" in _err()
+    assert ar(ctypes.byref(ps), P, None, None, P2, None, 4096, 1e-6, None) == 1 and "slot_bytes" in _err()
+    assert ar(ctypes.byref(ps), P, None, None, None, None, 64, 1e-6, None) == 1 and "null output" in _err()
+    assert ar(ctypes.byref(ps), P, None, None, P2, P2, 64, 1e-6, None) == 1 and "weight with out_norm" in _err()
+    assert ar(ctypes.byref(ps), ctypes.c_void_p(0x10008), None, None, P2, None, 64, 1e-6, None) == 1
+    assert "16-byte aligned" in _err()
+    assert lib.soinfer_tp_allgather(ctypes.byref(ps), P, 4096 + 16, P2, None) == 1 and "nbytes" in _err()
+    assert lib.soinfer_tp_allgather(ctypes.byref(ps), P, 24, P2, None) == 1 and "nbytes" in _err()
+    assert lib.soinfer_tp_argmax(ctypes.byref(ps), P, P, -1, P2, None) == 1 and "offset" in _err()
+    assert lib.soinfer_tp_argmax(ctypes.byref(ps), None, P, 0, P2, None) == 1 and "null pointer" in _err()
+    tp = lib.soinfer_gemv_w4a16_tp_partial
+    assert tp(ctypes.byref(ps), P, P, P, 4096, 2048, 128, 16, None) == 1 and "2N <= slot_bytes" in _err()
+    assert tp(ctypes.byref(ps), P, P, P, 64, 2000, 8, 250, None) == 1 and "multiples of 128" in _err()
+    # batched tensor-parallel GEMV: one peer task, no epilogue on it
+    bt = lib.soinfer_gemv_w4a16_batch_tp
+    arr, n = _tasks(_task(y=None), _task(y=None))
+    assert bt(ctypes.byref(ps), ctypes.addressof(arr), n, None, 0, None) == 1 and "at most one task" in _err()
+    arr, n = _tasks(_task(y=None, residual=P2))
+    assert bt(ctypes.byref(ps), ctypes.addressof(arr), n, None, 0, None) == 1 and "no epilogue" in _err()
+    arr, n = _tasks(_task(N=4096, y=None))
+    assert bt(ctypes.byref(ps), ctypes.addressof(arr), n, None, 0, None) == 1 and "exceed the exchange slot" in _err()
