@@ -4,7 +4,10 @@ oracle/_ref/libsoinfer_ref.so is the reference's csrc/kernels/*.cu compiled
 from its sources for sm_100a (oracle/Makefile `ref`).  Here it pins the
 oracle restatement (selector bit-exact vs the reference kernel) and shows the
 sm_100a kernels agree with the reference implementation itself: selector
-bit-exact, GEMV / sparse / attention within the parity tolerance.  Skipped
+bit-exact, DIP descriptors bit-exact on cache hits (misses: same channels;
+the reference's miss order comes from atomics), GEMV (naive and LOP3), INT8
+GEMV (per-channel, grouped, per-tensor), sparse and cache-or-stream up /
+down GEMVs, attention, rmsnorm and RoPE within the parity tolerance.  Skipped
 when the reference library was not built (it needs the reference sources)."""
 import numpy as np
 import pytest
@@ -104,3 +107,113 @@ def test_rmsnorm_vs_reference_kernel():
     native.ref_lib().ref_rmsnorm(_p(x), _p(w), _p(out_ref), 4, 2048, 1e-6)
     torch.cuda.synchronize()
     assert_close(ops.rmsnorm(x, w, 1e-6), out_ref.double(), "rmsnorm vs reference kernel")
+
+
+def test_naive_gemv_vs_reference_kernel():
+    N, K = 2048, 6144
+    p, s, pk = int4_weights(N, K, 128, seed=7)
+    Wd, sd = p.to(DEV), s.to(DEV)
+    x = fp16_randn(pk, 8).to(DEV)
+    y_ref = torch.empty(N, dtype=torch.float16, device=DEV)
+    torch.cuda.synchronize()
+    native.ref_lib().ref_gemv_w4a16_group(_p(Wd), _p(sd), _p(x), _p(y_ref), N, pk, 128, sd.shape[1])
+    torch.cuda.synchronize()
+    assert_close(ops.gemv_w4a16_group(Wd, sd, x, pk, 128), y_ref.double(), "naive GEMV vs reference kernel")
+
+
+@pytest.mark.parametrize("mode", ["per_channel", "grouped", "per_tensor"])
+def test_gemv_w8a16_vs_reference_kernel(mode):
+    N, K = 1024, 4096
+    gen = torch.Generator().manual_seed(11)
+    Wq = torch.randint(-127, 128, (N, K), generator=gen, dtype=torch.int8)
+    if mode == "per_channel":
+        g, G, rows, stride = K, 1, N, 1
+    elif mode == "grouped":
+        g, G, rows, stride = 128, K // 128, N, K // 128
+    else:
+        g, G, rows, stride = K, 1, 1, 0
+    scale = (torch.rand(rows, G, generator=gen) * 2e-3 + 5e-4).float()
+    x = fp16_randn(K, 12)
+    Wd, sd, xd = Wq.to(DEV), scale.to(DEV), x.to(DEV)
+    y_ref = torch.empty(N, dtype=torch.float16, device=DEV)
+    torch.cuda.synchronize()
+    native.ref_lib().ref_gemv_w8a16(_p(Wd), _p(sd), _p(xd), _p(y_ref), N, K, g, G, stride)
+    torch.cuda.synchronize()
+    assert_close(ops.gemv_w8a16(Wd, sd, xd, g), y_ref.double(), f"INT8 {mode} vs reference kernel", max_abs=None)
+
+
+def _dip_case(seed, I=6144, H=2048, k=3072, C=1229):
+    """Config-3 shapes: a hot cache of C channels, k selected channels, the
+    misses staged in the descriptors' miss order (ours: ascending)."""
+    rng = np.random.default_rng(seed)
+    hot = np.sort(rng.choice(I, C, replace=False))
+    slot_of = np.full(I, -1, np.int32)
+    slot_of[hot] = np.arange(C, dtype=np.int32)
+    sel = np.sort(rng.choice(I, k, replace=False)).astype(np.int32)
+    sel_d, slot_d = torch.from_numpy(sel).to(DEV), torch.from_numpy(slot_of).to(DEV)
+    desc, miss, cnt = ops.build_dip_descriptors(sel_d, slot_d)
+    return hot, sel_d, slot_d, desc, miss[:int(cnt.item())].cpu().numpy()
+
+
+def _cache_and_staging(p, s, hot, miss_ch):
+    h, m = torch.from_numpy(np.asarray(hot, np.int64)), torch.from_numpy(np.asarray(miss_ch, np.int64))
+    return (p[h].contiguous().to(DEV), s[h].contiguous().to(DEV), p[m].contiguous().to(DEV),
+            s[m].contiguous().to(DEV))
+
+
+def test_dip_descriptors_vs_reference_kernel():
+    hot, sel, slot_of, desc, _ = _dip_case(21)
+    k = sel.numel()
+    r_desc = torch.empty(k, dtype=torch.int32, device=DEV)
+    r_miss = torch.full((k,), -1, dtype=torch.int32, device=DEV)
+    r_cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    native.ref_lib().ref_build_dip_descriptors(_p(sel), k, _p(slot_of), _p(r_desc), _p(r_miss), _p(r_cnt))
+    torch.cuda.synchronize()
+    _, miss, cnt = ops.build_dip_descriptors(sel, slot_of)
+    assert int(cnt.item()) == int(r_cnt.item())
+    hit = desc >= 0
+    assert torch.equal(r_desc >= 0, hit)
+    assert torch.equal(desc[hit], r_desc[hit])  # cache slots: bit-exact
+    # misses: the reference's positions come from atomics (any order); each descriptor still names its channel
+    pos, r_pos = (desc[~hit] & 0x7FFFFFFF).long(), (r_desc[~hit] & 0x7FFFFFFF).long()
+    assert torch.equal(miss[pos], sel[~hit]) and torch.equal(r_miss[r_pos], sel[~hit])
+    assert torch.equal(pos, torch.arange(pos.numel(), device=DEV))  # ours: ascending selected order
+
+
+def test_dip_fused_up_and_down_vs_reference_kernels():
+    I, H, g = 6144, 2048, 128
+    hot, sel, _, desc, miss_ch = _dip_case(22, I=I, H=H)
+    k = sel.numel()
+    # up: rows are channels of W_up [I, H]
+    p, s, pk = int4_weights(I, H, g, seed=23)
+    cW, cS, sW, sS = _cache_and_staging(p, s, hot, miss_ch)
+    x = fp16_randn(pk, 24).to(DEV)
+    u_ref = torch.empty(k, dtype=torch.float16, device=DEV)
+    torch.cuda.synchronize()
+    native.ref_lib().ref_gemv_dip_fused_up(_p(cW), _p(cS), _p(sW), _p(sS), _p(desc), _p(x), _p(u_ref), k, pk, g,
+                                           s.shape[1])
+    torch.cuda.synchronize()
+    assert_close(ops.gemv_dip_fused_up(cW, cS, sW, sS, desc, x, pk, g), u_ref.double(), "fused up vs reference")
+    # down: rows are channels of down_T [I, H]
+    p2, s2, pk2 = int4_weights(I, H, g, seed=25)
+    cW2, cS2, sW2, sS2 = _cache_and_staging(p2, s2, hot, miss_ch)
+    h = fp16_randn(k, 26, 0.5).to(DEV)
+    y_ref = torch.empty(pk2, dtype=torch.float16, device=DEV)
+    torch.cuda.synchronize()
+    native.ref_lib().ref_gemv_dip_fused_down(_p(cW2), _p(cS2), _p(sW2), _p(sS2), _p(desc), _p(h), _p(y_ref), pk2, k,
+                                             g, s2.shape[1])
+    torch.cuda.synchronize()
+    assert_close(ops.gemv_dip_fused_down(cW2, cS2, sW2, sS2, desc, h, pk2, g), y_ref.double(), "fused down vs reference",
+                 max_abs=None)
+
+
+def test_rope_vs_reference_kernel():
+    torch.manual_seed(3)
+    x = torch.randn(40, 128, device=DEV, dtype=torch.float16)
+    cos, sin = ops.precompute_rope_cos_sin(128, 1e6, 777, DEV)
+    x_ref = x.clone()
+    torch.cuda.synchronize()
+    native.ref_lib().ref_rope_apply(_p(x_ref), _p(cos), _p(sin), 40, 128)
+    torch.cuda.synchronize()
+    assert_close(ops.apply_rope(x.clone(), cos, sin), x_ref.double(), "rope vs reference kernel")
