@@ -31,15 +31,15 @@ constexpr int kThreads = 256;
 constexpr int kColChunks = 8;            // 16-byte column chunks per column slab (256 columns)
 constexpr int kPhases = kThreads / kColChunks;
 constexpr int kTargetCtas = 296;
-constexpr int64_t kCounterBytes = 4096;  // room for 1024 column-slab tickets
+constexpr int64_t kCounterBytes = 4096;  // tickets that every workspace starts with: 1024 column slabs
 constexpr int64_t kStaticScratchBytes = 512 * 1024;
 constexpr int kMaxDevices = 64;
 
 // Scratch of the no-alloc entry point, one copy per device (file-scope device
 // memory: no allocation at call time).  Same layout as a caller workspace:
-// kCounterBytes of column-slab tickets, which must start at zero and which
-// every call leaves at zero, then the fp32 partial rows (overwritten by each
-// call).  Workspaces of up to kStaticScratchBytes fit: every shape from H =
+// the column-slab tickets (ticket_bytes(H): kCounterBytes, more for H above
+// 65536), which must start at zero and which every call leaves at zero, then
+// the fp32 partial rows (overwritten by each call).  Workspaces of up to kStaticScratchBytes fit: every shape from H =
 // 2048 to H = 16384 needs about 0.3 MiB.
 static __device__ __align__(256) unsigned char g_sparse_scratch[kStaticScratchBytes];
 
@@ -64,6 +64,16 @@ DownShape down_shape(int64_t H, int64_t k, bool vec4) {
   if (s.rows_per_slab < 1) s.rows_per_slab = 1;
   s.row_slabs = (k + s.rows_per_slab - 1) / s.rows_per_slab;
   return s;
+}
+
+// Ticket area of a workspace for H output columns: one int per column slab of
+// the wider of the two kernel shapes, at least kCounterBytes.  The first
+// kCounterBytes are kept zeroed by every call; a launch that needs more clears
+// the rest first (it may hold partial rows of an earlier, narrower call).
+int64_t ticket_bytes(int64_t H) {
+  const int64_t a = down_shape(H, 1, true).col_slabs, b = down_shape(H, 1, false).col_slabs;
+  const int64_t need = ((a > b ? a : b) * 4 + 255) / 256 * 256;
+  return need > kCounterBytes ? need : kCounterBytes;
 }
 
 template <RowMode M>
@@ -210,7 +220,13 @@ cudaError_t launch_mode(const RowSource& src, const half* h, half* y, int64_t H,
                     (M != RowMode::kDesc || aligned16(src.W2));
   const DownShape s = down_shape(H, k, vec4);
   int* tickets = reinterpret_cast<int*>(workspace);
-  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterBytes);
+  const int64_t tb = ticket_bytes(H);
+  float* partials = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + tb);
+  if (tb > kCounterBytes) {
+    cudaError_t e = cudaMemsetAsync(reinterpret_cast<char*>(workspace) + kCounterBytes, 0, (size_t)(tb - kCounterBytes),
+                                    stream);
+    if (e != cudaSuccess) return e;
+  }
   const dim3 grid((unsigned)s.col_slabs, (unsigned)s.row_slabs);
   if (vec4) {
     const size_t smem = (size_t)kPhases * kColChunks * 32 * sizeof(float);
@@ -232,7 +248,7 @@ int64_t sparse_workspace_bytes(int64_t H, int64_t k) {
   const DownShape a = down_shape(H, k, true);
   const DownShape b = down_shape(H, k, false);
   const int64_t slabs = a.row_slabs > b.row_slabs ? a.row_slabs : b.row_slabs;
-  return kCounterBytes + slabs * H * (int64_t)sizeof(float);
+  return ticket_bytes(H) + slabs * H * (int64_t)sizeof(float);
 }
 
 int64_t sparse_static_scratch_bytes() { return kStaticScratchBytes; }

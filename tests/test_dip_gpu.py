@@ -46,6 +46,23 @@ def test_sparse_accumulate_matches_oracle(k, H, g):
     assert_close(y, ref, f"sparse[{k}x{H}]")
 
 
+def test_sparse_accumulate_wide_h_after_a_narrow_call():
+    """H above 65536 on the scalar path (g = 8) needs more than 1024
+    column-slab tickets: the ticket area grows with H and is cleared before
+    the launch, because the cached workspace still holds the partial rows of
+    the narrower call that ran just before."""
+    p0, s0, pk0 = int4_weights(3072, 2048, 128, seed=11)
+    h0 = fp16_randn(3072, seed=12, std=0.5)
+    ops.gemv_w4a16_sparse_accumulate(p0.to(DEV), s0.to(DEV), h0.to(DEV), pk0, 128)
+    k, H, g = 40, 70000, 8
+    p, s, pk = int4_weights(k, H, g, seed=13)
+    h = fp16_randn(k, seed=14, std=0.5)
+    ref = port.sparse_accumulate(p.numpy(), s.numpy(), h.numpy(), pk, g)
+    for rep in range(2):
+        y = ops.gemv_w4a16_sparse_accumulate(p.to(DEV), s.to(DEV), h.to(DEV), pk, g)
+        assert_close(y, ref, f"sparse[{k}x{H}] g={g} rep {rep}")
+
+
 def test_sparse_accumulate_zero_rows_and_determinism():
     p, s, pk = int4_weights(3072, 2048, 128, seed=1)
     h = fp16_randn(3072, 2, 0.5).to(DEV)

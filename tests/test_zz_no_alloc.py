@@ -20,7 +20,7 @@ def _case(k, H, g, seed):
     return packed.to(DEV), scale.to(DEV), h.to(DEV)
 
 
-@pytest.mark.parametrize("H,k,g", [(2048, 3072, 128), (5120, 1088, 128), (1000, 37, 8)])
+@pytest.mark.parametrize("H,k,g", [(2048, 3072, 128), (5120, 1088, 128), (1000, 37, 8), (70000, 16, 8)])
 def test_noalloc_matches_workspace_entry_twice(H, k, g):
     for call in range(2):
         Wq, s, h = _case(k, H, g, seed=100 * call + k)
