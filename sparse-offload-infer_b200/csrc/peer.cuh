@@ -20,7 +20,11 @@
 // for e + 2 only after it saw everybody's e + 1 flag, which each rank sets
 // only after it finished reading its e inbox.  All ranks must run the same
 // sequence of exchanges.  Every poll is bounded (kPeerWaitNs): on timeout the
-// kernel records kErrPeerTimeout and returns (no hang).
+// kernel records kErrPeerTimeout and returns (no hang) without advancing its
+// epoch.  The ranks are then out of step (this rank already signalled e, a
+// late rank may not have), so after kErrPeerTimeout every rank resets its own
+// buffer's header (flags, epoch, ticket: soinfer_peer_buffer_reset) between
+// steps, with a host barrier before and after, and the exchanges restart at 1.
 #pragma once
 
 #include "common.cuh"

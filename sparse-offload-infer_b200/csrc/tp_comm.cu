@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(kThreads)
     }
     peer_signal_all(ps, par, e);
   }
-  if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout)) {
+  const bool ok = peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout);
+  if (ok) {
     float ss = 0.f;
     for (int i = tid; i < n8; i += kThreads) {
       float acc[8];
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   __syncthreads();
-  if (tid == 0) *peer_epoch(ps) = (int)e;
+  if (tid == 0 && ok) *peer_epoch(ps) = (int)e;  // a timed-out exchange is not counted (see peer.cuh)
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -115,14 +116,15 @@ __global__ void __launch_bounds__(kThreads)
     for (int r = 0; r < ps.world; ++r) reinterpret_cast<uint4*>(peer_slot(ps, r, par, ps.rank))[i] = v;
   }
   peer_signal_all(ps, par, e);
-  if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout)) {
+  const bool ok = peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout);
+  if (ok) {
     for (int r = 0; r < ps.world; ++r) {
       const uint4* src = reinterpret_cast<const uint4*>(peer_slot(ps, ps.rank, par, r));
       for (int i = tid; i < n16; i += kThreads) out[(int64_t)r * n16 + i] = __ldcg(src + i);
     }
   }
   __syncthreads();
-  if (tid == 0) *peer_epoch(ps) = (int)e;
+  if (tid == 0 && ok) *peer_epoch(ps) = (int)e;  // a timed-out exchange is not counted (see peer.cuh)
 }
 
 // fp16 bits -> order-preserving key (the fused LM-head argmax's key).
@@ -147,7 +149,8 @@ __global__ void tp_argmax_kernel(const PeerSet ps, const half* __restrict__ logi
     *reinterpret_cast<unsigned long long*>(peer_slot(ps, tid, par, ps.rank)) = key;
   }
   peer_signal_all(ps, par, e);
-  if (peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout) && tid == 0) {
+  const bool ok = peer_wait_all(ps, par, e, &g_tp_error, kErrPeerTimeout);
+  if (ok && tid == 0) {
     unsigned long long best = 0;
     for (int r = 0; r < ps.world; ++r) {
       const unsigned long long k = __ldcg(reinterpret_cast<const unsigned long long*>(peer_slot(ps, ps.rank, par, r)));
@@ -156,7 +159,7 @@ __global__ void tp_argmax_kernel(const PeerSet ps, const half* __restrict__ logi
     *out_idx = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   }
   __syncthreads();
-  if (tid == 0) *peer_epoch(ps) = (int)e;
+  if (tid == 0 && ok) *peer_epoch(ps) = (int)e;  // a timed-out exchange is not counted (see peer.cuh)
 }
 
 }  // namespace

@@ -227,6 +227,23 @@ class PeerExchange:
         self._next_normed = None  # (x, rmsnorm(x)) left by the last fused all-reduce for the next layer
         dist.barrier(group=group)
 
+    def reset(self) -> None:
+        """Recovery after a peer timeout (device error bit 2): a timed-out
+        exchange leaves the ranks out of step, so every rank -- between
+        steps, none of its kernels in flight -- zeroes its own buffer header
+        behind a barrier, and the exchanges restart from the first.
+        Collective: all ranks of the group call it."""
+        import torch.distributed as dist
+
+        from .. import _C
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        _C.peer_buffer_reset(self._own, self.device)
+        torch.cuda.synchronize(self.device)
+        self._next_normed = None
+        dist.barrier(group=self.group)
+
     def allreduce_add_rmsnorm(self, partial, residual=None, weight=None, eps: float = 1e-6):
         """(out_norm or None, out_sum): out_sum = fp16(residual + sum of the ranks' partials)."""
         from .. import _C

@@ -240,6 +240,16 @@ def test_tensor_parallel(world):
     assert same >= len(res[0]["full"]) - 3, (res[0]["eager"], res[0]["full"])
 
 
+def _read_i32(ptr: int, offset: int) -> int:
+    """One int32 of device memory at a raw address (test-only, through the CUDA runtime)."""
+    import ctypes
+
+    cudart = ctypes.CDLL("libcudart.so.12")
+    out = ctypes.c_int32()
+    assert cudart.cudaMemcpy(ctypes.byref(out), ctypes.c_void_p(ptr + offset), ctypes.c_size_t(4), 2) == 0
+    return out.value
+
+
 def test_exchange_wait_times_out_and_reports():
     """Failure detection without a fault: a two-rank exchange whose second
     rank never signals (its buffer is a second local allocation nobody
@@ -266,6 +276,16 @@ def test_exchange_wait_times_out_and_reports():
         assert _C.device_errors() & 2, "the timed-out wait did not report kErrPeerTimeout"
         y = torch.ones(4, device=dev) * 2  # the context is still usable
         assert float(y.sum().item()) == 8.0
+        assert _read_i32(own, 64) == 0, "a timed-out exchange must not advance the exchange count"
+        # recovery: reset the header, then the buffer serves exchanges again (here a one-rank set)
+        _C.peer_buffer_reset(own, dev)
+        solo = _C.PeerSetStruct()
+        solo.base[0] = own
+        solo.rank, solo.world, solo.slot_bytes = 0, 1, slot
+        _C.tp_allreduce_add_rmsnorm(solo, x, None, None, out, None, 1e-6, dev)
+        torch.cuda.synchronize(dev)
+        assert _C.device_errors() == 0
+        assert torch.equal(out, x) and _read_i32(own, 64) == 1
     finally:
         torch.cuda.synchronize(dev)
         _C.peer_buffer_destroy(own, dev)
