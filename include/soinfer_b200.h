@@ -432,7 +432,10 @@ int soinfer_quantize_pack_int4(const void* w, int32_t dtype, int64_t N, int64_t 
  * NVLink, then signal them with system-scope release flags; every wait is
  * bounded (1 s) and a timeout raises a device error bit
  * (soinfer_device_errors) instead of hanging.  All ranks must issue the same
- * sequence of exchange calls on their streams.
+ * sequence of exchange calls on their streams.  A timed-out exchange leaves
+ * the ranks out of step: after the error bit (bit 1) every rank calls
+ * soinfer_peer_buffer_reset on its own buffer between steps, with a host
+ * barrier before and after, before the next exchange.
  *
  * allreduce_add_rmsnorm: out_sum = fp16(residual + fp16(sum over ranks of
  * partial)) (sum in fp32, rank order; residual may be NULL), and when
@@ -462,6 +465,9 @@ int soinfer_peer_buffer_create(int64_t bytes, void** dptr, void* ipc_handle);
 int soinfer_peer_buffer_open(const void* ipc_handle, void** dptr);
 int soinfer_peer_buffer_close(void* dptr);
 int soinfer_peer_buffer_destroy(void* dptr);
+/* Zeroes this rank's exchange header (flags, exchange count, ticket) on
+ * `stream`: the recovery step after a peer timeout (see above). */
+int soinfer_peer_buffer_reset(void* dptr, void* stream);
 int soinfer_tp_allreduce_add_rmsnorm(const soinfer_peer_set* peers, const soinfer_half* partial,
                                      const soinfer_half* residual, const soinfer_half* weight,
                                      soinfer_half* out_sum, soinfer_half* out_norm, int64_t n, float eps,

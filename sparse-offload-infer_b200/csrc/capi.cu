@@ -102,6 +102,31 @@ int64_t soinfer_gemv_batch_workspace_bytes(int64_t num_tasks) {
   return gemv_batch_workspace_bytes(num_tasks);
 }
 
+// The streaming kernel serves a batch of plain, independent GEMVs (no dep, no
+// epilogue or prologue, no x / y overlap between tasks) that is large enough
+// to give every warp of the GPU at least two units.
+static bool stream_eligible(const soinfer_gemv_task* tasks, int64_t n, int sms) {
+  int64_t units = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const soinfer_gemv_task& t = tasks[i];
+    if (t.dep >= 0 || t.residual || t.glu_gate || t.norm_weight || !t.y || !aligned(t.x, 8)) return false;
+    units += cdiv(t.N, 16 * kStreamTiles);
+  }
+  if (units < 2LL * sms * kStreamWarps) return false;
+  for (int64_t i = 0; i < n; ++i) {
+    const uintptr_t ylo = reinterpret_cast<uintptr_t>(tasks[i].y), yhi = ylo + 2 * tasks[i].N;
+    for (int64_t j = 0; j < n; ++j) {
+      const uintptr_t xlo = reinterpret_cast<uintptr_t>(tasks[j].x), xhi = xlo + 2 * tasks[j].K;
+      if (xlo < yhi && ylo < xhi) return false;
+      if (j != i) {
+        const uintptr_t zlo = reinterpret_cast<uintptr_t>(tasks[j].y), zhi = zlo + 2 * tasks[j].N;
+        if (zlo < yhi && ylo < zhi) return false;  // two tasks writing the same rows: keep task order
+      }
+    }
+  }
+  return true;
+}
+
 static int gemv_batch_common(const char* name, const PeerSet* peers, const soinfer_gemv_task* tasks,
                              int64_t num_tasks, void* workspace, int64_t workspace_bytes, void* stream) {
   REQUIRE(num_tasks >= 0 && num_tasks <= kMaxBatchTasks, "%s: num_tasks must be in [0, %d]", name, kMaxBatchTasks);
@@ -143,6 +168,25 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
            t.K < (1 << 30);
   }
   cudaStream_t st = as_stream(stream);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (fast && !peers && stream_eligible(tasks, num_tasks, sms)) {
+    // a large list of independent GEMVs: the streaming kernel (gemv_stream.cu)
+    static GemvStreamParams S;
+    static std::mutex smu;
+    std::lock_guard<std::mutex> lk(smu);
+    S.num = (int)num_tasks;
+    for (int64_t i = 0; i < num_tasks; ++i) {
+      const soinfer_gemv_task& t = tasks[i];
+      S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.x), as_half(t.y), (int)t.N, (int)t.K,
+                                  (int)t.num_groups, (int)(t.group_size / 128), 0, 0};
+    }
+    if (plan_gemv_stream(S, sms)) {
+      REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
+              "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes());
+      return cuda_result(launch_gemv_stream(S, reinterpret_cast<int*>(workspace), st), name);
+    }
+  }
   if (fast) {
     static GemvBatchParams B;  // large: not on the stack
     static std::mutex mu;
@@ -173,8 +217,6 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
       d.eps = t.norm_eps;
       d.norm_out = as_half(t.norm_out);
     }
-    int sms = 148, dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (plan_gemv_batch(B, sms)) {
       REQUIRE(workspace && workspace_bytes >= gemv_batch_workspace_bytes(num_tasks) && aligned(workspace, 4),
               "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_batch_workspace_bytes(num_tasks));
@@ -778,6 +820,11 @@ int soinfer_peer_buffer_close(void* dptr) {
 int soinfer_peer_buffer_destroy(void* dptr) {
   REQUIRE(dptr, "peer_buffer_destroy: null pointer");
   return cuda_result(cudaFree(dptr), "peer_buffer_destroy");
+}
+
+int soinfer_peer_buffer_reset(void* dptr, void* stream) {
+  REQUIRE(dptr, "peer_buffer_reset: null pointer");
+  return cuda_result(cudaMemsetAsync(dptr, 0, (size_t)kPeerHeaderBytes, as_stream(stream)), "peer_buffer_reset");
 }
 
 int soinfer_tp_allreduce_add_rmsnorm(const soinfer_peer_set* peers, const soinfer_half* partial,

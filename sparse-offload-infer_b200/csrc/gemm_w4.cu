@@ -20,6 +20,7 @@
 // tokens] are summed in warp order (deterministic) and written.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace soinfer {
 namespace {
@@ -232,12 +233,7 @@ cudaError_t launch_gemm_w4(const uint8_t* W, const float* S, const half* X, int6
   p.smem_red = kWarps * 16 * kTokens * 4;
   p.smem_total = p.smem_x + p.smem_scale + p.smem_stage + p.smem_red;
   if (p.smem_total > 226 * 1024) return cudaErrorNotSupported;
-  static int attr_bytes = 0;
-  if (p.smem_total > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_w4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_total);
-    if (e != cudaSuccess) return e;
-    attr_bytes = p.smem_total;
-  }
+  if (cudaError_t e = ensure_smem_attr<gemm_w4_kernel>(p.smem_total); e != cudaSuccess) return e;
   gemm_w4_kernel<<<grid, kThreads, p.smem_total, stream>>>(W, S, X, ldx, Y, ldy, (int)N, (int)K, p);
   return cudaGetLastError();
 }

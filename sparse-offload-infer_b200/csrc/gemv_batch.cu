@@ -59,6 +59,7 @@
 // sparse-offload-infer.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "peer.cuh"
 #include "ring_place.h"
 
@@ -825,13 +826,8 @@ namespace {
 
 template <class Params>
 cudaError_t launch_params(const Params& B, int* counters, cudaStream_t stream) {
-  static int attr_bytes = 0;  // callers serialise launches (the C ABI holds a mutex)
   auto kernel = gemv_batch_kernel<Params>;
-  if (B.smem_bytes > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B.smem_bytes);
-    if (e != cudaSuccess) return e;
-    attr_bytes = B.smem_bytes;
-  }
+  if (cudaError_t e = ensure_smem_attr<gemv_batch_kernel<Params>>(B.smem_bytes); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(B.grid);
   cfg.blockDim = dim3(kThreads);

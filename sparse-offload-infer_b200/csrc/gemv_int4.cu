@@ -456,12 +456,7 @@ template <RowMode M, bool PEER>
 cudaError_t launch_bulk(const RowSource& src, const half* x, half* y, int64_t nrows, int64_t K, const BulkPlan& plan,
                         int grid, const PeerSet& ps, cudaStream_t stream, bool pdl, const half* glu = nullptr) {
   auto kernel = gemv_w4_bulk_kernel<M, PEER>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  if (cudaError_t e = ensure_smem_attr<gemv_w4_bulk_kernel<M, PEER>>(200 * 1024); e != cudaSuccess) return e;
   return launch_ex(kernel, dim3(grid), dim3(kThreads), (size_t)plan.smem_total, stream, 1, pdl, src, x, y,
                    (int)nrows, (int)K, plan, ps, glu);
 }

@@ -1,0 +1,354 @@
+// Streaming INT4 GEMV over a list of independent GEMVs: the weight stream of
+// many matrices in one launch, every warp its own pipeline.
+//
+// Why a second batched kernel: in the persistent batched GEMV (gemv_batch.cu)
+// a CTA's slab of each task is split along K across a group of warps, so
+// every task costs a hand-off chain (x ready -> items -> partial rows ->
+// epilogue sum) and the consumer warps spend most cycles waiting on it.  When
+// no task of a launch reads another task's output, none of that is needed:
+// here a warp owns whole units -- T 16-row tiles over the full K -- so its
+// row sums never leave registers, and it fetches its own operands.
+//
+// Work split: units (task, 16*T rows) are handed out in task order by a
+// global ticket (one atomicAdd per unit, grabbed one unit ahead); the planner
+// orders the tasks by decreasing K (bigger units first, so the launch ends on
+// the smallest ones).  Rows past N are clamped on load and never stored.
+//
+// Per warp: a private ring of D shared-memory stages, each one 128-K chunk of
+// the unit -- 16*T rows x 64 B of packed weights (cp.async 16 B per lane per
+// 8 rows), the chunk's 256 B of x (8 B per lane) and the rows' scales for the
+// chunk's group (4 B per lane) -- plus a 16-byte tag (task, row0, chunk,
+// flags) written by lane 0.  The fetch of chunk i + D is issued right after
+// chunk i is read out of its stage, so D chunks per warp are always in flight
+// (16 warps x D x 16T x 64 B per SM); completion is cp.async.wait_group, no
+// mbarrier and no cross-warp synchronisation.  The fetch cursor runs ahead
+// across unit boundaries, so the pipeline never drains between units.
+//
+// Math per chunk (identical to gemv_batch.cu's): the biased LOP3 unpack into
+// exact fp16 (1024 + (n ^ 8), 1024 + 16 (n ^ 8)) feeding mma.sync.m16n8k16
+// with x replicated over the B columns (fp32 accumulation), the bias removed
+// with the chunk's x sums (one MMA), then acc = fma(scale, dot - bias, acc)
+// in chunk order -- so a row's result depends only on its own bytes and x.
+//
+// Reference semantics per GEMV: csrc/kernels/gemv_w4a16_group.cu:77-127 of
+// sparse-offload-infer (y[n] = half(sum_k s[n, k/g] * q[n,k] * x[k]), fp32
+// accumulation).
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+
+namespace soinfer {
+
+namespace {
+
+
+// Stage layout for units of T 16-row tiles.
+template <int T>
+struct StageLayout {
+  static constexpr int kRows = 16 * T;
+  static constexpr int kW = 0;                   // [2T row groups][32 lanes][16 B]
+  static constexpr int kX = kRows * 64;          // chunk x: 256 B, t-pieces 2 / 3 shifted by 16 B
+  static constexpr int kS = kX + 288;            // [kRows] fp32 scales
+  static constexpr int kTag = kS + kRows * 4;    // int4 tag
+  static constexpr int kBytes = kTag + 16;
+};
+
+__device__ __forceinline__ void cpa16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The LOP3 constants of the unpack, held in registers for the whole kernel
+// (asm-defined, so the compiler cannot re-materialise them at every use).
+struct UnpackK {
+  uint32_t lo, hi;  // 0x6408 / 0x6480 per half: the fp16 1024 exponent with the n ^ 8 bias bit
+  __device__ __forceinline__ UnpackK() {
+    asm volatile("mov.b32 %0, 0x64086408;" : "=r"(lo));
+    asm volatile("mov.b32 %0, 0x64806480;" : "=r"(hi));
+  }
+};
+
+// Biased row sums of one 128-K chunk for rows g and g + 8 of a 16-row tile
+// (see gemv_batch.cu): returns E + O / 16 per row.
+__device__ __forceinline__ void st_chunk_dot(const uint4 wa, const uint4 wb, const uint4 xf[4], const UnpackK& k,
+                                             float& s0, float& s1) {
+  const uint32_t r0[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t r1[4] = {wb.x, wb.y, wb.z, wb.w};
+  float e[4] = {0.f, 0.f, 0.f, 0.f}, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t t0 = r0[j] >> 8, t1 = r1[j] >> 8;
+    const uint32_t ae[4] = {lop3_and_xor(r0[j], 0x000f000fu, k.lo), lop3_and_xor(r1[j], 0x000f000fu, k.lo),
+                            lop3_and_xor(t0, 0x000f000fu, k.lo), lop3_and_xor(t1, 0x000f000fu, k.lo)};
+    mma_16816(e, ae, xf[j].x, xf[j].z);
+    const uint32_t ao[4] = {lop3_and_xor(r0[j], 0x00f000f0u, k.hi), lop3_and_xor(r1[j], 0x00f000f0u, k.hi),
+                            lop3_and_xor(t0, 0x00f000f0u, k.hi), lop3_and_xor(t1, 0x00f000f0u, k.hi)};
+    mma_16816(o, ao, xf[j].y, xf[j].w);
+  }
+  s0 = fmaf(o[0], 0.0625f, e[0]);
+  s1 = fmaf(o[2], 0.0625f, e[2]);
+}
+
+// The chunk's bias 1032 XL + 72 XH (gemv_batch.cu chunk_bias) from this
+// lane's 8 bytes of the chunk's x (bytes 8 * lane .. 8 * lane + 7).
+__device__ __forceinline__ float st_chunk_bias(uint2 xw) {
+  const uint32_t a[4] = {0x64086408u, 0x64086408u, 0x54805480u, 0x54805480u};  // 1032 1032 | 72 72
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  mma_16816(d, a, xw.x, xw.y);
+  float bias = d[0] + d[1];
+  bias += __shfl_xor_sync(0xffffffffu, bias, 1);
+  bias += __shfl_xor_sync(0xffffffffu, bias, 2);
+  return bias;
+}
+
+// Fetch cursor: the unit being fetched and this lane's source pointers at
+// the current chunk (set once per unit, advanced by adds per chunk).
+template <int T>
+struct Cursor {
+  static constexpr int kSP = (16 * T + 31) / 32;  // scale rows per lane
+  const uint8_t* wp[2 * T];  // 16 B of row row0 + g + 8r (clamped to N - 1) at the chunk
+  const float* sp[kSP];      // scale of row row0 + lane + 32i (clamped) at the chunk's group
+  const half* xp;            // 8 B of x at the chunk
+  int task, row0, chunk, nch, sub, cpg, nt;
+  bool done;
+};
+
+template <int T, class P>
+__device__ __forceinline__ void st_resolve(const P& B, int u, int lane, Cursor<T>& c) {
+  if (u >= B.total_units) {
+    c.done = true;
+    return;
+  }
+  int lo = 0, hi = B.num - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (B.tasks[mid].ubegin <= u) lo = mid;
+    else hi = mid - 1;
+  }
+  const auto& tk = B.tasks[lo];
+  c.task = lo;
+  c.nt = tk.nt;
+  c.row0 = (u - tk.ubegin) * (16 * tk.nt);
+  c.chunk = 0;
+  c.nch = tk.K >> 7;
+  c.sub = 0;
+  c.cpg = tk.cpg;
+  const int64_t rb = tk.K >> 1;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int r = 0; r < 2 * T; ++r) c.wp[r] = tk.W + (int64_t)min(c.row0 + g + 8 * r, tk.N - 1) * rb + t * 16;
+#pragma unroll
+  for (int i = 0; i < Cursor<T>::kSP; ++i) c.sp[i] = tk.S + (int64_t)min(c.row0 + lane + 32 * i, tk.N - 1) * tk.G;
+  c.xp = tk.x + lane * 4;
+}
+
+template <int T, int D, int W, class P>
+__global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_constant__ P B, int* __restrict__ ctr) {
+  using L = StageLayout<T>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  uint8_t* ring = smem + warp * (D * L::kBytes);
+  const uint32_t ring_u32 = smem_u32(ring);
+
+  // The first unit of every warp is fixed (unit = global warp index), so the
+  // launch does not start with every warp contending for the ticket; later
+  // units come from the ticket, offset by the warp count, one grabbed ahead
+  // (lane 0 holds it).
+  int nxt = 0;
+  if (lane == 0) nxt = B.total_warps + atomicAdd(ctr, 1);
+  Cursor<T> f;
+  f.done = false;
+  st_resolve(B, (int)blockIdx.x * W + warp, lane, f);
+  const UnpackK uk;
+
+  auto fetch = [&](int s) {
+    const uint32_t st = ring_u32 + s * L::kBytes;
+    if (f.done) {
+      if (lane == 0) *reinterpret_cast<int4*>(ring + s * L::kBytes + L::kTag) = make_int4(0, 0, 0, 0);
+      cpa_commit();
+      return;
+    }
+#pragma unroll
+    for (int r = 0; r < 2 * T; ++r)
+      if (r < 2 * f.nt) cpa16(st + L::kW + r * 512 + lane * 16, f.wp[r]);
+    cpa8(st + L::kX + lane * 8 + ((lane >> 4) << 4), f.xp);
+#pragma unroll
+    for (int i = 0; i < Cursor<T>::kSP; ++i)
+      if (lane + 32 * i < 16 * f.nt) cpa4(st + L::kS + (lane + 32 * i) * 4, f.sp[i]);
+    if (lane == 0)
+      *reinterpret_cast<int4*>(ring + s * L::kBytes + L::kTag) =
+          make_int4(f.task, f.row0, f.chunk, (f.nt << 2) | (f.chunk == f.nch - 1 ? 2 : 0) | 1);
+    cpa_commit();
+    // advance the cursor (chunk -> scale group -> next unit)
+    if (++f.chunk == f.nch) {
+      const int u = __shfl_sync(0xffffffffu, nxt, 0);
+      if (lane == 0) nxt = B.total_warps + atomicAdd(ctr, 1);
+      st_resolve(B, u, lane, f);
+    } else {
+#pragma unroll
+      for (int r = 0; r < 2 * T; ++r) f.wp[r] += 64;
+      f.xp += 128;
+      if (++f.sub == f.cpg) {
+        f.sub = 0;
+#pragma unroll
+        for (int i = 0; i < Cursor<T>::kSP; ++i) ++f.sp[i];
+      }
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < D; ++s) fetch(s);
+
+  float acc[2 * T];
+#pragma unroll
+  for (int r = 0; r < 2 * T; ++r) acc[r] = 0.f;
+  const int xoff = L::kX + t * 64 + ((t >> 1) << 4);
+  const int boff = L::kX + lane * 8 + ((lane >> 4) << 4);
+  int s = 0;
+  while (true) {
+    cpa_wait<D - 1>();
+    __syncwarp();
+    const uint8_t* stg = ring + s * L::kBytes;
+    const int4 tag = *reinterpret_cast<const int4*>(stg + L::kTag);
+    if (!(tag.w & 1)) break;
+    const int nt = tag.w >> 2;  // tiles in this unit (1..T)
+    uint4 w[2 * T];
+#pragma unroll
+    for (int r = 0; r < 2 * T; ++r)
+      if (r < 2 * nt) w[r] = *reinterpret_cast<const uint4*>(stg + L::kW + r * 512 + lane * 16);
+    uint4 xf[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xf[j] = *reinterpret_cast<const uint4*>(stg + xoff + j * 16);
+    const uint2 xb = *reinterpret_cast<const uint2*>(stg + boff);
+    float sc[2 * T];
+#pragma unroll
+    for (int r = 0; r < 2 * T; ++r)
+      if (r < 2 * nt) sc[r] = reinterpret_cast<const float*>(stg + L::kS)[g + 8 * r];
+    __syncwarp();  // every lane has read the stage: refill it with the chunk D ahead
+    fetch(s);
+    const float bias = st_chunk_bias(xb);
+#pragma unroll
+    for (int tt = 0; tt < T; ++tt) {
+      if (tt >= nt) break;
+      float d0, d1;
+      st_chunk_dot(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
+      acc[2 * tt] = fmaf(sc[2 * tt], d0 - bias, acc[2 * tt]);
+      acc[2 * tt + 1] = fmaf(sc[2 * tt + 1], d1 - bias, acc[2 * tt + 1]);
+    }
+    if (tag.w & 2) {  // last chunk of the unit: rows g + 8r of the unit
+      const auto& tk = B.tasks[tag.x];
+      if (t == 0) {
+#pragma unroll
+        for (int r = 0; r < 2 * T; ++r) {
+          const int row = tag.y + g + 8 * r;
+          if (r < 2 * nt && row < tk.N) tk.y[row] = __float2half_rn(acc[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2 * T; ++r) acc[r] = 0.f;
+    }
+    s = (s + 1 == D) ? 0 : s + 1;
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  // the last warp out resets the ticket and the exit count for the next launch
+  if (lane == 0) {
+    __threadfence();
+    const int done = atomicAdd(ctr + 1, 1);
+    if (done == B.total_warps - 1) {
+      atomicExch(ctr, 0);
+      atomicExch(ctr + 1, 0);
+    }
+  }
+}
+
+template <int T, int D, int W, class P>
+cudaError_t launch_stream_params(const P& B, int* ctr, cudaStream_t stream) {
+  auto kernel = gemv_stream_kernel<T, D, W, P>;
+  const int smem = W * D * StageLayout<T>::kBytes;
+  if (cudaError_t e = ensure_smem_attr<gemv_stream_kernel<T, D, W, P>>(smem); e != cudaSuccess) return e;
+  kernel<<<B.grid, W * 32, smem, stream>>>(B, ctr);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int64_t gemv_stream_workspace_bytes() { return 256; }
+
+bool plan_gemv_stream(GemvStreamParams& B, int sms) {
+  return plan_stream_units(B, sms, kStreamTiles, kStreamWarps, 125, 100);
+}
+
+bool plan_stream_units(GemvStreamParams& B, int sms, int max_tiles, int warps_per_cta, int tail1_pct, int tail2_pct) {
+  if (B.num < 1 || B.num > kMaxBatchTasks) return false;
+  // bigger units first: stable order by decreasing K
+  GemvStreamTask sorted[kMaxBatchTasks];
+  int n = 0;
+  for (int pass_k = 1 << 30; n < B.num;) {
+    int next_k = 0;
+    for (int i = 0; i < B.num; ++i) {
+      const int k = B.tasks[i].K;
+      if (k == pass_k) sorted[n++] = B.tasks[i];
+      else if (k < pass_k && k > next_k) next_k = k;
+    }
+    pass_k = next_k;
+    if (next_k == 0 && n < B.num) return false;
+  }
+  // Units of max_tiles tiles, except at the end of the order, where the
+  // launch's tail is decided: the last ~1.25 units per warp are single tiles
+  // and the ~1 per warp before them pairs of tiles, so the warps finish
+  // close together.
+  const int64_t warps = (int64_t)sms * warps_per_cta;
+  int64_t tail1 = warps * tail1_pct / 100, tail2 = warps * tail2_pct / 100;
+  for (int i = B.num - 1; i >= 0; --i) {
+    GemvStreamTask& tk = sorted[i];
+    if (tk.K % 128 != 0 || tk.cpg < 1 || tk.N < 1) return false;
+    const int64_t tiles = (tk.N + 15) / 16;
+    if (tail1 > 0) {
+      tk.nt = 1;
+      tail1 -= tiles;
+    } else if (tail2 > 0 && max_tiles > 2) {
+      tk.nt = 2;
+      tail2 -= (tiles + 1) / 2;
+    } else {
+      tk.nt = max_tiles;
+    }
+  }
+  int64_t u = 0;
+  for (int i = 0; i < B.num; ++i) {
+    GemvStreamTask& tk = sorted[i];
+    tk.ubegin = (int)u;
+    u += (tk.N + 16 * tk.nt - 1) / (16 * tk.nt);
+  }
+  if (u >= (1 << 30)) return false;
+  for (int i = 0; i < B.num; ++i) B.tasks[i] = sorted[i];
+  B.total_units = (int)u;
+  B.grid = sms;
+  B.total_warps = (int)warps;
+  return true;
+}
+
+cudaError_t launch_gemv_stream(const GemvStreamParams& B, int* ctr, cudaStream_t stream) {
+  if (B.num <= kSmallBatchTasks) {
+    static GemvStreamParamsT<kSmallBatchTasks> S;  // callers serialise launches
+    S.num = B.num;
+    S.grid = B.grid;
+    S.total_units = B.total_units;
+    S.total_warps = B.total_warps;
+    for (int i = 0; i < B.num; ++i) S.tasks[i] = B.tasks[i];
+    return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps>(S, ctr, stream);
+  }
+  return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps>(B, ctr, stream);
+}
+
+}  // namespace soinfer

@@ -123,6 +123,45 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms);
 cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream);
 cudaError_t read_and_clear_gemv_batch_error(int* out);
 
+// Streaming INT4 GEMV over independent tasks (gemv_stream.cu): no task reads
+// another task's output, no epilogue, K and group size multiples of 128.
+struct GemvStreamTask {
+  const uint8_t* W;
+  const float* S;
+  const half* x;
+  half* y;
+  int N, K, G, cpg;
+  int ubegin;  // filled by plan_gemv_stream: first unit of the task
+  int nt;      // filled by plan_gemv_stream: 16-row tiles per unit of the task
+};
+template <int MaxTasks>
+struct GemvStreamParamsT {
+  int num, grid, total_units, total_warps;
+  GemvStreamTask tasks[MaxTasks];
+};
+using GemvStreamParams = GemvStreamParamsT<kMaxBatchTasks>;
+#ifndef SOINFER_STREAM_TILES
+#define SOINFER_STREAM_TILES 3
+#endif
+#ifndef SOINFER_STREAM_STAGES
+#define SOINFER_STREAM_STAGES 2
+#endif
+#ifndef SOINFER_STREAM_WARPS
+#define SOINFER_STREAM_WARPS 16
+#endif
+constexpr int kStreamTiles = SOINFER_STREAM_TILES;    // 16-row tiles per unit
+constexpr int kStreamStages = SOINFER_STREAM_STAGES;  // chunks in flight per warp
+constexpr int kStreamWarps = SOINFER_STREAM_WARPS;    // warps per CTA (one CTA per SM)
+// Zeroed workspace bytes (a unit ticket and an exit count; left zeroed on return).
+int64_t gemv_stream_workspace_bytes();
+// Orders the tasks (decreasing K) and fills the unit offsets; false if the shape is not served.
+bool plan_gemv_stream(GemvStreamParams& B, int sms);
+// The same for a kernel instance of max_tiles tiles per unit and warps_per_cta
+// warps; the last tail1_pct / 100 units per warp are single tiles, the
+// tail2_pct / 100 before them pairs.
+bool plan_stream_units(GemvStreamParams& B, int sms, int max_tiles, int warps_per_cta, int tail1_pct, int tail2_pct);
+cudaError_t launch_gemv_stream(const GemvStreamParams& B, int* ctr, cudaStream_t stream);
+
 // INT8 GEMV (per-tensor / per-channel / grouped scales).
 cudaError_t launch_gemv_w8(const int8_t* Wq, const float* scale, const half* x, half* y, int64_t N,
                            int64_t K, int64_t group_size, int64_t num_groups, int64_t scale_row_stride,

@@ -76,6 +76,7 @@ _SIGNATURES = {
     "soinfer_peer_buffer_open": (_INT, [_P, _P]),
     "soinfer_peer_buffer_close": (_INT, [_P]),
     "soinfer_peer_buffer_destroy": (_INT, [_P]),
+    "soinfer_peer_buffer_reset": (_INT, [_P, _P]),
     "soinfer_tp_allreduce_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _F32, _P]),
     "soinfer_gemv_w4a16_tp_partial": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_batch_tp": (_INT, [_P, _P, _I64, _P, _I64, _P]),
@@ -122,10 +123,18 @@ def last_error() -> str:
 
 
 def device_errors() -> int:
-    """Reads and clears the device-side error bits (bit 0: a bounded copy wait
-    timed out; bit 1: a peer-exchange wait timed out -- a rank never signalled)."""
+    """Reads and clears the device-side error bits (bit 0: a bounded copy or
+    dependency wait timed out; bit 1: a peer-exchange wait timed out -- a rank
+    never signalled).  When any bit is set, a kernel that gave up may have
+    left its self-resetting counters dirty, so every cached workspace is
+    re-zeroed before this returns (the next launch starts clean).  A peer
+    timeout also needs PeerExchange.reset() on every rank."""
     flags = ctypes.c_int(0)
     _call("soinfer_device_errors", ctypes.byref(flags))
+    if flags.value:
+        torch.cuda.synchronize()
+        reset_workspaces()
+        torch.cuda.synchronize()
     return flags.value
 
 
@@ -362,9 +371,10 @@ def gemv_w4a16_batch(tasks, peers=None) -> None:
 
 def reset_workspaces() -> None:
     """Re-zero every cached workspace (needed after a device error left a
-    kernel's self-resetting counters dirty)."""
+    kernel's self-resetting counters dirty; device_errors() calls it)."""
     for ws in _workspaces.values():
-        ws.zero_()
+        with torch.cuda.device(ws.device):
+            ws.zero_()
 
 
 def gemv_w4a16_rows(Wq_packed, scale, rows, x, K: int, group_size: int, out: torch.Tensor | None = None,
@@ -958,6 +968,12 @@ def peer_buffer_close(ptr: int, device) -> None:
 def peer_buffer_destroy(ptr: int, device) -> None:
     with torch.cuda.device(device):
         _call("soinfer_peer_buffer_destroy", ptr)
+
+
+def peer_buffer_reset(ptr: int, device) -> None:
+    """Zeroes this rank's exchange header on the current stream (recovery after a peer timeout)."""
+    with torch.cuda.device(device):
+        _call("soinfer_peer_buffer_reset", ptr, _stream(torch.device(device)))
 
 
 def tp_allreduce_add_rmsnorm(peers: PeerSetStruct, partial, residual, weight, out_sum, out_norm, eps: float,

@@ -41,6 +41,42 @@ def test_independent_tasks_match_oracle(shapes):
         assert_close(t[3], refs[i], f"batch task {i} {shapes[i]}")
 
 
+def test_large_independent_batch_takes_the_stream_kernel():
+    """A batch of plain, independent GEMVs large enough for the streaming
+    kernel (gemv_stream.cu: one warp per 32-row unit over the full K, units
+    handed out by a ticket): 40 tasks over four matrices -- the configs[0]
+    gate and down shapes, a ragged N and a group size of 256 -- every task
+    against the single-GEMV op, three of them against the float64 oracle, and
+    two launches bit-identical (the ticket resets itself)."""
+    shapes = [(6144, 2048, 128), (2048, 6144, 128), (6000, 2048, 128), (4000, 4096, 256)]
+    mats = [int4_weights(n, k, g, seed=80 + i) for i, (n, k, g) in enumerate(shapes)]
+    dmats = [(p.to(DEV), s.to(DEV)) for p, s, _ in mats]
+    tasks, xs = [], []
+    for i in range(40):
+        m = i % 4
+        n, k, g = shapes[m]
+        x = fp16_randn(k, 90 + i)
+        xs.append(x)
+        tasks.append((dmats[m][0], dmats[m][1], x.to(DEV), torch.empty(n, dtype=torch.float16, device=DEV), k, g, -1))
+    batch = _C.GemvBatch(tasks)
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    first = [t[3].clone() for t in tasks]
+    for t in tasks:
+        t[3].fill_(0)
+    batch.run()
+    torch.cuda.synchronize()
+    for i, t in enumerate(tasks):
+        assert torch.equal(t[3], first[i]), f"task {i}: second launch differs"
+        single = ops.gemv_w4a16_group_lop3(t[0], t[1], t[2], t[4], t[5])
+        assert_close(t[3], single.float().cpu().numpy(), f"stream task {i} vs single GEMV")
+    for i in (0, 1, 2, 3):
+        p, s, pk = mats[i % 4]
+        ref = port.gemv_w4a16(p.numpy(), s.numpy(), xs[i].numpy(), pk, shapes[i % 4][2])
+        assert_close(tasks[i][3], ref, f"stream task {i} vs oracle")
+
+
 def test_mixed_item_sizes_share_the_ring():
     """One CTA's item stream mixes large and small items in an irregular
     order, so the ring's wrap point moves from lap to lap: every task still
@@ -220,3 +256,36 @@ def test_norm_prologue_matches_rmsnorm_then_gemv(k):
     hn = port.rmsnorm(x.numpy()[None], w.numpy(), eps)[0]
     assert_close(y, port.gemv_w4a16(p.numpy(), s.numpy(), hn, pk, 128), f"norm prologue K={k}", max_abs=None)
     assert_close(y, ref_sep.double(), f"norm prologue vs rmsnorm op K={k}", max_abs=None)
+
+
+def test_batch_after_a_timed_out_dependency_matches_oracle():
+    """Failure detection without a fault: the batch workspace's completion
+    counter of task 0 is set far below zero, so task 1's dependency wait can
+    never be satisfied -- it gives up after its bound (1 s), sets the error
+    bit and exits, leaving the counters dirty.  device_errors() reports the
+    bit and re-zeroes the cached workspaces, and the same batch then matches
+    the oracle."""
+    p0, s0, k0 = int4_weights(6144, 2048, 128, seed=31)
+    p1, s1, k1 = int4_weights(2048, 6144, 128, seed=32)
+    x = fp16_randn(k0, 33)
+    y0 = torch.empty(6144, dtype=torch.float16, device=DEV)
+    y1 = torch.empty(2048, dtype=torch.float16, device=DEV)
+    batch = _C.GemvBatch([(p0.to(DEV), s0.to(DEV), x.to(DEV), y0, k0, 128, -1),
+                          (p1.to(DEV), s1.to(DEV), y0, y1, k1, 128, 0)])
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    ws = _C._workspace("batch", torch.device(DEV, torch.cuda.current_device()),
+                       _C.lib().soinfer_gemv_batch_workspace_bytes(2))
+    ws[:4].view(torch.int32).fill_(-(1 << 30))  # a completion count nothing can raise to the grid size
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() & 1, "the timed-out dependency wait did not report"
+    y0.zero_(), y1.zero_()
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    r0 = port.gemv_w4a16(p0.numpy(), s0.numpy(), x.numpy(), k0, 128)
+    assert_close(y0, r0, "task 0 after recovery")
+    r1 = port.gemv_w4a16(p1.numpy(), s1.numpy(), y0.cpu().numpy(), k1, 128)
+    assert_close(y1, r1, "task 1 after recovery")
