@@ -3,16 +3,19 @@
 metric: INT4 g128 GEMV HBM throughput (GB/s, % of measured HBM peak).
 
 Workload (configs[0] shapes, run on the GPU): per layer copy one gate_proj
-GEMV [6144 x 2048] and one down_proj GEMV [2048 x 6144]; one step = one pass
-over LAYERS distinct layer copies (default 64 -> 128 GEMVs over 858 MB of
-packed weights, far above the 126 MB L2, so no L2 flush is needed), issued as
-ONE persistent batched launch (soinfer_gemv_w4a16_batch).  Weights ~N(0, 0.02)
+GEMV [6144 x 2048] and one down_proj GEMV [2048 x 6144]; one launch = one
+pass over LAYERS distinct layer copies (default 64 -> 128 GEMVs over 858 MB of
+packed weights, far above the 126 MB L2, so no L2 flush is needed) through
+soinfer_gemv_w4a16_batch (independent GEMVs: the streaming kernel,
+gemv_stream.cu); one step = LAUNCHES_PER_STEP (16) such launches back to back,
+so that the default 20 timed steps span ~50 ms.  Weights ~N(0, 0.02)
 quantized to group-128 INT4 on the GPU with soinfer.quant; x ~N(0, 1) fp16;
 seeded.  `value` = algorithmic bytes (packed weights + fp32 scales + x + y
 per GEMV, 6,701,056 B) of all ranks / max rank time, timed with CUDA events.
-The GEMVs of a step are independent (every x is ready); the same stream with
-each down_proj reading its gate_proj output (a dependency inside the launch)
-is reported as config.chained_gate_down.
+The GEMVs of a launch are independent (every x is ready); the same stream
+with each down_proj reading its gate_proj output (a dependency inside the
+launch: the persistent batched kernel, gemv_batch.cu) is reported as
+config.chained_gate_down.
 
 `e2e`: the same chain through the public streaming API (WeightPipeline: packed
 weights streamed from the pinned host arena by the copy engine, double
@@ -41,6 +44,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 H, I, G = 2048, 6144, 128
+LAUNCHES_PER_STEP = 16
 METRIC = "INT4 g128 GEMV HBM GB/s"
 UNIT = "GB/s"
 
@@ -167,30 +171,143 @@ def cpu_gemv_sample(seconds: float, threads: int):
     return gbs, desc, n_gemv
 
 
+def op_suite(ops, formats, pack, device, iters: int = 200) -> dict:
+    """Per-call latency of the hot-path ops at the BASELINE config shapes,
+    through the given `ops` module with the same names and arguments -- this
+    build's soinfer.ops, or the reference's own (its extension compiled for
+    sm_100a, baseline/_ref) in the reference arm.  Inputs come from the
+    module's own quantizer (bit-exact between the two), seeded identically.
+    Each figure: mean of `iters` back-to-back calls on the current stream
+    after 20 warm-up calls, CUDA events; the weights of one call fit in L2, as
+    in decode."""
+    gen = torch.Generator().manual_seed(0)
+    cfg = formats.QuantConfig(bits=4, granularity="group", group_size=G)
+
+    def q4(n, k):
+        qt = formats.quantize(torch.randn(n, k, generator=gen) * 0.02, cfg)
+        p, _ = pack.pack_int4(qt.qweight)
+        return p.contiguous().to(device), qt.scale.contiguous().to(device)
+
+    def timed(fn):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize(device)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize(device)
+        return s.elapsed_time(e) * 1e3 / iters
+
+    out = {}
+
+    def rec(name, us, nbytes):
+        out[name] = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1)}
+
+    for n, k in ((I, H), (H, I)):
+        W, S = q4(n, k)
+        x = torch.randn(k, generator=gen).half().to(device)
+        rec(f"gemv_int4_{n}x{k}", timed(lambda: ops.gemv_w4a16_group_lop3(W, S, x, k, G)), gemv_bytes(n, k))
+    for n in (I, 17408):
+        a = torch.randn(n, generator=gen).abs().to(device)
+        rec(f"topk_{n}_k{n // 2}", timed(lambda: ops.topk_threshold_select(a, n // 2)), n * 4 + (n // 2) * 4)
+    k_sel = I // 2
+    WT, ST = q4(I, H)  # down_proj_T rows
+    idx = torch.sort(torch.randperm(I, generator=gen)[:k_sel]).values
+    Wsel, Ssel = WT[idx.to(device)].contiguous(), ST[idx.to(device)].contiguous()
+    h = torch.randn(k_sel, generator=gen).half().to(device)
+    sel_bytes = k_sel * (H // 2 + (H // G) * 4) + 2 * k_sel + 2 * H
+    rec(f"sparse_accumulate_{k_sel}x{H}", timed(lambda: ops.gemv_w4a16_sparse_accumulate(Wsel, Ssel, h, H, G)),
+        sel_bytes)
+    hot = torch.arange(0, I, 5)  # a 20% hot set
+    slot_of = torch.full((I,), -1, dtype=torch.int32)
+    slot_of[hot] = torch.arange(hot.numel(), dtype=torch.int32)
+    idx32 = idx.to(torch.int32).to(device)
+    desc, miss, mc = ops.build_dip_descriptors(idx32, slot_of.to(device))
+    miss = miss[: int(mc.item())].long()
+    cW, cS = WT[hot.to(device)].contiguous(), ST[hot.to(device)].contiguous()
+    sW, sS = WT[miss].contiguous(), ST[miss].contiguous()
+    rec(f"fused_down_20pct_{k_sel}x{H}",
+        timed(lambda: ops.gemv_dip_fused_down(cW, cS, sW, sS, desc, h, H, G)), sel_bytes)
+    for nq, ctx in ((16, 2048), (40, 4096)):
+        q = torch.randn(nq, 128, generator=gen).half().to(device)
+        kc = torch.randn(8, ctx, 128, generator=gen).half().to(device)
+        vc = torch.randn(8, ctx, 128, generator=gen).half().to(device)
+        rec(f"decode_attention_{nq}q8kv_ctx{ctx}", timed(lambda: ops.decode_attention(q, kc, vc, ctx)),
+            2 * 8 * ctx * 128 * 2 + 2 * nq * 128 * 2)
+    W8 = torch.randint(-127, 128, (5120, 5120), generator=gen, dtype=torch.int8).to(device)
+    S8 = (torch.rand(5120, 1, generator=gen) * 0.01).to(device)
+    x8 = torch.randn(5120, generator=gen).half().to(device)
+    rec("gemv_int8_5120x5120_per_channel", timed(lambda: ops.gemv_w8a16(W8, S8, x8, 5120)),
+        5120 * 5120 + 5120 * 4 + 4 * 5120)
+    return out
+
+
 def run_reference(args) -> None:
+    """The reference arm: sparse-offload-infer's own CPU path for the
+    headline op -- soinfer.quant.formats.dequantize once outside the timer,
+    then fp32 torch.mv on every host core (the reference tests' oracle,
+    tests/test_m4_kernels.py:157-168) -- from the reference package installed
+    under baseline/_ref, or the oracle's numpy restatement when that install
+    is absent.  Also times the reference's own CUDA ops (its extension built
+    for sm_100a) at the BASELINE shapes on this GPU (config.ref_ops_b200)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    # warmup + K timed steps; one step = 4 GEMVs (two layer copies) of the same workload
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    have_ref = os.path.isfile(os.path.join(ref_root, "soinfer", "quant", "formats.py"))
     per_step = []
-    from oracle import reference_port as port
+    if have_ref:
+        for p in (ROOT, os.path.join(ROOT, "sparse-offload-infer_b200")):
+            while p in sys.path:
+                sys.path.remove(p)
+        sys.path.insert(0, ref_root)
+        import soinfer  # the reference package
+        from soinfer.quant import formats, pack
 
-    rng = np.random.default_rng(0)
-    mats = []
-    for n, k in [(I, H), (H, I), (I, H), (H, I)]:
-        w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
-        q, s = port.quantize_group(w, G)
-        mats.append(port.dequant_int4(port.pack_int4(q), s, k, G))
-    x0 = rng.standard_normal(H).astype(np.float16).astype(np.float32)
+        assert soinfer.__file__.startswith(ref_root), soinfer.__file__
+        torch.set_num_threads(threads)
+        cfg = formats.QuantConfig(bits=4, granularity="group", group_size=G)
+        gen = torch.Generator().manual_seed(0)
+        mats = []
+        for n, k in [(I, H), (H, I), (I, H), (H, I)]:
+            qt = formats.quantize(torch.randn(n, k, generator=gen) * 0.02, cfg)
+            mats.append(formats.dequantize(qt).float().contiguous())
+        x0 = torch.randn(H, generator=gen).half().float()
 
-    def step():
-        x = x0
-        for j in range(0, 4, 2):
-            y = (mats[j] @ x).astype(np.float16).astype(np.float32)
-            x = mats[j + 1] @ y
-        return x
+        def step():
+            x = x0
+            for j in range(0, 4, 2):
+                y = torch.mv(mats[j], x).half().float()
+                x = torch.mv(mats[j + 1], y)
+            return x
 
+        kind = "reference"
+        sample = (f"per step 4 fp32 torch.mv (2x gate {I}x{H} + 2x down {H}x{I}) of weights dequantized by the "
+                  f"reference's soinfer.quant.formats.dequantize outside the timer, {threads} torch threads")
+    else:
+        from oracle import reference_port as port
+
+        rng = np.random.default_rng(0)
+        mats = []
+        for n, k in [(I, H), (H, I), (I, H), (H, I)]:
+            w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float32)
+            q, s_ = port.quantize_group(w, G)
+            mats.append(port.dequant_int4(port.pack_int4(q), s_, k, G))
+        x0 = rng.standard_normal(H).astype(np.float16).astype(np.float32)
+
+        def step():
+            x = x0
+            for j in range(0, 4, 2):
+                y = (mats[j] @ x).astype(np.float16).astype(np.float32)
+                x = mats[j + 1] @ y
+            return x
+
+        kind = "port"
+        sample = (f"per step 4 fp32 matvecs (2x gate {I}x{H} + 2x down {H}x{I}) of pre-dequantized INT4 weights "
+                  f"(oracle restatement; no reference install), numpy BLAS on {threads} threads")
     for _ in range(args.warmup):
         step()
     for _ in range(args.steps):
@@ -199,15 +316,23 @@ def run_reference(args) -> None:
         per_step.append(time.perf_counter() - t0)
     total = sum(per_step)
     value = 4 * args.steps * BYTES_PER_GEMV / total / 1e9
-    sample = (f"per step 4 fp32 matvecs (2x gate {I}x{H} + 2x down {H}x{I}) of pre-dequantized INT4 weights, "
-              f"numpy BLAS on {threads} threads; dequantization outside the timer")
+    ref_ops = None
+    if have_ref and torch.cuda.is_available() and not args.no_ref_ops:
+        try:
+            from soinfer import ops as ref_ops_mod
+
+            ref_ops = op_suite(ref_ops_mod, formats, pack, torch.device("cuda", 0))
+        except Exception as exc:  # the extension could not run here: report why, keep the CPU line
+            ref_ops = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[0]: INT4 g128 GEMV gate_proj 6144x2048 + down_proj 2048x6144 (CPU port)",
-                   "gemvs_per_step": 4, "bytes_per_gemv": BYTES_PER_GEMV, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "config": {"workload": "configs[0]: INT4 g128 GEMV gate_proj 6144x2048 + down_proj 2048x6144 "
+                               "(the reference's CPU torch path)",
+                   "gemvs_per_step": 4, "bytes_per_gemv": BYTES_PER_GEMV, "parallelism": "host cores",
+                   "ref_ops_b200": ref_ops},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -281,10 +406,10 @@ def run_ours(args) -> None:
         err = float(np.abs(got.double().cpu().numpy() - ref).max())
         assert err < 1e-2 * max(1.0, float(np.abs(ref).max())), f"gemv spot check failed: max-abs {err}"
 
-    launches_per_step = 1
-    gemvs_per_step = 2 * L
+    launches_per_step = LAUNCHES_PER_STEP
+    gemvs_per_step = 2 * L * launches_per_step
     bytes_per_step = gemvs_per_step * BYTES_PER_GEMV
-    for _ in range(args.warmup):
+    for _ in range(args.warmup * launches_per_step):
         batch.run()
     torch.cuda.synchronize(device)
 
@@ -296,7 +421,7 @@ def run_ours(args) -> None:
     with sampler:
         cur = torch.cuda.current_stream(device)
         start.record(cur)
-        for _ in range(args.steps):
+        for _ in range(args.steps * launches_per_step):
             batch.run()
         end.record(cur)
         torch.cuda.synchronize(device)
@@ -309,22 +434,22 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
     value = world * args.steps * bytes_per_step / (max_ms / 1e3) / 1e9
-    per_launch_s = (elapsed_ms / 1e3) / args.steps
-    achieved = bytes_per_step / per_launch_s / 1e9
+    per_launch_s = (elapsed_ms / 1e3) / (args.steps * launches_per_step)
+    achieved = 2 * L * BYTES_PER_GEMV / per_launch_s / 1e9
 
     # chained variant (reported, not the headline)
     for _ in range(2):
         chained.run()
     torch.cuda.synchronize(device)
     cs, ce = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    csteps = max(3, args.steps // 4)
+    csteps = max(3, args.steps // 4) * launches_per_step
     cs.record(cur)
     for _ in range(csteps):
         chained.run()
     ce.record(cur)
     torch.cuda.synchronize(device)
     assert _C.device_errors() == 0, "device error flag set by the chained batched GEMV"
-    chained_gbs = csteps * bytes_per_step / (cs.elapsed_time(ce) / 1e3) / 1e9
+    chained_gbs = csteps * 2 * L * BYTES_PER_GEMV / (cs.elapsed_time(ce) / 1e3) / 1e9
 
     gemm_m8 = run_gemm_m8(layers, device) if args.gemm_m8 else None
 
@@ -335,6 +460,12 @@ def run_ours(args) -> None:
     decode_tp = run_decode_tp(args, device, world, rank, dist) if args.tp_decode else None
     decode_int8 = run_decode_int8(args, device) if args.int8_decode and world == 1 else None
     dip_blocks = run_dip_blocks(args, device) if args.dip_blocks and world == 1 else None
+    ops_b200 = None
+    if args.ops and world == 1:
+        from soinfer import ops as our_ops
+        from soinfer.quant import formats, pack
+
+        ops_b200 = op_suite(our_ops, formats, pack, device)
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -356,22 +487,27 @@ def run_ours(args) -> None:
         "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4w-f16a-f32acc", "data": "synthetic",
         "config": {"workload": "configs[0]: INT4 g128 GEMV, gate_proj 6144x2048 + down_proj 2048x6144 per layer "
-                               f"copy, {L} layer copies per step in one persistent batched launch",
-                   "layers": L, "gemvs_per_step": gemvs_per_step, "bytes_per_gemv": BYTES_PER_GEMV,
+                               f"copy, {L} layer copies per launch (one soinfer_gemv_w4a16_batch call), "
+                               f"{launches_per_step} launches per step",
+                   "layers": L, "launches_per_step": launches_per_step, "gemvs_per_step": gemvs_per_step,
+                   "bytes_per_gemv": BYTES_PER_GEMV,
                    "weights_bytes": L * 2 * (I * H // 2),
                    "l2": "inputs larger than L2 (weights far above the 126 MB L2), no flush",
-                   "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "steps": csteps,
-                                         "note": "each down_proj reads its gate_proj output (in-kernel dependency)"},
+                   "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "launches": csteps,
+                                         "note": "each down_proj reads its gate_proj output (in-kernel dependency; "
+                                                 "persistent batched kernel gemv_batch_kernel)"},
                    "gemm_m8": gemm_m8,
                    "decode": decode,
                    "decode_14b_tp": decode_tp,
                    "decode_14b_int8": decode_int8,
                    "dip_blocks": dip_blocks,
+                   "ops_b200": ops_b200,
                    "parallelism": f"{world} independent replicas (no collective)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                     "traffic": profile_traffic("gemv_batch_kernel"),
-                     "kernel": "gemv_batch_kernel (persistent; one launch = 128 INT4 g128 GEMVs)"},
+                     "traffic": profile_traffic("gemv_stream_kernel"),
+                     "kernel": "gemv_stream_kernel (one launch = 128 INT4 g128 GEMVs; achieved = bytes per launch / "
+                               "mean launch time)"},
         "e2e": e2e,
         "gpu_launches": args.steps * launches_per_step,
         "clocks": sampler.summary(),
@@ -482,30 +618,100 @@ def run_e2e(args, layers, device, world, dist) -> dict:
             "path": "soinfer.runtime.generate.WeightPipeline (copy-engine double buffering from the pinned arena)"}
 
 
+def zipf_hot_set(I: int, frac: float, seed: int = 0):
+    """configs[2]'s hot channel set: a Zipf(s=1.1) frequency ranking over a
+    seeded permutation of the I channels, the top round(frac * I) kept by the
+    reference's StaticFrequencyPolicy."""
+    from soinfer.offload.hot_cache import StaticFrequencyPolicy
+
+    rng = np.random.default_rng(seed)
+    freq = np.empty(I, dtype=np.int64)
+    freq[rng.permutation(I)] = (1e9 / np.arange(1, I + 1) ** 1.1).astype(np.int64)
+    return StaticFrequencyPolicy(freq, round(frac * I)).hot_list
+
+
 def run_decode(args, device) -> dict:
     """batch-1 greedy decode of the Qwen3-1.7B-shaped INT4 model
-    (random-init weights resident in HBM), 70 random prompt tokens then
-    args.decode_tokens new tokens, one CUDA graph per token; dense and DIP
-    k/I = 0.5.  tok/s counts the generating replays only (prompt timed apart)."""
+    (random-init weights), 70 random prompt tokens then args.decode_tokens new
+    tokens.  Resident variants, one CUDA graph per token (GraphDecoder): dense,
+    DIP k/I = 0.5, and cache-aware DIP k/I = 0.5 with a 20% Zipf hot cache in
+    HBM and the other up_proj / down_proj_T rows read from the pinned arena by
+    the device (zero-copy over PCIe) -- its tokens must equal DIP's.  Offload
+    variant: streamed dense (every matrix copied from the pinned arena by the
+    copy engine each token, double-buffered: WeightPipeline, eager).  tok/s
+    counts the generating steps only (prompt timed apart)."""
+    import copy
+
+    from soinfer.offload.hot_cache import HotCache
     from soinfer.runtime import generate as gen
     from soinfer.runtime.loader import QWEN3_1_7B, synthetic_streaming_model
 
-    model = synthetic_streaming_model(QWEN3_1_7B, seed=1, resident=True, offload=False, device=device)
-    prompt = torch.randint(0, QWEN3_1_7B.vocab_size, (70,), generator=torch.Generator().manual_seed(0)).tolist()
+    arch = QWEN3_1_7B
+    model = synthetic_streaming_model(arch, seed=1, resident=True, offload=True, include_dip=True, device=device)
+    prompt = torch.randint(0, arch.vocab_size, (70,), generator=torch.Generator().manual_seed(0)).tolist()
+    n_new = args.decode_tokens
+    peak = pcie_h2d_peak(device)
     out = {"model": "Qwen3-1.7B-shaped: 28 layers, hidden 2048, intermediate 6144, 16 q / 8 kv heads, head_dim 128, "
-                    "vocab 151936; INT4 g128 random-init weights resident in HBM",
-           "prompt_tokens": len(prompt), "new_tokens": args.decode_tokens, "max_seq_len": 2048,
-           "step": "one CUDA graph per token (soinfer.runtime.generate.GraphDecoder)"}
+                    "vocab 151936; INT4 g128 random-init weights",
+           "prompt_tokens": len(prompt), "new_tokens": n_new, "max_seq_len": 2048,
+           "step": "one CUDA graph per token (soinfer.runtime.generate.GraphDecoder)",
+           "pcie_h2d_peak_gbs": round(peak, 2)}
+    toks = {}
     for name, dip_k in (("dense", None), ("dip_k3072", 3072)):
         gd = gen.GraphDecoder(model, dip_k=dip_k, max_seq_len=2048)
         gd.generate(prompt, 4)  # capture + warm-up
         tm = {}
-        gd.generate(prompt, args.decode_tokens, timings=tm)
-        n = args.decode_tokens - 1
+        toks[name] = gd.generate(prompt, n_new, timings=tm)
+        n = n_new - 1
         out[name] = {"tok_s": round(n / (tm["decode_ms"] / 1e3), 1), "ms_per_token": round(tm["decode_ms"] / n, 4),
                      "prefill_ms": round(tm["prefill_ms"], 2)}
         del gd
-    del model
+    # cache-aware DIP: 20% hot cache resident, misses from the pinned arena
+    hot = zipf_hot_set(arch.intermediate_size, 0.2)
+    caches = [HotCache.build(model, li, hot) for li in range(arch.num_layers)]
+    host = copy.copy(model)
+    host.resident = {n_: t for n_, t in model.resident.items()
+                     if not (n_.endswith("mlp.up_proj.weight") or n_.endswith(gen.DOWN_PROJ_T_SUFFIX))}
+    gd = gen.GraphDecoder(host, dip_k=3072, max_seq_len=2048, caches=caches)
+    gd.generate(prompt, 4)
+    tm = {}
+    ids = gd.generate(prompt, n_new, timings=tm)
+    misses = gd.miss_counts.sum().item()  # over every replay of this generate (prompt + new tokens)
+    steps = len(prompt) + n_new - 1
+    h2d_per_token = misses / steps * gen.miss_row_bytes(host)
+    n = n_new - 1
+    ms_tok = tm["decode_ms"] / n
+    out["cached_dip_k3072"] = {
+        "tok_s": round(n / (tm["decode_ms"] / 1e3), 1), "ms_per_token": round(ms_tok, 4),
+        "prefill_ms": round(tm["prefill_ms"], 2), "hot_channels": len(hot),
+        "tokens_equal_dip": ids == toks["dip_k3072"],
+        "h2d_bytes_per_token": int(h2d_per_token), "h2d_gbs": round(h2d_per_token / (ms_tok / 1e3) / 1e9, 2),
+        "h2d_frac_of_peak": round(h2d_per_token / (ms_tok / 1e3) / 1e9 / peak, 4),
+        "note": "one CUDA graph per token: descriptors, miss gather (zero-copy from the pinned arena, count read on "
+                "the device) and fused cache-or-stream GEMVs; 20% Zipf(1.1) hot set"}
+    assert ids == toks["dip_k3072"], "cache-aware DIP tokens differ from DIP's"
+    del gd, caches, host
+    # offload-streamed dense: every matrix from the pinned arena each token
+    streamed = copy.copy(model)
+    streamed.resident = {}
+    ns = min(n_new, 24)
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ids_s = gen.generate_streaming(streamed, prompt[:8], 2, max_seq_len=64)  # warm-up
+    s_.record()
+    ids_s = gen.generate_streaming(streamed, prompt[:1], ns, max_seq_len=64)
+    e_.record()
+    torch.cuda.synchronize(device)
+    wbytes = sum(m.n * m.handle.row_nbytes for nm, m in model.matrices.items()
+                 if not nm.endswith(gen.DOWN_PROJ_T_SUFFIX))
+    ms_tok = s_.elapsed_time(e_) / (ns + 1)  # 1 prompt step + ns generating steps
+    out["streamed_dense"] = {"tok_s": round(1e3 / ms_tok, 1), "ms_per_token": round(ms_tok, 3),
+                             "tokens": ns, "h2d_bytes_per_token": int(wbytes),
+                             "h2d_gbs": round(wbytes / (ms_tok / 1e3) / 1e9, 2),
+                             "h2d_frac_of_peak": round(wbytes / (ms_tok / 1e3) / 1e9 / peak, 4),
+                             "note": "eager; each matrix copied by the copy engine on a side stream, double "
+                                     "buffered (WeightPipeline); 1-token prompt, timed over every step"}
+    assert ids_s[:1] == prompt[:1]
+    del model, streamed
     torch.cuda.empty_cache()
     return out
 
@@ -587,18 +793,32 @@ def run_decode_tp(args, device, world, rank, dist) -> dict:
                 "sums + residual + RMSNorm (soinfer.runtime.tp.PeerExchange)" if world > 1 else "single GPU")}
 
 
-def pcie_h2d_peak(device, nbytes: int = 256 << 20, reps: int = 5) -> float:
-    """Pinned host -> device copy bandwidth (GB/s), best of `reps`."""
-    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+def pcie_h2d_peak(device, reps: int = 3) -> float:
+    """Pinned host -> device copy bandwidth (GB/s): the best over copy sizes
+    (64 MB, 256 MB, 1 GB) and over 1 or 2 copies in flight on separate
+    streams (each of the two moving half of the bytes), best of `reps`."""
     best = 0.0
-    for _ in range(reps + 1):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        dst.copy_(src, non_blocking=True)
-        e.record()
-        torch.cuda.synchronize(device)
-        best = max(best, nbytes / (s.elapsed_time(e) / 1e3) / 1e9)
+    big = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    streams = [torch.cuda.Stream(device) for _ in range(2)]
+    for nbytes in (64 << 20, 256 << 20, 1 << 30):
+        for ways in (1, 2):
+            part = nbytes // ways
+            for _ in range(reps + 1):
+                torch.cuda.synchronize(device)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                cur = torch.cuda.current_stream(device)
+                s.record(cur)
+                for w in range(ways):
+                    streams[w].wait_stream(cur)
+                    with torch.cuda.stream(streams[w]):
+                        dst[w * part:(w + 1) * part].copy_(big[w * part:(w + 1) * part], non_blocking=True)
+                for w in range(ways):
+                    cur.wait_stream(streams[w])
+                e.record(cur)
+                torch.cuda.synchronize(device)
+                best = max(best, nbytes / (s.elapsed_time(e) / 1e3) / 1e9)
+    del big, dst
     return best
 
 
@@ -610,9 +830,9 @@ def run_dip_blocks(args, device, reps: int = 20) -> dict:
       graph per step; algorithmic bytes per block 13,443,072;
     * cache-aware DIP block: 20% hot cache (Zipf s=1.1 ranking over a seeded
       permutation), the misses' rows streamed from the pinned arena by the
-      device-driven gather (one host read of the miss count per block, as the
-      reference); H2D bytes = misses x (up + down_T row bytes), against the
-      measured pinned H2D peak."""
+      device-driven gather (the miss count stays on the device: one CUDA
+      graph per step); H2D bytes = misses x (up + down_T row bytes), against
+      the measured pinned H2D peak."""
     import copy
 
     from soinfer import ops
@@ -657,42 +877,46 @@ def run_dip_blocks(args, device, reps: int = 20) -> dict:
         e.record(st)
     torch.cuda.synchronize(device)
     dip_ms = s.elapsed_time(e) / reps
-    ref0 = outs[0].clone()
+    ref = [o.clone() for o in outs]
     del graph
     block_bytes = 13_443_072
 
-    # cache-aware DIP: hot rows resident, misses from the pinned arena
-    rng = np.random.default_rng(0)
-    perm = rng.permutation(Ii)
-    freq = np.empty(Ii, dtype=np.int64)
-    freq[perm] = (1e9 / np.arange(1, Ii + 1) ** 1.1).astype(np.int64)
-    hot = StaticFrequencyPolicy(freq, round(0.2 * Ii)).hot_list
+    # cache-aware DIP: hot rows resident, misses from the pinned arena (device-side miss count)
+    hot = zipf_hot_set(Ii, 0.2)
     caches = [HotCache.build(model, li, hot) for li in range(L)]
     host_model = copy.copy(model)  # same matrices; up / down_T rows read from the arena
     host_model.resident = {n: t for n, t in model.resident.items()
                            if not (n.endswith("mlp.up_proj.weight") or n.endswith(gen.DOWN_PROJ_T_SUFFIX))}
-    miss = [0] * L
+    misses = torch.zeros(L, dtype=torch.int64, device=device)
 
-    def cached_step(count):
+    def cached_step():
         for li in range(L):
             gate, idx = gate_and_select(li)
-            outs[li] = gen.cached_dip_mlp_tail(host_model, li, h3[li], gate, idx, bufs, caches[li],
-                                               miss if count else None)
+            outs[li] = gen.cached_dip_mlp_tail(host_model, li, h3[li], gate, idx, bufs, caches[li], misses)
 
-    cached_step(False)
-    torch.cuda.synchronize(device)
-    assert torch.equal(outs[0], ref0), "cache-aware DIP differs from DIP"
-    creps = 5
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(creps):
-        cached_step(True)
-    e.record()
+    creps = 10
+    with torch.cuda.stream(st):
+        cached_step()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            cached_step()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        misses.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(st)
+        for _ in range(creps):
+            graph.replay()
+        e.record(st)
     torch.cuda.synchronize(device)
     cached_ms = s.elapsed_time(e) / creps
-    miss_bytes = sum(miss) / creps
+    identical = all(torch.equal(a, b) for a, b in zip(outs, ref))
+    assert identical, "cache-aware DIP differs from DIP"
+    miss_bytes = int(misses.sum().item()) * gen.miss_row_bytes(host_model) / creps
     peak = pcie_h2d_peak(device)
-    del model, host_model, caches, bufs
+    del graph, model, host_model, caches, bufs
     torch.cuda.empty_cache()
     return {"shapes": "Qwen3-1.7B MLP: H 2048, I 6144, k 3072, INT4 g128; 28 layer copies per step",
             "dip_block": {"us_per_block": round(dip_ms * 1e3 / L, 2),
@@ -704,9 +928,10 @@ def run_dip_blocks(args, device, reps: int = 20) -> dict:
                                  "h2d_gbs": round(miss_bytes / (cached_ms / 1e3) / 1e9, 2),
                                  "pcie_h2d_peak_gbs": round(peak, 2),
                                  "h2d_frac_of_peak": round(miss_bytes / (cached_ms / 1e3) / 1e9 / peak, 4),
-                                 "bit_identical_to_dip": True, "steps": creps,
-                                 "note": "eager (one miss-count read per block); misses gathered over PCIe "
-                                         "from the pinned arena by the device"}}
+                                 "bit_identical_to_dip": identical, "layers_compared": L, "steps": creps,
+                                 "note": "CUDA graph per step (the miss count never leaves the device); misses "
+                                         "gathered zero-copy over PCIe from the pinned arena by one device gather "
+                                         "per block; all 28 block outputs of the last replay equal DIP's"}}
 
 
 def run_decode_int8(args, device) -> dict:
@@ -748,6 +973,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-ops", action="store_true", help="reference arm: skip timing its CUDA ops")
+    ap.add_argument("--ops", type=int, default=1, help="also time this build's hot-path ops (config.ops_b200)")
     ap.add_argument("--decode", type=int, default=1, help="also measure configs[3] decode tok/s (reported in config)")
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")

@@ -313,6 +313,25 @@ int soinfer_gather_rows_naive(const uint8_t* matrix, int64_t num_rows, int64_t r
 int soinfer_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
                                const int32_t* rows, int64_t k, uint8_t* gpu_dst, void* stream);
 
+/* One source of soinfer_gather_rows_device_multi. */
+typedef struct soinfer_gather_src {
+  const uint8_t* matrix; /* [num_rows, row_nbytes]: device or pinned host memory (zero-copy) */
+  int64_t num_rows;
+  int64_t row_nbytes;    /* a positive multiple of 4 */
+  uint8_t* dst;          /* device [max_k, row_nbytes] */
+} soinfer_gather_src;
+
+/* Device-driven gather of the same rows from up to 4 matrices in one launch,
+ * with the row count read from device memory: rows[j] of every source for
+ * j < min(*count, max_k) (count NULL: max_k rows); rows at or past the count
+ * are not touched.  This is the cache-aware DIP miss gather (the missed
+ * channels' up_proj and down_proj_T rows and their scale rows) without the
+ * host ever learning the miss count, so the step can be captured in a CUDA
+ * graph.  Replaces runtime/generate.py:376-388 of the reference (the
+ * miss-count download, then gather_rows_staged per matrix). */
+int soinfer_gather_rows_device_multi(const soinfer_gather_src* srcs, int32_t num_srcs, const int32_t* rows,
+                                     const int32_t* count, int64_t max_k, void* stream);
+
 /* ---------------------------------------------- attention-side glue ------ */
 
 /* out[r, :] = fp16( x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * weight ), fp32 math.

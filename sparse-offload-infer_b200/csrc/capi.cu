@@ -179,7 +179,7 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
     for (int64_t i = 0; i < num_tasks; ++i) {
       const soinfer_gemv_task& t = tasks[i];
       S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.x), as_half(t.y), (int)t.N, (int)t.K,
-                                  (int)t.num_groups, (int)(t.group_size / 128), 0, 0};
+                                  (int)t.num_groups, (int)(t.group_size / 128), 0};
     }
     if (plan_gemv_stream(S, sms)) {
       REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
@@ -554,6 +554,29 @@ int soinfer_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t 
   REQUIRE(num_rows >= 1 && matrix && rows && gpu_dst, "%s: null pointer or empty matrix", name);
   return cuda_result(launch_gather_rows_device(matrix, num_rows, row_nbytes, rows, k, gpu_dst, as_stream(stream)),
                      name);
+}
+
+int soinfer_gather_rows_device_multi(const soinfer_gather_src* srcs, int32_t num_srcs, const int32_t* rows,
+                                     const int32_t* count, int64_t max_k, void* stream) {
+  const char* name = "gather_rows_device_multi";
+  REQUIRE(num_srcs >= 0 && num_srcs <= kMaxGatherSrc, "%s: num_srcs must be in [0, %d]", name, kMaxGatherSrc);
+  REQUIRE(max_k >= 0, "%s: max_k must be >= 0", name);
+  if (num_srcs == 0 || max_k == 0) return SOINFER_OK;
+  REQUIRE(srcs && rows, "%s: null pointer", name);
+  GatherMulti P = {};
+  P.num = num_srcs;
+  P.rows = rows;
+  P.count = count;
+  P.max_k = max_k;
+  for (int i = 0; i < num_srcs; ++i) {
+    const soinfer_gather_src& g = srcs[i];
+    REQUIRE(g.matrix && g.dst && g.num_rows >= 1, "%s: source %d: null pointer or empty matrix", name, i);
+    REQUIRE(g.row_nbytes >= 4 && g.row_nbytes % 4 == 0 && aligned(g.matrix, 4) && aligned(g.dst, 4),
+            "%s: source %d: row_nbytes must be a positive multiple of 4 with 4-byte aligned matrix / dst", name, i);
+    P.src[i] = GatherSrc{g.matrix, g.num_rows, g.row_nbytes, g.dst,
+                         (g.row_nbytes % 16 == 0 && aligned(g.matrix, 16) && aligned(g.dst, 16)) ? 1 : 0};
+  }
+  return cuda_result(launch_gather_multi(P, as_stream(stream)), name);
 }
 
 int soinfer_rmsnorm(const soinfer_half* x, const soinfer_half* weight, soinfer_half* out, int64_t rows, int64_t hidden,

@@ -119,7 +119,7 @@ struct Cursor {
   const uint8_t* wp[2 * T];  // 16 B of row row0 + g + 8r (clamped to N - 1) at the chunk
   const float* sp[kSP];      // scale of row row0 + lane + 32i (clamped) at the chunk's group
   const half* xp;            // 8 B of x at the chunk
-  int task, row0, chunk, nch, sub, cpg, nt;
+  int task, row0, chunk, nch, sub, cpg;
   bool done;
 };
 
@@ -137,8 +137,7 @@ __device__ __forceinline__ void st_resolve(const P& B, int u, int lane, Cursor<T
   }
   const auto& tk = B.tasks[lo];
   c.task = lo;
-  c.nt = tk.nt;
-  c.row0 = (u - tk.ubegin) * (16 * tk.nt);
+  c.row0 = (u - tk.ubegin) * (16 * T);
   c.chunk = 0;
   c.nch = tk.K >> 7;
   c.sub = 0;
@@ -161,15 +160,15 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
   uint8_t* ring = smem + warp * (D * L::kBytes);
   const uint32_t ring_u32 = smem_u32(ring);
 
-  // The first unit of every warp is fixed (unit = global warp index), so the
-  // launch does not start with every warp contending for the ticket; later
-  // units come from the ticket, offset by the warp count, one grabbed ahead
-  // (lane 0 holds it).
-  int nxt = 0;
-  if (lane == 0) nxt = B.total_warps + atomicAdd(ctr, 1);
+  // first unit, and the next one grabbed ahead (lane 0 holds it)
+  int nxt = 0, first = 0;
+  if (lane == 0) {
+    first = atomicAdd(ctr, 1);
+    nxt = atomicAdd(ctr, 1);
+  }
   Cursor<T> f;
   f.done = false;
-  st_resolve(B, (int)blockIdx.x * W + warp, lane, f);
+  st_resolve(B, __shfl_sync(0xffffffffu, first, 0), lane, f);
   const UnpackK uk;
 
   auto fetch = [&](int s) {
@@ -180,20 +179,19 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
       return;
     }
 #pragma unroll
-    for (int r = 0; r < 2 * T; ++r)
-      if (r < 2 * f.nt) cpa16(st + L::kW + r * 512 + lane * 16, f.wp[r]);
+    for (int r = 0; r < 2 * T; ++r) cpa16(st + L::kW + r * 512 + lane * 16, f.wp[r]);
     cpa8(st + L::kX + lane * 8 + ((lane >> 4) << 4), f.xp);
 #pragma unroll
     for (int i = 0; i < Cursor<T>::kSP; ++i)
-      if (lane + 32 * i < 16 * f.nt) cpa4(st + L::kS + (lane + 32 * i) * 4, f.sp[i]);
+      if (lane + 32 * i < L::kRows) cpa4(st + L::kS + (lane + 32 * i) * 4, f.sp[i]);
     if (lane == 0)
       *reinterpret_cast<int4*>(ring + s * L::kBytes + L::kTag) =
-          make_int4(f.task, f.row0, f.chunk, (f.nt << 2) | (f.chunk == f.nch - 1 ? 2 : 0) | 1);
+          make_int4(f.task, f.row0, f.chunk, (f.chunk == f.nch - 1 ? 2 : 0) | 1);
     cpa_commit();
     // advance the cursor (chunk -> scale group -> next unit)
     if (++f.chunk == f.nch) {
       const int u = __shfl_sync(0xffffffffu, nxt, 0);
-      if (lane == 0) nxt = B.total_warps + atomicAdd(ctr, 1);
+      if (lane == 0) nxt = atomicAdd(ctr, 1);
       st_resolve(B, u, lane, f);
     } else {
 #pragma unroll
@@ -222,25 +220,21 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     const uint8_t* stg = ring + s * L::kBytes;
     const int4 tag = *reinterpret_cast<const int4*>(stg + L::kTag);
     if (!(tag.w & 1)) break;
-    const int nt = tag.w >> 2;  // tiles in this unit (1..T)
     uint4 w[2 * T];
 #pragma unroll
-    for (int r = 0; r < 2 * T; ++r)
-      if (r < 2 * nt) w[r] = *reinterpret_cast<const uint4*>(stg + L::kW + r * 512 + lane * 16);
+    for (int r = 0; r < 2 * T; ++r) w[r] = *reinterpret_cast<const uint4*>(stg + L::kW + r * 512 + lane * 16);
     uint4 xf[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) xf[j] = *reinterpret_cast<const uint4*>(stg + xoff + j * 16);
     const uint2 xb = *reinterpret_cast<const uint2*>(stg + boff);
     float sc[2 * T];
 #pragma unroll
-    for (int r = 0; r < 2 * T; ++r)
-      if (r < 2 * nt) sc[r] = reinterpret_cast<const float*>(stg + L::kS)[g + 8 * r];
+    for (int r = 0; r < 2 * T; ++r) sc[r] = reinterpret_cast<const float*>(stg + L::kS)[g + 8 * r];
     __syncwarp();  // every lane has read the stage: refill it with the chunk D ahead
     fetch(s);
     const float bias = st_chunk_bias(xb);
 #pragma unroll
     for (int tt = 0; tt < T; ++tt) {
-      if (tt >= nt) break;
       float d0, d1;
       st_chunk_dot(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
       acc[2 * tt] = fmaf(sc[2 * tt], d0 - bias, acc[2 * tt]);
@@ -252,7 +246,7 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
 #pragma unroll
         for (int r = 0; r < 2 * T; ++r) {
           const int row = tag.y + g + 8 * r;
-          if (r < 2 * nt && row < tk.N) tk.y[row] = __float2half_rn(acc[r]);
+          if (row < tk.N) tk.y[row] = __float2half_rn(acc[r]);
         }
       }
 #pragma unroll
@@ -286,12 +280,10 @@ cudaError_t launch_stream_params(const P& B, int* ctr, cudaStream_t stream) {
 int64_t gemv_stream_workspace_bytes() { return 256; }
 
 bool plan_gemv_stream(GemvStreamParams& B, int sms) {
-  return plan_stream_units(B, sms, kStreamTiles, kStreamWarps, 125, 100);
-}
-
-bool plan_stream_units(GemvStreamParams& B, int sms, int max_tiles, int warps_per_cta, int tail1_pct, int tail2_pct) {
   if (B.num < 1 || B.num > kMaxBatchTasks) return false;
-  // bigger units first: stable order by decreasing K
+  // bigger units first: stable order by decreasing K.  (Measured: smaller
+  // units at the end of the order, to shorten the tail, cost more in
+  // per-unit overhead than they saved.)
   GemvStreamTask sorted[kMaxBatchTasks];
   int n = 0;
   for (int pass_k = 1 << 30; n < B.num;) {
@@ -304,37 +296,18 @@ bool plan_stream_units(GemvStreamParams& B, int sms, int max_tiles, int warps_pe
     pass_k = next_k;
     if (next_k == 0 && n < B.num) return false;
   }
-  // Units of max_tiles tiles, except at the end of the order, where the
-  // launch's tail is decided: the last ~1.25 units per warp are single tiles
-  // and the ~1 per warp before them pairs of tiles, so the warps finish
-  // close together.
-  const int64_t warps = (int64_t)sms * warps_per_cta;
-  int64_t tail1 = warps * tail1_pct / 100, tail2 = warps * tail2_pct / 100;
-  for (int i = B.num - 1; i >= 0; --i) {
-    GemvStreamTask& tk = sorted[i];
-    if (tk.K % 128 != 0 || tk.cpg < 1 || tk.N < 1) return false;
-    const int64_t tiles = (tk.N + 15) / 16;
-    if (tail1 > 0) {
-      tk.nt = 1;
-      tail1 -= tiles;
-    } else if (tail2 > 0 && max_tiles > 2) {
-      tk.nt = 2;
-      tail2 -= (tiles + 1) / 2;
-    } else {
-      tk.nt = max_tiles;
-    }
-  }
   int64_t u = 0;
   for (int i = 0; i < B.num; ++i) {
     GemvStreamTask& tk = sorted[i];
+    if (tk.K % 128 != 0 || tk.cpg < 1 || tk.N < 1) return false;
     tk.ubegin = (int)u;
-    u += (tk.N + 16 * tk.nt - 1) / (16 * tk.nt);
+    u += (tk.N + 16 * kStreamTiles - 1) / (16 * kStreamTiles);
   }
   if (u >= (1 << 30)) return false;
   for (int i = 0; i < B.num; ++i) B.tasks[i] = sorted[i];
   B.total_units = (int)u;
   B.grid = sms;
-  B.total_warps = (int)warps;
+  B.total_warps = sms * kStreamWarps;
   return true;
 }
 

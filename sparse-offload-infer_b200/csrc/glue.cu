@@ -213,7 +213,54 @@ __global__ void gather_rows_kernel(const uint8_t* __restrict__ matrix, const int
   }
 }
 
+// Multi-source gather with the row count in device memory: every thread
+// copies 16-byte pieces (4-byte pieces for a source whose rows are not
+// 16-byte aligned) of rows rows[j], j < min(*count, max_k), of every source;
+// a warp's lanes read consecutive pieces of one row, so each warp load is one
+// contiguous burst (over PCIe when the matrix is pinned host memory).
+__global__ void gather_multi_kernel(const GatherMulti P) {
+  pdl_launch_dependents();
+  pdl_wait();
+  int64_t n = P.max_k;
+  if (P.count != nullptr) {
+    const int64_t c = *P.count;
+    n = c < 0 ? 0 : (c < n ? c : n);
+  }
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+#pragma unroll 1
+  for (int s = 0; s < P.num; ++s) {
+    const GatherSrc& g = P.src[s];
+    const int64_t unit = g.vec16 ? 16 : 4;
+    const int64_t per_row = g.row_nbytes / unit;
+    const int64_t total = P.max_k * per_row;
+    for (int64_t e = tid; e < total; e += stride) {
+      const int64_t j = e / per_row;
+      if (j >= n) break;  // rows are in j order: nothing further in this source
+      const int64_t c = e - j * per_row;
+      int64_t r = P.rows[j];
+      r = r < 0 ? 0 : (r >= g.num_rows ? g.num_rows - 1 : r);
+      if (g.vec16) {
+        const uint4 v = ldg_stream_u4(g.matrix + r * g.row_nbytes + c * 16);
+        *reinterpret_cast<uint4*>(g.dst + j * g.row_nbytes + c * 16) = v;
+      } else {
+        const uint32_t v = ldg_stream_u32(g.matrix + r * g.row_nbytes + c * 4);
+        *reinterpret_cast<uint32_t*>(g.dst + j * g.row_nbytes + c * 4) = v;
+      }
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_gather_multi(const GatherMulti& P, cudaStream_t stream) {
+  int64_t total = 0;
+  for (int s = 0; s < P.num; ++s) total += P.max_k * (P.src[s].row_nbytes / (P.src[s].vec16 ? 16 : 4));
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  return launch_ex(gather_multi_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, 1, kPdl, P);
+}
 
 cudaError_t launch_rmsnorm(const half* x, const half* w, half* out, int64_t rows, int64_t hidden, float eps,
                            cudaStream_t stream) {

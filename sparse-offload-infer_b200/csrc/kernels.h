@@ -132,7 +132,6 @@ struct GemvStreamTask {
   half* y;
   int N, K, G, cpg;
   int ubegin;  // filled by plan_gemv_stream: first unit of the task
-  int nt;      // filled by plan_gemv_stream: 16-row tiles per unit of the task
 };
 template <int MaxTasks>
 struct GemvStreamParamsT {
@@ -156,10 +155,6 @@ constexpr int kStreamWarps = SOINFER_STREAM_WARPS;    // warps per CTA (one CTA 
 int64_t gemv_stream_workspace_bytes();
 // Orders the tasks (decreasing K) and fills the unit offsets; false if the shape is not served.
 bool plan_gemv_stream(GemvStreamParams& B, int sms);
-// The same for a kernel instance of max_tiles tiles per unit and warps_per_cta
-// warps; the last tail1_pct / 100 units per warp are single tiles, the
-// tail2_pct / 100 before them pairs.
-bool plan_stream_units(GemvStreamParams& B, int sms, int max_tiles, int warps_per_cta, int tail1_pct, int tail2_pct);
 cudaError_t launch_gemv_stream(const GemvStreamParams& B, int* ctr, cudaStream_t stream);
 
 // INT8 GEMV (per-tensor / per-channel / grouped scales).
@@ -185,6 +180,23 @@ cudaError_t launch_build_descriptors(const int32_t* sel, int64_t k, const int32_
                                      int32_t* desc, int32_t* miss, int32_t* miss_count, cudaStream_t stream);
 
 // Gathers.
+// Multi-source device gather (glue.cu): rows rows[0 .. min(*count, max_k)) of
+// up to kMaxGatherSrc matrices into their destinations (count NULL: max_k rows).
+constexpr int kMaxGatherSrc = 4;
+struct GatherSrc {
+  const uint8_t* matrix;
+  int64_t num_rows, row_nbytes;
+  uint8_t* dst;
+  int vec16;  // 16-byte pieces (rows, matrix and dst 16-byte aligned) or 4-byte pieces
+};
+struct GatherMulti {
+  GatherSrc src[kMaxGatherSrc];
+  int num;
+  const int32_t* rows;
+  const int32_t* count;
+  int64_t max_k;
+};
+cudaError_t launch_gather_multi(const GatherMulti& P, cudaStream_t stream);
 cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,
                                       const int32_t* rows, int64_t k, uint8_t* dst, cudaStream_t stream);
 

@@ -77,6 +77,7 @@ _SIGNATURES = {
     "soinfer_peer_buffer_close": (_INT, [_P]),
     "soinfer_peer_buffer_destroy": (_INT, [_P]),
     "soinfer_peer_buffer_reset": (_INT, [_P, _P]),
+    "soinfer_gather_rows_device_multi": (_INT, [_P, ctypes.c_int32, _P, _P, _I64, _P]),
     "soinfer_tp_allreduce_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _F32, _P]),
     "soinfer_gemv_w4a16_tp_partial": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_batch_tp": (_INT, [_P, _P, _I64, _P, _I64, _P]),
@@ -682,6 +683,37 @@ def gather_rows_device(matrix, rows, gpu_dst) -> None:
     dev = gpu_dst.device
     with torch.cuda.device(dev):
         _call("soinfer_gather_rows_device", _ptr(matrix), matrix.size(0), rb, _ptr(rows), k, _ptr(gpu_dst),
+              _stream(dev))
+
+
+class _GatherSrc(ctypes.Structure):
+    _fields_ = [("matrix", _P), ("num_rows", _I64), ("row_nbytes", _I64), ("dst", _P)]
+
+
+def gather_rows_device_multi(pairs, rows, count=None, max_k: int | None = None) -> None:
+    """One launch gathering rows[j] of every (matrix, dst) pair for
+    j < min(count[0], max_k) (count: int32 [1] CUDA, read on the device; None:
+    max_k rows).  matrix: 2D uint8 (CUDA or pinned host, read zero-copy) or any
+    contiguous 2D tensor viewed as bytes per row; dst: CUDA, >= max_k rows."""
+    name = "gather_rows_device_multi"
+    _check(1 <= len(pairs) <= 4, name, ": 1 to 4 (matrix, dst) pairs")
+    _check_cuda(rows, name + "(rows)", torch.int32, ": must be int32")
+    max_k = rows.numel() if max_k is None else max_k
+    _check(0 <= max_k <= rows.numel(), name, ": max_k must be in [0, rows.numel()]")
+    if count is not None:
+        _check_cuda(count, name + "(count)", torch.int32, ": must be int32")
+    arr = (_GatherSrc * len(pairs))()
+    dev = rows.device
+    for i, (m, d) in enumerate(pairs):
+        _check(m.dim() == 2 and m.is_contiguous() and (m.is_cuda or m.is_pinned()), name,
+               f"(matrix {i}): must be a contiguous 2D CUDA or pinned host tensor")
+        rb = m.size(1) * m.element_size()
+        _check(d.is_cuda and d.is_contiguous() and d.device == dev, name, f"(dst {i}): must be a contiguous CUDA tensor "
+               "on the rows' device")
+        _check(d.numel() * d.element_size() >= max_k * rb, name, f"(dst {i}): too small for max_k rows")
+        arr[i] = _GatherSrc(m.data_ptr(), m.size(0), rb, d.data_ptr())
+    with torch.cuda.device(dev):
+        _call("soinfer_gather_rows_device_multi", ctypes.addressof(arr), len(pairs), _ptr(rows), _ptr(count), max_k,
               _stream(dev))
 
 

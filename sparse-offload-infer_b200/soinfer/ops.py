@@ -94,6 +94,13 @@ def gather_rows_device(matrix: torch.Tensor, rows: torch.Tensor, gpu_dst: torch.
     _C.gather_rows_device(matrix, rows, gpu_dst)
 
 
+def gather_rows_device_multi(pairs, rows: torch.Tensor, count: torch.Tensor | None = None,
+                             max_k: int | None = None) -> None:
+    """B200 addition: one device-driven gather of rows[j], j < min(count, max_k), from every (matrix, dst)
+    pair; count (int32 [1] CUDA) is read on the device -- no host round trip for the miss count."""
+    _C.gather_rows_device_multi(pairs, rows, count, max_k)
+
+
 def gemv_w4a16_sparse_accumulate(Wq_selected: torch.Tensor, scale_selected: torch.Tensor,
                                  h_selected: torch.Tensor, H: int, group_size: int) -> torch.Tensor:
     """Sparse 'down' GEMV: y[H] = sum_i h_selected[i] * dequant(W_T[i, :]) over k gathered rows of the

@@ -335,22 +335,28 @@ def run_decoder_layer_streaming(pipeline: WeightPipeline, model: StreamingModel,
 @dataclass
 class DipBuffers:
     """Device rows for the selected (DIP) or missed (cached DIP) up_proj /
-    down_proj_T rows, allocated once for the largest k (reference
-    generate.py:185-212; no pinned staging: the gather is device-driven)."""
+    down_proj_T rows and their scale rows, allocated once for the largest k
+    (reference generate.py:185-212; no pinned staging: the gather is
+    device-driven)."""
 
     gpu_up: torch.Tensor     # CUDA uint8 [max_k * up_row_nbytes]
     gpu_down: torch.Tensor   # CUDA uint8 [max_k * downT_row_nbytes]
     up_row_nbytes: int
     down_row_nbytes: int
+    gpu_up_scale: torch.Tensor | None = None    # CUDA fp32 [max_k, up groups]
+    gpu_down_scale: torch.Tensor | None = None  # CUDA fp32 [max_k, downT groups]
 
     @staticmethod
     def make(model: StreamingModel, max_k: int) -> "DipBuffers":
-        up_rb = model.matrix(0, "mlp.up_proj.weight").handle.row_nbytes
-        down_rb = model.matrix(0, DOWN_PROJ_T_SUFFIX).handle.row_nbytes
+        up = model.matrix(0, "mlp.up_proj.weight")
+        down_t = model.matrix(0, DOWN_PROJ_T_SUFFIX)
+        up_rb, down_rb = up.handle.row_nbytes, down_t.handle.row_nbytes
         dev = model.device
         return DipBuffers(gpu_up=torch.empty(max_k * up_rb, dtype=torch.uint8, device=dev),
                           gpu_down=torch.empty(max_k * down_rb, dtype=torch.uint8, device=dev),
-                          up_row_nbytes=up_rb, down_row_nbytes=down_rb)
+                          up_row_nbytes=up_rb, down_row_nbytes=down_rb,
+                          gpu_up_scale=torch.empty(max_k, up.scale.size(1), dtype=torch.float32, device=dev),
+                          gpu_down_scale=torch.empty(max_k, down_t.scale.size(1), dtype=torch.float32, device=dev))
 
     def up_rows(self, k: int) -> torch.Tensor:
         return self.gpu_up[: k * self.up_row_nbytes].view(k, self.up_row_nbytes)
@@ -416,45 +422,55 @@ def dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: 
 
 
 def run_decoder_layer_cached_dip(pipeline: WeightPipeline, model: StreamingModel, layer_idx: int,
-                                 x_flat: torch.Tensor, pos: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                                 x_flat: torch.Tensor, pos, k_cache: torch.Tensor, v_cache: torch.Tensor,
                                  dip_k: int, bufs: DipBuffers, caches: list[HotCache],
-                                 miss_bytes: list[int] | None = None) -> torch.Tensor:
+                                 miss_counts: torch.Tensor | None = None) -> torch.Tensor:
     """Cache-aware DIP layer (reference generate.py:313-404): the selected
     channels resolve to hot-cache slots or staging rows (the misses, gathered
     from the arena); one fused GEMV per direction reads both.  Bit-identical
-    to run_decoder_layer_dip on the same inputs.  miss_bytes[layer] counts
-    the streamed bytes."""
+    to run_decoder_layer_dip on the same inputs.  No host read: the miss count
+    stays on the device, so the layer runs inside GraphDecoder's per-token
+    graph.  miss_counts (int64 [num_layers] CUDA, optional) accumulates each
+    layer's miss count on the device."""
     h2, h3, gate = _attention_and_gate(pipeline, model, layer_idx, x_flat, pos, k_cache, v_cache)
     idx = _select(gate, dip_k)
-    return h2 + cached_dip_mlp_tail(model, layer_idx, h3, gate, idx, bufs, caches[layer_idx], miss_bytes)
+    return cached_dip_mlp_tail(model, layer_idx, h3, gate, idx, bufs, caches[layer_idx], miss_counts, residual=h2)
 
 
 def cached_dip_mlp_tail(model: StreamingModel, layer_idx: int, h3: torch.Tensor, gate: torch.Tensor,
                         idx: torch.Tensor, bufs: DipBuffers, cache: HotCache,
-                        miss_bytes: list[int] | None = None) -> torch.Tensor:
+                        miss_counts: torch.Tensor | None = None,
+                        residual: torch.Tensor | None = None) -> torch.Tensor:
     """The cache-aware DIP MLP after the selection (the cached-DIP block minus the
-    gate GEMV and selector): selected channels resolve to hot-cache slots or
-    misses; the misses' up / down_T rows are gathered from the pinned arena by
-    the device (zero-copy over PCIe); one fused GEMV per direction reads both.
-    One host read (the miss count).  Returns the down output (no residual)."""
+    gate GEMV and selector): the selected channels resolve to hot-cache slots
+    or misses (descriptors, ordered miss list and miss count, all on the
+    device); one device-driven gather brings the misses' up / down_T rows and
+    scale rows (zero-copy over PCIe from the pinned arena, or from HBM when
+    the matrix is resident) into staging sized for every selected channel,
+    reading the count on the device; one fused GEMV per direction reads cache
+    and staging rows.  Returns residual + down (or down)."""
     up = model.matrix(layer_idx, "mlp.up_proj.weight")
     down_t = model.matrix(layer_idx, DOWN_PROJ_T_SUFFIX)
     g = model.group_size
+    k = idx.numel()
     desc, miss, miss_count = ops.build_dip_descriptors(idx, cache.slot_of)
-    mc = int(miss_count.item())  # sizes the staging rows (the reference's sync)
-    miss = miss[:mc]
-    miss_long = miss.long()
-    up_rows, down_rows = bufs.up_rows(mc), bufs.down_rows(mc)
-    if mc:
-        ops.gather_rows_device(model.weight_source(up), miss, up_rows)
-        ops.gather_rows_device(model.weight_source(down_t), miss, down_rows)
-    if miss_bytes is not None:
-        miss_bytes[layer_idx] += mc * (bufs.up_row_nbytes + bufs.down_row_nbytes)
-    u_sel = ops.gemv_dip_fused_up(cache.up_Wq, cache.up_scale, up_rows, up.scale.index_select(0, miss_long), desc,
-                                  h3, up.packed_k, g)
+    up_rows, down_rows = bufs.up_rows(k), bufs.down_rows(k)
+    up_sc, down_sc = bufs.gpu_up_scale[:k], bufs.gpu_down_scale[:k]
+    ops.gather_rows_device_multi([(model.weight_source(up), up_rows), (model.weight_source(down_t), down_rows),
+                                  (up.scale, up_sc), (down_t.scale, down_sc)], miss, miss_count, k)
+    if miss_counts is not None:
+        miss_counts[layer_idx : layer_idx + 1].add_(miss_count)
+    u_sel = ops.gemv_dip_fused_up(cache.up_Wq, cache.up_scale, up_rows, up_sc, desc, h3, up.packed_k, g)
     h_sel = ops.swiglu(gate, u_sel, idx)
-    return ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows,
-                                   down_t.scale.index_select(0, miss_long), desc, h_sel, model.hidden_size, g)
+    down = ops.gemv_dip_fused_down(cache.down_Wq, cache.down_scale, down_rows, down_sc, desc, h_sel,
+                                   model.hidden_size, g)
+    return down if residual is None else residual + down
+
+
+def miss_row_bytes(model: StreamingModel) -> int:
+    """Streamed bytes per missed channel: one up_proj row + one down_proj_T row."""
+    return (model.matrix(0, "mlp.up_proj.weight").handle.row_nbytes
+            + model.matrix(0, DOWN_PROJ_T_SUFFIX).handle.row_nbytes)
 
 
 def dip_bytes_per_token(model: StreamingModel, dip_k: int, dense: bool = False) -> int:
@@ -540,13 +556,21 @@ def generate_dip(model: StreamingModel, prompt_ids: list[int], n_new: int, dip_k
 def generate_cached_dip(model: StreamingModel, prompt_ids: list[int], n_new: int, dip_k: int,
                         caches: list[HotCache], eos_token_id: int | None = None, max_seq_len: int = 512,
                         miss_bytes: list[int] | None = None) -> list[int]:
-    """Greedy decode, cache-aware DIP MLPs (reference generate.py:503-542)."""
+    """Greedy decode, cache-aware DIP MLPs (reference generate.py:503-542).
+    miss_bytes[layer] (optional) is increased by the streamed bytes, read
+    from the device counters once at the end."""
     pipeline = WeightPipeline(model, suffixes=DIP_DENSE_SUFFIXES)
     bufs = DipBuffers.make(model, dip_k)
-    return _greedy(model, prompt_ids, n_new,
-                   lambda li, x, p, kc, vc: run_decoder_layer_cached_dip(pipeline, model, li, x, p, kc, vc, dip_k,
-                                                                         bufs, caches, miss_bytes),
-                   eos_token_id, max_seq_len)
+    counts = torch.zeros(model.num_layers, dtype=torch.int64, device=model.device) if miss_bytes is not None else None
+    out = _greedy(model, prompt_ids, n_new,
+                  lambda li, x, p, kc, vc: run_decoder_layer_cached_dip(pipeline, model, li, x, p, kc, vc, dip_k,
+                                                                        bufs, caches, counts),
+                  eos_token_id, max_seq_len)
+    if miss_bytes is not None:
+        per_row = miss_row_bytes(model)
+        for li, c in enumerate(counts.cpu().tolist()):
+            miss_bytes[li] += int(c) * per_row
+    return out
 
 
 class GraphDecoder:
@@ -561,15 +585,25 @@ class GraphDecoder:
     generate_dip on the same model (same kernels, same order)."""
 
     def __init__(self, model: StreamingModel, dip_k: int | None = None, max_seq_len: int = 2048, layer_fn=None,
-                 token_fn=None):
+                 token_fn=None, caches: list[HotCache] | None = None):
         """layer_fn(pipeline, model, layer_idx, x, where, k_cache, v_cache) -> x and
         token_fn(model, xn) -> int32 [1] replace the dense / DIP layer and the
-        fused LM-head argmax (tensor parallelism plugs in here)."""
-        names = [f"model.layers.{i}.{s}" for i in range(model.num_layers) for s in LINEAR_SUFFIXES]
-        if dip_k is not None:
+        fused LM-head argmax (tensor parallelism plugs in here).  caches (with
+        dip_k): cache-aware DIP -- up_proj / down_proj_T may stay in the pinned
+        arena (misses read zero-copy by the device gather); the per-layer miss
+        counts accumulate in self.miss_counts."""
+        if caches is not None and dip_k is None:
+            raise ValueError("GraphDecoder: caches need dip_k (cache-aware DIP)")
+        streamed_ok = ("mlp.up_proj.weight", "mlp.down_proj.weight") if caches is not None else ()
+        names = [f"model.layers.{i}.{s}" for i in range(model.num_layers) for s in LINEAR_SUFFIXES
+                 if s not in streamed_ok]
+        if dip_k is not None and caches is None:
             names.append(f"model.layers.0.{DOWN_PROJ_T_SUFFIX}")
         if not all(model.is_resident(n) for n in names):
             raise ValueError("GraphDecoder needs every decoder weight resident in HBM (StreamingModel.resident)")
+        self.caches = caches
+        self.miss_counts = (torch.zeros(model.num_layers, dtype=torch.int64, device=model.device)
+                            if caches is not None else None)
         self.model, self.dip_k, self.max_seq_len = model, dip_k, max_seq_len
         dev = model.device
         self.stream = torch.cuda.Stream(dev)
@@ -593,6 +627,9 @@ class GraphDecoder:
                 x = self.layer_fn(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
             elif self.dip_k is None:
                 x = run_decoder_layer_streaming(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
+            elif self.caches is not None:
+                x = run_decoder_layer_cached_dip(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li],
+                                                 self.dip_k, self.bufs, self.caches, self.miss_counts)
             else:
                 x = run_decoder_layer_dip(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li],
                                           self.dip_k, self.bufs)
@@ -632,6 +669,8 @@ class GraphDecoder:
             for kc, vc in zip(self.k_caches, self.v_caches):
                 kc.zero_()
                 vc.zero_()
+            if self.miss_counts is not None:
+                self.miss_counts.zero_()
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
             ev[0].record(self.stream)
             for _ in range(P):

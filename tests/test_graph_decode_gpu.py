@@ -87,6 +87,42 @@ def test_graph_decoder_tokens_equal_eager(model):
     assert gdip.generate(prompt, 6) == dip
 
 
+def test_graph_cached_dip_tokens_equal_graph_dip():
+    """Cache-aware DIP inside the per-token CUDA graph: no host read of the
+    miss count (the descriptors, the miss gather -- zero-copy from the pinned
+    arena -- and the fused GEMVs all take it on the device), and the tokens
+    equal graph DIP's bit for bit over 16 new tokens for an empty cache, a 20%
+    Zipf(1.1) hot set and a full cache; the device miss counters match."""
+    import copy
+
+    from soinfer.offload.hot_cache import HotCache, StaticFrequencyPolicy
+
+    I, dip_k = ARCH.intermediate_size, ARCH.intermediate_size // 2
+    full = synthetic_streaming_model(ARCH, seed=6, resident=True, offload=True, include_dip=True)
+    host = copy.copy(full)  # up_proj / down_proj_T read from the pinned arena
+    host.resident = {n: t for n, t in full.resident.items()
+                     if not (n.endswith("mlp.up_proj.weight") or n.endswith(gen.DOWN_PROJ_T_SUFFIX))}
+    prompt, n_new = [3, 141, 59, 26], 16
+    ref = gen.GraphDecoder(full, dip_k=dip_k, max_seq_len=64).generate(prompt, n_new)
+    assert ref == gen.generate_dip(full, prompt, n_new, dip_k, max_seq_len=64)
+    rng = np.random.default_rng(0)
+    freq = np.empty(I, dtype=np.int64)
+    freq[rng.permutation(I)] = (1e9 / np.arange(1, I + 1) ** 1.1).astype(np.int64)
+    steps = len(prompt) + n_new - 1
+    for frac in (0.0, 0.2, 1.0):
+        hot = StaticFrequencyPolicy(freq.tolist(), round(frac * I)).hot_list
+        caches = [HotCache.build(full, li, hot) for li in range(ARCH.num_layers)]
+        gd = gen.GraphDecoder(host, dip_k=dip_k, max_seq_len=64, caches=caches)
+        assert gd.generate(prompt, n_new) == ref, f"cached DIP tokens differ (cache fraction {frac})"
+        counts = gd.miss_counts.cpu().tolist()
+        if frac == 0.0:
+            assert counts == [steps * dip_k] * ARCH.num_layers
+        elif frac == 1.0:
+            assert counts == [0] * ARCH.num_layers
+        else:
+            assert all(0 < c < steps * dip_k for c in counts)
+
+
 def test_graph_decoder_needs_resident_weights():
     streamed = synthetic_streaming_model(ARCH, seed=5, resident=False, offload=True)
     with pytest.raises(ValueError):

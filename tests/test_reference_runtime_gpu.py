@@ -1,0 +1,87 @@
+"""Full-model token parity with the reference implementation's own runtime.
+
+One seeded random-init Qwen3 checkpoint (4 layers of the Qwen3-1.7B shape,
+written as sharded safetensors in a temporary directory) is decoded greedily
+by both implementations from the same prompt:
+
+* the reference -- its loader (CPU quantize + pack into the pinned arena) and
+  its generate_streaming / generate_dip / generate_cached_dip loops on its
+  own CUDA kernels (sparse-offload-infer installed with its extension,
+  compiled for sm_100a, under baseline/_ref), run in a subprocess by
+  tests/reference_runner.py;
+* this build -- load_streaming_model on the same directory (GPU quantize +
+  pack, bit-exact with the reference's), the eager loops and the per-token
+  CUDA-graph decoder (dense, DIP k/I = 0.5, cache-aware DIP with the same hot
+  set).
+
+The greedy tokens must be equal.  Skipped when baseline/_ref holds no
+reference install (it is not committed)."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+transformers = pytest.importorskip("transformers")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+N_NEW = 16
+PROMPT = [11, 42, 7, 93, 5, 64, 30, 77]
+
+
+@pytest.fixture(scope="module")
+def checkpoint(tmp_path_factory):
+    if not os.path.isfile(os.path.join(REF, "soinfer", "runtime", "generate.py")):
+        pytest.skip("no reference install under baseline/_ref")
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(0)
+    config = Qwen3Config(hidden_size=2048, intermediate_size=6144, num_attention_heads=16, num_key_value_heads=8,
+                         head_dim=128, num_hidden_layers=4, rms_norm_eps=1e-6, rope_theta=1_000_000, vocab_size=100,
+                         tie_word_embeddings=False)
+    model = Qwen3ForCausalLM(config).half()
+    d = str(tmp_path_factory.mktemp("qwen3_random"))
+    model.save_pretrained(d, max_shard_size="200MB", safe_serialization=True)
+    assert os.path.isfile(os.path.join(d, "model.safetensors.index.json"))
+    return d, config
+
+
+@pytest.fixture(scope="module")
+def reference_tokens(checkpoint, tmp_path_factory):
+    d, config = checkpoint
+    out = str(tmp_path_factory.mktemp("ref_out") / "tokens.json")
+    hot = list(range(0, config.intermediate_size, 5))  # every 5th channel: a 20% hot set
+    cmd = [sys.executable, os.path.join(ROOT, "tests", "reference_runner.py"), REF, d, out, json.dumps(PROMPT),
+           str(N_NEW), str(config.intermediate_size // 2), json.dumps(hot)]
+    env = {k: v for k, v in os.environ.items() if k != "PYTHONPATH"}
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=1200, env=env, cwd="/tmp")
+    assert r.returncode == 0, f"reference runner failed:\n{r.stdout[-2000:]}\n{r.stderr[-4000:]}"
+    with open(out) as f:
+        return json.load(f), hot
+
+
+def test_dense_dip_and_cached_dip_tokens_equal_the_reference_runtime(checkpoint, reference_tokens):
+    from soinfer.offload.hot_cache import HotCache
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import load_streaming_model
+
+    d, config = checkpoint
+    ref, hot = reference_tokens
+    dip_k = config.intermediate_size // 2
+    assert ref["cached_dip"] == ref["dip"], "the reference's own cached DIP differs from its DIP"
+    model = load_streaming_model(d, group_size=128, include_dip=True, resident=True)
+    max_seq = len(PROMPT) + N_NEW + 1
+    dense = gen.generate_streaming(model, PROMPT, N_NEW, max_seq_len=max_seq)
+    dip = gen.generate_dip(model, PROMPT, N_NEW, dip_k, max_seq_len=max_seq)
+    assert dense == ref["dense"], f"dense: reference {ref['dense']} vs {dense}"
+    assert dip == ref["dip"], f"DIP k/I=0.5: reference {ref['dip']} vs {dip}"
+    caches = [HotCache.build(model, li, hot) for li in range(model.num_layers)]
+    assert gen.generate_cached_dip(model, PROMPT, N_NEW, dip_k, caches, max_seq_len=max_seq) == ref["cached_dip"]
+    assert gen.GraphDecoder(model, max_seq_len=64).generate(PROMPT, N_NEW) == ref["dense"]
+    assert gen.GraphDecoder(model, dip_k=dip_k, max_seq_len=64).generate(PROMPT, N_NEW) == ref["dip"]
+    assert gen.GraphDecoder(model, dip_k=dip_k, max_seq_len=64, caches=caches).generate(PROMPT, N_NEW) == \
+        ref["cached_dip"]
