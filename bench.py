@@ -171,15 +171,16 @@ def cpu_gemv_sample(seconds: float, threads: int):
     return gbs, desc, n_gemv
 
 
-def op_suite(ops, formats, pack, device, iters: int = 200) -> dict:
+def op_suite(ops, formats, pack, device, capturable: bool, iters: int = 200) -> dict:
     """Per-call latency of the hot-path ops at the BASELINE config shapes,
     through the given `ops` module with the same names and arguments -- this
     build's soinfer.ops, or the reference's own (its extension compiled for
     sm_100a, baseline/_ref) in the reference arm.  Inputs come from the
     module's own quantizer (bit-exact between the two), seeded identically.
-    Each figure: mean of `iters` back-to-back calls on the current stream
-    after 20 warm-up calls, CUDA events; the weights of one call fit in L2, as
-    in decode."""
+    Per op: call_us, the mean of `iters` back-to-back calls on the current
+    stream after 20 warm-up calls (CUDA events: the binding's host cost shows
+    when it exceeds the kernel's), and device_us, the device time per call
+    (see timed); the weights of one call fit in L2, as in decode."""
     gen = torch.Generator().manual_seed(0)
     cfg = formats.QuantConfig(bits=4, granularity="group", group_size=G)
 
@@ -189,6 +190,14 @@ def op_suite(ops, formats, pack, device, iters: int = 200) -> dict:
         return p.contiguous().to(device), qt.scale.contiguous().to(device)
 
     def timed(fn):
+        """(call us, device us): back-to-back calls timed with CUDA events
+        (includes each binding's host cost when it exceeds the kernel's), and
+        the device time of one call: a CUDA graph of `iters` calls replayed
+        (this build's ops launch on the current stream), or the CUPTI
+        durations of the launched kernels through torch.profiler (the
+        reference's ops launch on the legacy default stream, which cannot be
+        captured; they use no programmatic dependent launch, so their kernel
+        durations do not overlap)."""
         for _ in range(20):
             fn()
         torch.cuda.synchronize(device)
@@ -198,12 +207,48 @@ def op_suite(ops, formats, pack, device, iters: int = 200) -> dict:
             fn()
         e.record()
         torch.cuda.synchronize(device)
-        return s.elapsed_time(e) * 1e3 / iters
+        call_us = s.elapsed_time(e) * 1e3 / iters
+        dev_us = None
+        if capturable:
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=st):
+                    for _ in range(iters):
+                        fn()
+                graph.replay()
+                s.record(st)
+                graph.replay()
+                e.record(st)
+            torch.cuda.synchronize(device)
+            dev_us = s.elapsed_time(e) * 1e3 / iters
+            del graph
+        else:
+            try:
+                from torch.autograd import DeviceType
+                from torch.profiler import ProfilerActivity, profile
+
+                n = 50
+                with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                    for _ in range(n):
+                        fn()
+                    torch.cuda.synchronize(device)
+                tot = 0.0
+                for ev in prof.events():
+                    if getattr(ev, "device_type", None) == DeviceType.CUDA:
+                        tot += float(getattr(ev, "device_time", None) or getattr(ev, "cuda_time", 0.0) or 0.0)
+                dev_us = tot / n if tot > 0 else None
+            except Exception:  # no CUPTI here: the call time stands alone
+                dev_us = None
+        return call_us, dev_us
 
     out = {}
 
-    def rec(name, us, nbytes):
-        out[name] = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1)}
+    def rec(name, t, nbytes):
+        call_us, dev_us = t
+        out[name] = {"call_us": round(call_us, 2), "device_us": round(dev_us, 2) if dev_us else None,
+                     "device_gbs": round(nbytes / dev_us / 1e3, 1) if dev_us else None}
 
     for n, k in ((I, H), (H, I)):
         W, S = q4(n, k)
@@ -321,7 +366,7 @@ def run_reference(args) -> None:
         try:
             from soinfer import ops as ref_ops_mod
 
-            ref_ops = op_suite(ref_ops_mod, formats, pack, torch.device("cuda", 0))
+            ref_ops = op_suite(ref_ops_mod, formats, pack, torch.device("cuda", 0), capturable=False)
         except Exception as exc:  # the extension could not run here: report why, keep the CPU line
             ref_ops = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     line = {
@@ -465,7 +510,7 @@ def run_ours(args) -> None:
         from soinfer import ops as our_ops
         from soinfer.quant import formats, pack
 
-        ops_b200 = op_suite(our_ops, formats, pack, device)
+        ops_b200 = op_suite(our_ops, formats, pack, device, capturable=True)
 
     peaks = measured_peaks()
     peak = peaks.get("hbm_gbs")
@@ -516,10 +561,12 @@ def run_ours(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_gemm_m8(layers, device, reps: int = 20) -> dict:
+def run_gemm_m8(layers, device, reps: int = 40) -> dict:
     """configs[4]'s batch-8 variant on the headline stream: the same 64 layer
-    copies x (gate, down), each GEMM multiplying 8 token rows in one pass over
-    the weights (soinfer_gemm_w4a16), 128 launches captured in one CUDA graph."""
+    copies x (gate, down), each matrix multiplying 8 token rows, all 128
+    matrices in ONE launch (soinfer_gemm_w4a16_batch: the streaming kernel
+    with the 8 tokens in the MMA columns); the older per-matrix kernel
+    (soinfer_gemm_w4a16, 128 launches in one CUDA graph) is reported beside it."""
     from soinfer import _C
 
     M = 8
@@ -528,8 +575,29 @@ def run_gemm_m8(layers, device, reps: int = 20) -> dict:
     Xd = torch.randn(M, I, generator=gen, device=device).half()
     Yg = [torch.empty(M, I, dtype=torch.float16, device=device) for _ in layers]
     Yd = [torch.empty(M, H, dtype=torch.float16, device=device) for _ in layers]
+    L = len(layers)
+    w_bytes = 2 * L * (I * H // 2 + I * H // 128 * 4)
+    act_bytes = L * M * 2 * (H + I) * 2
+    tasks = []
+    for li, (gw, gs, dw, ds) in enumerate(layers):
+        tasks += [(gw, gs, Xg, Yg[li], H, G), (dw, ds, Xd, Yd[li], I, G)]
+    batch = _C.GemmBatch(tasks)
+    for _ in range(3):
+        batch.run()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        batch.run()
+    e.record()
+    torch.cuda.synchronize(device)
+    assert _C.device_errors() == 0, "device error flag set by the batched multi-token GEMM"
+    ms = s.elapsed_time(e) / reps
+    # spot check: one token row of the first gate against the single-matrix kernel
+    ref = _C.gemm_w4a16(layers[0][0], layers[0][1], Xg, H, G)
+    assert (Yg[0].float() - ref.float()).abs().max().item() < 1e-2 * max(1.0, ref.float().abs().max().item())
 
-    def step():
+    def step_old():
         for li, (gw, gs, dw, ds) in enumerate(layers):
             _C.gemm_w4a16(gw, gs, Xg, H, G, out=Yg[li])
             _C.gemm_w4a16(dw, ds, Xd, I, G, out=Yd[li])
@@ -537,30 +605,29 @@ def run_gemm_m8(layers, device, reps: int = 20) -> dict:
     st = torch.cuda.Stream(device)
     st.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(st):
-        step()
+        step_old()
         torch.cuda.synchronize(device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=st):
-            step()
+            step_old()
         for _ in range(3):
             graph.replay()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(st)
-        for _ in range(reps):
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(st)
+        for _ in range(20):
             graph.replay()
-        e.record(st)
+        e2.record(st)
     torch.cuda.synchronize(device)
-    assert _C.device_errors() == 0, "device error flag set by the multi-token GEMM"
-    ms = s.elapsed_time(e) / reps
-    L = len(layers)
-    w_bytes = 2 * L * (I * H // 2 + I * H // 128 * 4)
-    act_bytes = L * M * 2 * (H + I) * 2
+    ms_old = s2.elapsed_time(e2) / 20
     del graph
     return {"m": M, "value": round((w_bytes + act_bytes) / (ms / 1e3) / 1e9, 2), "unit": UNIT,
-            "ms_per_step": round(ms, 4), "gemms_per_step": 2 * L,
+            "ms_per_launch": round(ms, 4), "gemms_per_launch": 2 * L,
             "token_gemvs_per_s": round(2 * L * M / (ms / 1e3), 1),
-            "note": "each launch = 8 tokens x one INT4 g128 matrix (mma.sync columns carry the tokens), "
-                    "128 launches in one CUDA graph"}
+            "per_matrix_kernel": {"value": round((w_bytes + act_bytes) / (ms_old / 1e3) / 1e9, 2), "unit": UNIT,
+                                  "ms_per_step": round(ms_old, 4),
+                                  "note": "soinfer_gemm_w4a16, one launch per matrix, 128 launches in a CUDA graph"},
+            "note": "one soinfer_gemm_w4a16_batch launch = 128 matrices x 8 tokens (streaming kernel, tokens in "
+                    "the mma.sync columns)"}
 
 
 def run_e2e(args, layers, device, world, dist) -> dict:

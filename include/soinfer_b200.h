@@ -425,6 +425,32 @@ int soinfer_gemm_w4a16(const uint8_t* Wq_packed, const float* scale, const soinf
                        soinfer_half* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
                        int64_t num_groups, void* stream);
 
+/* One task of soinfer_gemm_w4a16_batch: Y[m, 0:N] = dequant(Wq) X[m, 0:K]
+ * for the batch's M tokens (X row stride ldx, Y row stride ldy, elements). */
+typedef struct soinfer_gemm_task {
+  const uint8_t* Wq;
+  const float* scale;
+  const soinfer_half* X;
+  soinfer_half* Y;
+  int64_t N, K, group_size, num_groups, ldx, ldy;
+} soinfer_gemm_task;
+
+/* Bytes of zero-initialised device workspace soinfer_gemm_w4a16_batch needs
+ * (a work ticket and an exit count; left zeroed on return). */
+int64_t soinfer_gemm_batch_workspace_bytes(void);
+
+/* Batched decode of M <= 8 tokens over a list of up to 256 independent INT4
+ * matrices in ONE launch: every task's Y = X W^T as in soinfer_gemm_w4a16,
+ * with the weights of all tasks streamed by the same kernel as
+ * soinfer_gemv_w4a16_batch's independent GEMVs (a warp per 48-row unit over
+ * the full K, the M tokens in the tensor-core MMA's columns).  No task may
+ * read another's Y.  Needs K and group_size multiples of 128, 16-byte aligned
+ * Wq and X rows (ldx * 2 % 16 == 0), 4-byte aligned scales; otherwise
+ * SOINFER_ERR_UNSUPPORTED.  No reference counterpart (the reference decodes
+ * one token at a time, runtime/generate.py:429-463). */
+int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, int64_t M, void* workspace,
+                             int64_t workspace_bytes, void* stream);
+
 /* Load-time INT4 quantization + packing on the GPU (reference
  * python/soinfer/quant/formats.py:77-110 with calibrate.min_max:22-27 and
  * quant/pack.py:31-69): w [N, K] with row stride ld (dtype 0 fp32, 1 fp16,

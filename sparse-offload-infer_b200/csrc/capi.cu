@@ -176,10 +176,11 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
     static std::mutex smu;
     std::lock_guard<std::mutex> lk(smu);
     S.num = (int)num_tasks;
+    S.m = 1;
     for (int64_t i = 0; i < num_tasks; ++i) {
       const soinfer_gemv_task& t = tasks[i];
       S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.x), as_half(t.y), (int)t.N, (int)t.K,
-                                  (int)t.num_groups, (int)(t.group_size / 128), 0};
+                                  (int)t.num_groups, (int)(t.group_size / 128), (int)t.K, (int)t.N, 0};
     }
     if (plan_gemv_stream(S, sms)) {
       REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
@@ -252,6 +253,43 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
         return rc;
   }
   return SOINFER_OK;
+}
+
+int64_t soinfer_gemm_batch_workspace_bytes(void) { return gemv_stream_workspace_bytes(); }
+
+int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, int64_t M, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  const char* name = "gemm_w4a16_batch";
+  REQUIRE(num_tasks >= 0 && num_tasks <= kMaxBatchTasks, "%s: num_tasks must be in [0, %d]", name, kMaxBatchTasks);
+  REQUIRE(M >= 1 && M <= 8, "%s: M must be in [1, 8]", name);
+  if (num_tasks == 0) return SOINFER_OK;
+  REQUIRE(tasks, "%s: null task list", name);
+  static GemvStreamParams S;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  S.num = (int)num_tasks;
+  S.m = (int)M;
+  for (int64_t i = 0; i < num_tasks; ++i) {
+    const soinfer_gemm_task& t = tasks[i];
+    char tn[64];
+    snprintf(tn, sizeof(tn), "%s[task %lld]", name, (long long)i);
+    if (int st = check_int4_layout(tn, t.K, t.group_size, t.num_groups)) return st;
+    REQUIRE(t.N >= 1 && t.N < (1 << 30) && t.K < (1 << 30), "%s: N must be in [1, 2^30)", tn);
+    REQUIRE(t.Wq && t.scale && t.X && t.Y, "%s: null pointer", tn);
+    REQUIRE(t.ldx >= t.K && t.ldy >= t.N && t.ldx < (1 << 30) && t.ldy < (1 << 30), "%s: ldx >= K, ldy >= N", tn);
+    if (!(t.K % 128 == 0 && t.group_size % 128 == 0 && aligned(t.Wq, 16) && aligned(t.X, 16) && t.ldx % 8 == 0 &&
+          aligned(t.scale, 4) && aligned(t.Y, 2)))
+      return set_error(SOINFER_ERR_UNSUPPORTED, "%s: needs K and group_size multiples of 128, 16-byte aligned "
+                       "Wq and X rows, 4-byte aligned scales", tn);
+    S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.X), as_half(t.Y), (int)t.N, (int)t.K, (int)t.num_groups,
+                                (int)(t.group_size / 128), (int)t.ldx, (int)t.ldy, 0};
+  }
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  REQUIRE(plan_gemv_stream(S, sms), "%s: batch too large", name);
+  REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
+          "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes());
+  return cuda_result(launch_gemv_stream(S, reinterpret_cast<int*>(workspace), as_stream(stream)), name);
 }
 
 int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,

@@ -42,13 +42,14 @@ namespace soinfer {
 namespace {
 
 
-// Stage layout for units of T 16-row tiles.
-template <int T>
+// Stage layout for units of T 16-row tiles and MT token columns (1, or up
+// to 8 for the multi-token form).
+template <int T, int MT>
 struct StageLayout {
   static constexpr int kRows = 16 * T;
   static constexpr int kW = 0;                   // [2T row groups][32 lanes][16 B]
-  static constexpr int kX = kRows * 64;          // chunk x: 256 B, t-pieces 2 / 3 shifted by 16 B
-  static constexpr int kS = kX + 288;            // [kRows] fp32 scales
+  static constexpr int kX = kRows * 64;          // per token: the chunk's 256 B of x, t-pieces 2 / 3 shifted by 16 B
+  static constexpr int kS = kX + 288 * MT;       // [kRows] fp32 scales
   static constexpr int kTag = kS + kRows * 4;    // int4 tag
   static constexpr int kBytes = kTag + 16;
 };
@@ -99,6 +100,46 @@ __device__ __forceinline__ void st_chunk_dot(const uint4 wa, const uint4 wb, con
   s1 = fmaf(o[2], 0.0625f, e[2]);
 }
 
+// Multi-token form of st_chunk_dot: B column n carries token n, so every D
+// element is a distinct (row, token) sum: s[0] = (g, 2t), s[1] = (g, 2t + 1),
+// s[2] = (g + 8, 2t), s[3] = (g + 8, 2t + 1).
+__device__ __forceinline__ void st_chunk_dot4(const uint4 wa, const uint4 wb, const uint4 xf[4], const UnpackK& k,
+                                              float s[4]) {
+  const uint32_t r0[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t r1[4] = {wb.x, wb.y, wb.z, wb.w};
+  float e[4] = {0.f, 0.f, 0.f, 0.f}, o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t t0 = r0[j] >> 8, t1 = r1[j] >> 8;
+    const uint32_t ae[4] = {lop3_and_xor(r0[j], 0x000f000fu, k.lo), lop3_and_xor(r1[j], 0x000f000fu, k.lo),
+                            lop3_and_xor(t0, 0x000f000fu, k.lo), lop3_and_xor(t1, 0x000f000fu, k.lo)};
+    mma_16816(e, ae, xf[j].x, xf[j].z);
+    const uint32_t ao[4] = {lop3_and_xor(r0[j], 0x00f000f0u, k.hi), lop3_and_xor(r1[j], 0x00f000f0u, k.hi),
+                            lop3_and_xor(t0, 0x00f000f0u, k.hi), lop3_and_xor(t1, 0x00f000f0u, k.hi)};
+    mma_16816(o, ao, xf[j].y, xf[j].w);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s[i] = fmaf(o[i], 0.0625f, e[i]);
+}
+
+// Per-token chunk biases for the multi-token form, from the x fragments the
+// lane already holds: with A uniform (1032 for the low-nibble positions x0
+// x1 x4 x5 of each 8-group, 72 for the high ones), column n of D sums
+// token n's x over the positions its B operand covers; eight MMAs cover the
+// chunk, so b[0] / b[1] = the bias of tokens 2t / 2t + 1.
+__device__ __forceinline__ void st_chunk_bias_tokens(const uint4 xf[4], float b[2]) {
+  const uint32_t lo[4] = {0x64086408u, 0x64086408u, 0x64086408u, 0x64086408u};  // 1032
+  const uint32_t hi[4] = {0x54805480u, 0x54805480u, 0x54805480u, 0x54805480u};  // 72
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mma_16816(d, lo, xf[j].x, xf[j].z);
+    mma_16816(d, hi, xf[j].y, xf[j].w);
+  }
+  b[0] = d[0];
+  b[1] = d[1];
+}
+
 // The chunk's bias 1032 XL + 72 XH (gemv_batch.cu chunk_bias) from this
 // lane's 8 bytes of the chunk's x (bytes 8 * lane .. 8 * lane + 7).
 __device__ __forceinline__ float st_chunk_bias(uint2 xw) {
@@ -113,18 +154,19 @@ __device__ __forceinline__ float st_chunk_bias(uint2 xw) {
 
 // Fetch cursor: the unit being fetched and this lane's source pointers at
 // the current chunk (set once per unit, advanced by adds per chunk).
-template <int T>
+template <int T, int MT>
 struct Cursor {
   static constexpr int kSP = (16 * T + 31) / 32;  // scale rows per lane
+  static constexpr int kXP = MT == 1 ? 1 : MT / 2;  // x pieces per lane (8 B for one token, else 16 B)
   const uint8_t* wp[2 * T];  // 16 B of row row0 + g + 8r (clamped to N - 1) at the chunk
   const float* sp[kSP];      // scale of row row0 + lane + 32i (clamped) at the chunk's group
-  const half* xp;            // 8 B of x at the chunk
+  const half* xp[kXP];       // this lane's x pieces at the chunk (token (lane + 32i) / 16, clamped to m - 1)
   int task, row0, chunk, nch, sub, cpg;
   bool done;
 };
 
-template <int T, class P>
-__device__ __forceinline__ void st_resolve(const P& B, int u, int lane, Cursor<T>& c) {
+template <int T, int MT, class P>
+__device__ __forceinline__ void st_resolve(const P& B, int u, int lane, Cursor<T, MT>& c) {
   if (u >= B.total_units) {
     c.done = true;
     return;
@@ -147,13 +189,23 @@ __device__ __forceinline__ void st_resolve(const P& B, int u, int lane, Cursor<T
 #pragma unroll
   for (int r = 0; r < 2 * T; ++r) c.wp[r] = tk.W + (int64_t)min(c.row0 + g + 8 * r, tk.N - 1) * rb + t * 16;
 #pragma unroll
-  for (int i = 0; i < Cursor<T>::kSP; ++i) c.sp[i] = tk.S + (int64_t)min(c.row0 + lane + 32 * i, tk.N - 1) * tk.G;
-  c.xp = tk.x + lane * 4;
+  for (int i = 0; i < Cursor<T, MT>::kSP; ++i)
+    c.sp[i] = tk.S + (int64_t)min(c.row0 + lane + 32 * i, tk.N - 1) * tk.G;
+  if constexpr (MT == 1) {
+    c.xp[0] = tk.x + lane * 4;
+  } else {
+#pragma unroll
+    for (int i = 0; i < Cursor<T, MT>::kXP; ++i) {
+      const int p = lane + 32 * i;
+      c.xp[i] = tk.x + (int64_t)min(p >> 4, B.m - 1) * tk.ldx + (p & 15) * 8;
+    }
+  }
 }
 
-template <int T, int D, int W, class P>
+template <int T, int D, int W, int MT, class P>
 __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_constant__ P B, int* __restrict__ ctr) {
-  using L = StageLayout<T>;
+  using L = StageLayout<T, MT>;
+  using C = Cursor<T, MT>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -166,7 +218,7 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     first = atomicAdd(ctr, 1);
     nxt = atomicAdd(ctr, 1);
   }
-  Cursor<T> f;
+  C f;
   f.done = false;
   st_resolve(B, __shfl_sync(0xffffffffu, first, 0), lane, f);
   const UnpackK uk;
@@ -180,9 +232,17 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     }
 #pragma unroll
     for (int r = 0; r < 2 * T; ++r) cpa16(st + L::kW + r * 512 + lane * 16, f.wp[r]);
-    cpa8(st + L::kX + lane * 8 + ((lane >> 4) << 4), f.xp);
+    if constexpr (MT == 1) {
+      cpa8(st + L::kX + lane * 8 + ((lane >> 4) << 4), f.xp[0]);
+    } else {
 #pragma unroll
-    for (int i = 0; i < Cursor<T>::kSP; ++i)
+      for (int i = 0; i < C::kXP; ++i) {
+        const int p = lane + 32 * i, c16 = p & 15;
+        cpa16(st + L::kX + (p >> 4) * 288 + c16 * 16 + ((c16 >> 3) << 4), f.xp[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < C::kSP; ++i)
       if (lane + 32 * i < L::kRows) cpa4(st + L::kS + (lane + 32 * i) * 4, f.sp[i]);
     if (lane == 0)
       *reinterpret_cast<int4*>(ring + s * L::kBytes + L::kTag) =
@@ -196,11 +256,12 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     } else {
 #pragma unroll
       for (int r = 0; r < 2 * T; ++r) f.wp[r] += 64;
-      f.xp += 128;
+#pragma unroll
+      for (int i = 0; i < C::kXP; ++i) f.xp[i] += 128;
       if (++f.sub == f.cpg) {
         f.sub = 0;
 #pragma unroll
-        for (int i = 0; i < Cursor<T>::kSP; ++i) ++f.sp[i];
+        for (int i = 0; i < C::kSP; ++i) ++f.sp[i];
       }
     }
   };
@@ -208,10 +269,11 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
 #pragma unroll
   for (int s = 0; s < D; ++s) fetch(s);
 
-  float acc[2 * T];
+  constexpr int kAcc = MT == 1 ? 2 * T : 4 * T;  // per tile: rows g, g + 8 (x tokens 2t, 2t + 1)
+  float acc[kAcc];
 #pragma unroll
-  for (int r = 0; r < 2 * T; ++r) acc[r] = 0.f;
-  const int xoff = L::kX + t * 64 + ((t >> 1) << 4);
+  for (int r = 0; r < kAcc; ++r) acc[r] = 0.f;
+  const int xoff = L::kX + (MT == 1 ? 0 : g * 288) + t * 64 + ((t >> 1) << 4);
   const int boff = L::kX + lane * 8 + ((lane >> 4) << 4);
   int s = 0;
   while (true) {
@@ -226,31 +288,56 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     uint4 xf[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) xf[j] = *reinterpret_cast<const uint4*>(stg + xoff + j * 16);
-    const uint2 xb = *reinterpret_cast<const uint2*>(stg + boff);
+    uint2 xb = make_uint2(0, 0);
+    if constexpr (MT == 1) xb = *reinterpret_cast<const uint2*>(stg + boff);
     float sc[2 * T];
 #pragma unroll
     for (int r = 0; r < 2 * T; ++r) sc[r] = reinterpret_cast<const float*>(stg + L::kS)[g + 8 * r];
     __syncwarp();  // every lane has read the stage: refill it with the chunk D ahead
     fetch(s);
-    const float bias = st_chunk_bias(xb);
+    if constexpr (MT == 1) {
+      const float bias = st_chunk_bias(xb);
 #pragma unroll
-    for (int tt = 0; tt < T; ++tt) {
-      float d0, d1;
-      st_chunk_dot(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
-      acc[2 * tt] = fmaf(sc[2 * tt], d0 - bias, acc[2 * tt]);
-      acc[2 * tt + 1] = fmaf(sc[2 * tt + 1], d1 - bias, acc[2 * tt + 1]);
+      for (int tt = 0; tt < T; ++tt) {
+        float d0, d1;
+        st_chunk_dot(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
+        acc[2 * tt] = fmaf(sc[2 * tt], d0 - bias, acc[2 * tt]);
+        acc[2 * tt + 1] = fmaf(sc[2 * tt + 1], d1 - bias, acc[2 * tt + 1]);
+      }
+    } else {
+      float bt[2];
+      st_chunk_bias_tokens(xf, bt);
+#pragma unroll
+      for (int tt = 0; tt < T; ++tt) {
+        float d[4];
+        st_chunk_dot4(w[2 * tt], w[2 * tt + 1], xf, uk, d);
+        acc[4 * tt + 0] = fmaf(sc[2 * tt], d[0] - bt[0], acc[4 * tt + 0]);
+        acc[4 * tt + 1] = fmaf(sc[2 * tt], d[1] - bt[1], acc[4 * tt + 1]);
+        acc[4 * tt + 2] = fmaf(sc[2 * tt + 1], d[2] - bt[0], acc[4 * tt + 2]);
+        acc[4 * tt + 3] = fmaf(sc[2 * tt + 1], d[3] - bt[1], acc[4 * tt + 3]);
+      }
     }
     if (tag.w & 2) {  // last chunk of the unit: rows g + 8r of the unit
       const auto& tk = B.tasks[tag.x];
-      if (t == 0) {
+      if constexpr (MT == 1) {
+        if (t == 0) {
 #pragma unroll
-        for (int r = 0; r < 2 * T; ++r) {
-          const int row = tag.y + g + 8 * r;
-          if (row < tk.N) tk.y[row] = __float2half_rn(acc[r]);
+          for (int r = 0; r < 2 * T; ++r) {
+            const int row = tag.y + g + 8 * r;
+            if (row < tk.N) tk.y[row] = __float2half_rn(acc[r]);
+          }
         }
+      } else {
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = tag.y + 16 * tt + g + 8 * (q >> 1), tok = 2 * t + (q & 1);
+            if (row < tk.N && tok < B.m) tk.y[(int64_t)tok * tk.ldy + row] = __float2half_rn(acc[4 * tt + q]);
+          }
       }
 #pragma unroll
-      for (int r = 0; r < 2 * T; ++r) acc[r] = 0.f;
+      for (int r = 0; r < kAcc; ++r) acc[r] = 0.f;
     }
     s = (s + 1 == D) ? 0 : s + 1;
   }
@@ -266,11 +353,11 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
   }
 }
 
-template <int T, int D, int W, class P>
+template <int T, int D, int W, int MT, class P>
 cudaError_t launch_stream_params(const P& B, int* ctr, cudaStream_t stream) {
-  auto kernel = gemv_stream_kernel<T, D, W, P>;
-  const int smem = W * D * StageLayout<T>::kBytes;
-  if (cudaError_t e = ensure_smem_attr<gemv_stream_kernel<T, D, W, P>>(smem); e != cudaSuccess) return e;
+  auto kernel = gemv_stream_kernel<T, D, W, MT, P>;
+  const int smem = W * D * StageLayout<T, MT>::kBytes;
+  if (cudaError_t e = ensure_smem_attr<gemv_stream_kernel<T, D, W, MT, P>>(smem); e != cudaSuccess) return e;
   kernel<<<B.grid, W * 32, smem, stream>>>(B, ctr);
   return cudaGetLastError();
 }
@@ -312,16 +399,18 @@ bool plan_gemv_stream(GemvStreamParams& B, int sms) {
 }
 
 cudaError_t launch_gemv_stream(const GemvStreamParams& B, int* ctr, cudaStream_t stream) {
+  if (B.m > 1) return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps, 8>(B, ctr, stream);
   if (B.num <= kSmallBatchTasks) {
     static GemvStreamParamsT<kSmallBatchTasks> S;  // callers serialise launches
     S.num = B.num;
     S.grid = B.grid;
     S.total_units = B.total_units;
     S.total_warps = B.total_warps;
+    S.m = B.m;
     for (int i = 0; i < B.num; ++i) S.tasks[i] = B.tasks[i];
-    return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps>(S, ctr, stream);
+    return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps, 1>(S, ctr, stream);
   }
-  return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps>(B, ctr, stream);
+  return launch_stream_params<kStreamTiles, kStreamStages, kStreamWarps, 1>(B, ctr, stream);
 }
 
 }  // namespace soinfer

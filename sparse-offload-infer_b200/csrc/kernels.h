@@ -128,14 +128,16 @@ cudaError_t read_and_clear_gemv_batch_error(int* out);
 struct GemvStreamTask {
   const uint8_t* W;
   const float* S;
-  const half* x;
-  half* y;
+  const half* x;  // [m, K], row stride ldx (m tokens)
+  half* y;        // [m, N], row stride ldy
   int N, K, G, cpg;
-  int ubegin;  // filled by plan_gemv_stream: first unit of the task
+  int ldx, ldy;   // token strides in elements (multi-token form)
+  int ubegin;     // filled by plan_gemv_stream: first unit of the task
 };
 template <int MaxTasks>
 struct GemvStreamParamsT {
   int num, grid, total_units, total_warps;
+  int m;  // tokens per task: 1 (GEMV) or 2..8 (every task multiplies m token rows)
   GemvStreamTask tasks[MaxTasks];
 };
 using GemvStreamParams = GemvStreamParamsT<kMaxBatchTasks>;

@@ -78,6 +78,8 @@ _SIGNATURES = {
     "soinfer_peer_buffer_destroy": (_INT, [_P]),
     "soinfer_peer_buffer_reset": (_INT, [_P, _P]),
     "soinfer_gather_rows_device_multi": (_INT, [_P, ctypes.c_int32, _P, _P, _I64, _P]),
+    "soinfer_gemm_batch_workspace_bytes": (_I64, []),
+    "soinfer_gemm_w4a16_batch": (_INT, [_P, _I64, _I64, _P, _I64, _P]),
     "soinfer_tp_allreduce_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _F32, _P]),
     "soinfer_gemv_w4a16_tp_partial": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     "soinfer_gemv_w4a16_batch_tp": (_INT, [_P, _P, _I64, _P, _I64, _P]),
@@ -933,6 +935,53 @@ def gemm_w4a16(Wq_packed, scale, X, K: int, group_size: int, out: torch.Tensor |
         _call("soinfer_gemm_w4a16", _ptr(Wq_packed), _ptr(scale), _ptr(X), X.stride(0), _ptr(Y), Y.stride(0), M, N,
               K, group_size, scale.size(1), _stream(dev))
     return Y
+
+
+class _GemmTask(ctypes.Structure):
+    _fields_ = [("Wq", _P), ("scale", _P), ("X", _P), ("Y", _P), ("N", _I64), ("K", _I64), ("group_size", _I64),
+                ("num_groups", _I64), ("ldx", _I64), ("ldy", _I64)]
+
+
+class GemmBatch:
+    """A prepared list of independent multi-token INT4 GEMMs run as one
+    launch (soinfer_gemm_w4a16_batch): tasks = sequence of
+    (Wq_packed [N, K/2] uint8, scale [N, G] f32, X [M, K] fp16, Y [M, N] fp16,
+    K, group_size), every X with the same M <= 8 rows.  The tensors must stay
+    alive while the batch is used."""
+
+    def __init__(self, tasks):
+        n = len(tasks)
+        _check(0 < n <= MAX_BATCH_TASKS, "gemm_w4a16_batch: 1 ..", MAX_BATCH_TASKS, " tasks")
+        arr = (_GemmTask * n)()
+        dev, M = None, None
+        for i, (W, scale, X, Y, K, group_size) in enumerate(tasks):
+            name = f"gemm_w4a16_batch[task {i}]"
+            _check(W.is_cuda and W.dtype == torch.uint8 and W.is_contiguous() and W.dim() == 2, name,
+                   "(Wq_packed): must be a contiguous 2D uint8 CUDA tensor")
+            _check(W.size(1) == _cdiv(K, 8) * 4, name, ": Wq_packed.size(1) must be ceil(K/8)*4 for the given K")
+            _f32(scale, name + "(scale)")
+            _check(scale.dim() == 2 and scale.size(0) == W.size(0), name, ": scale must be 2D [N, num_groups]")
+            _check(X.is_cuda and X.dtype == torch.float16 and X.dim() == 2 and X.size(1) == K and X.stride(1) == 1,
+                   name, ": X must be fp16 [M, K] with unit K stride")
+            _check(Y.is_cuda and Y.dtype == torch.float16 and Y.dim() == 2 and Y.size(1) == W.size(0)
+                   and Y.size(0) == X.size(0) and Y.stride(1) == 1, name, ": Y must be fp16 [M, N]")
+            _check(M is None or X.size(0) == M, name, ": every task must have the same M")
+            M = X.size(0)
+            d = _same_device(W, scale, X, Y)
+            _check(dev is None or d == dev, name, ": all tasks must be on one device")
+            dev = d
+            arr[i] = _GemmTask(W.data_ptr(), scale.data_ptr(), X.data_ptr(), Y.data_ptr(), W.size(0), K, group_size,
+                               scale.size(1), X.stride(0), Y.stride(0))
+        _check(1 <= M <= 8, "gemm_w4a16_batch: M must be in [1, 8]")
+        self._arr, self.n, self.m, self.device = arr, n, M, dev
+        self._keep = [tuple(t) for t in tasks]
+
+    def run(self) -> None:
+        dev = self.device
+        with torch.cuda.device(dev):
+            ws = _workspace("gemm_batch", dev, lib().soinfer_gemm_batch_workspace_bytes())
+            _call("soinfer_gemm_w4a16_batch", ctypes.addressof(self._arr), self.n, self.m, ws.data_ptr(), ws.numel(),
+                  _stream(dev))
 
 
 # ------------------------------------------------------------ load-time quantization

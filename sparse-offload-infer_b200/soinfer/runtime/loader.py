@@ -32,6 +32,14 @@ def _load_small(model_dir: str, weight_map: dict[str, str], name: str, device) -
     return t.to(dtype=torch.float16, device=device).contiguous()
 
 
+def _rope_theta(cfg: dict) -> float:
+    """RoPE base from config.json: the top-level rope_theta of older files, or
+    rope_parameters.rope_theta as recent transformers write it."""
+    if "rope_theta" in cfg:
+        return float(cfg["rope_theta"])
+    return float((cfg.get("rope_parameters") or {}).get("rope_theta", 10000.0))
+
+
 def load_streaming_model(model_dir: str, group_size: int = 128, include_dip: bool = False,
                          resident: bool = False, device=None, arena_dir: str | None = None) -> StreamingModel:
     """Quantize every decoder layer's linear weights into a pinned INT4 arena
@@ -72,7 +80,7 @@ def load_streaming_model(model_dir: str, group_size: int = 128, include_dip: boo
         layer_norms=norms, hidden_size=cfg["hidden_size"], num_attention_heads=cfg["num_attention_heads"],
         num_key_value_heads=cfg["num_key_value_heads"],
         head_dim=cfg.get("head_dim", cfg["hidden_size"] // cfg["num_attention_heads"]),
-        rms_norm_eps=cfg["rms_norm_eps"], rope_theta=float(cfg["rope_theta"]), group_size=group_size, resident=res)
+        rms_norm_eps=cfg["rms_norm_eps"], rope_theta=_rope_theta(cfg), group_size=group_size, resident=res)
 
 
 @dataclass(frozen=True)

@@ -32,8 +32,36 @@ def main() -> None:
            "dip": g.generate_dip(model, prompt, n_new, dip_k, max_seq_len=max_seq)}
     caches = [HotCache.build(model, layer, hot) for layer in range(model.num_layers)]
     res["cached_dip"] = g.generate_cached_dip(model, prompt, n_new, dip_k, caches, max_seq_len=max_seq)
+    # teacher-forced logits along the reference's own DIP token sequence
+    # (the loop of generate.teacher_forced_nll:545-582, keeping the logits)
+    seq = res["dip"]
+    pipe = g.WeightPipeline(model)
+    res["tf_dense"] = teacher_forced_logits(
+        g, model, lambda m, li, x, p, kc, vc: g.run_decoder_layer_streaming(pipe, m, li, x, p, kc, vc), seq, max_seq)
+    pipe_d = g.WeightPipeline(model, suffixes=g.DIP_DENSE_SUFFIXES)
+    bufs = g.DipBuffers.make(model, max_k=dip_k)
+    res["tf_dip"] = teacher_forced_logits(
+        g, model, lambda m, li, x, p, kc, vc: g.run_decoder_layer_dip(pipe_d, m, li, x, p, kc, vc, dip_k, bufs), seq,
+        max_seq)
     with open(out, "w") as f:
         json.dump(res, f)
+
+
+def teacher_forced_logits(g, model, layer_fn, token_ids, max_seq_len):
+    import torch
+
+    ops = g.ops
+    shape = (model.num_key_value_heads, max_seq_len, model.head_dim)
+    kcs = [torch.zeros(shape, device="cuda", dtype=torch.float16) for _ in range(model.num_layers)]
+    vcs = [torch.zeros(shape, device="cuda", dtype=torch.float16) for _ in range(model.num_layers)]
+    out = []
+    for pos, tok in enumerate(token_ids[:-1]):
+        x = model.embed_tokens[tok].contiguous()
+        for li in range(model.num_layers):
+            x = layer_fn(model, li, x, pos, kcs[li], vcs[li])
+        xn = ops.rmsnorm(x.unsqueeze(0), model.final_norm, model.rms_norm_eps).squeeze(0).contiguous()
+        out.append(ops.gemv_fp16_v3(model.lm_head, xn).float().cpu().tolist())
+    return out
 
 
 if __name__ == "__main__":

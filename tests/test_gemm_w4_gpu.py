@@ -70,3 +70,42 @@ def test_argument_checks():
         ops.gemm_w4a16(p.to(DEV), s.to(DEV), X.to(DEV), pk, 128)  # 9 tokens
     lib = _C.lib()
     assert lib.soinfer_gemm_w4a16(None, None, None, 256, None, 64, 9, 64, 256, 128, 2, None) == 1
+
+
+@pytest.mark.parametrize("m", [8, 3, 1])
+def test_gemm_batch_streams_many_matrices_in_one_launch(m):
+    """soinfer_gemm_w4a16_batch: 24 independent matrices (configs' gate /
+    down shapes, a ragged N with group size 256, a 14B TP shard) times the
+    same M tokens in one launch of the streaming kernel -- every token row
+    equals the single-matrix GEMM within the GEMV tolerance, four tasks
+    against the float64 oracle, X / Y with strides beyond K / N, and a
+    second launch bit-identical (the work ticket resets itself)."""
+    shapes = [(6144, 2048, 128), (2048, 6144, 128), (1000, 4096, 256), (4352, 5120, 128)]
+    mats = [int4_weights(n, k, g, seed=200 + i) for i, (n, k, g) in enumerate(shapes)]
+    dmats = [(p.to(DEV), s.to(DEV)) for p, s, _ in mats]
+    gen = torch.Generator().manual_seed(m)
+    tasks, hostX = [], []
+    for i in range(24):
+        n, k, g = shapes[i % 4]
+        Xs = torch.randn(m, k + 64, generator=gen).half()
+        hostX.append(Xs[:, :k])
+        X = Xs.to(DEV)[:, :k]
+        Y = torch.full((m, n + 8), 7.0, dtype=torch.float16, device=DEV)[:, :n]
+        tasks.append((dmats[i % 4][0], dmats[i % 4][1], X, Y, k, g))
+    batch = _C.GemmBatch(tasks)
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    first = [t[3].clone() for t in tasks]
+    batch.run()
+    torch.cuda.synchronize()
+    for i, (W, S, X, Y, k, g) in enumerate(tasks):
+        assert torch.equal(Y, first[i]), f"task {i}: second launch differs"
+        single = ops.gemm_w4a16(W, S, X.contiguous(), k, g)
+        for r in range(m):
+            assert_close(Y[r], single[r].double().cpu().numpy(), f"batch task {i} token {r} vs single GEMM")
+    for i in range(4):
+        p, s, pk = mats[i]
+        for r in range(m):
+            ref = port.gemv_w4a16(p.numpy(), s.numpy(), hostX[i][r].numpy(), pk, shapes[i][2])
+            assert_close(tasks[i][3][r], ref, f"batch task {i} token {r} vs oracle")

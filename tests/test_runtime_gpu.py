@@ -128,7 +128,7 @@ def test_cached_dip_bit_identical_to_dip(models, cache_size):
     pa, pb = (gen.WeightPipeline(model, gen.DIP_DENSE_SUFFIXES) for _ in range(2))
     kca, vca = gen._kv_caches(model, 8)
     kcb, vcb = gen._kv_caches(model, 8)
-    miss = torch.zeros(model.num_layers, dtype=torch.int64, device=DEV)
+    miss = torch.zeros(model.num_layers, dtype=torch.int64, device="cuda")
     xa = xb = model.embed_tokens[5]
     for pos in range(3):
         for layer in range(model.num_layers):
