@@ -79,22 +79,39 @@ struct UnpackK {
   }
 };
 
+// D = A * B with a zero accumulator (the first MMA of a chain).
+__device__ __forceinline__ void mma_16816_c0(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // Biased row sums of one 128-K chunk for rows g and g + 8 of a 16-row tile
-// (see gemv_batch.cu): returns E + O / 16 per row.
+// (see gemv_batch.cu): returns E + O / 16 per row.  PAIRED: each 16-byte x
+// fragment holds (x0x1, x4x5, x2x3, x6x7) -- the stage stores x that way --
+// so each MMA's two B registers are adjacent; otherwise (x0x1, x2x3, x4x5,
+// x6x7) as in memory.
+template <bool PAIRED>
 __device__ __forceinline__ void st_chunk_dot(const uint4 wa, const uint4 wb, const uint4 xf[4], const UnpackK& k,
                                              float& s0, float& s1) {
   const uint32_t r0[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t r1[4] = {wb.x, wb.y, wb.z, wb.w};
-  float e[4] = {0.f, 0.f, 0.f, 0.f}, o[4] = {0.f, 0.f, 0.f, 0.f};
+  float e[4], o[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t t0 = r0[j] >> 8, t1 = r1[j] >> 8;
     const uint32_t ae[4] = {lop3_and_xor(r0[j], 0x000f000fu, k.lo), lop3_and_xor(r1[j], 0x000f000fu, k.lo),
                             lop3_and_xor(t0, 0x000f000fu, k.lo), lop3_and_xor(t1, 0x000f000fu, k.lo)};
-    mma_16816(e, ae, xf[j].x, xf[j].z);
+    const uint32_t be0 = xf[j].x, be1 = PAIRED ? xf[j].y : xf[j].z;
+    if (j == 0) mma_16816_c0(e, ae, be0, be1);
+    else mma_16816(e, ae, be0, be1);  // (v0,v1) with x0x1, (v4,v5) with x4x5
     const uint32_t ao[4] = {lop3_and_xor(r0[j], 0x00f000f0u, k.hi), lop3_and_xor(r1[j], 0x00f000f0u, k.hi),
                             lop3_and_xor(t0, 0x00f000f0u, k.hi), lop3_and_xor(t1, 0x00f000f0u, k.hi)};
-    mma_16816(o, ao, xf[j].y, xf[j].w);
+    const uint32_t bo0 = PAIRED ? xf[j].z : xf[j].y, bo1 = xf[j].w;
+    if (j == 0) mma_16816_c0(o, ao, bo0, bo1);
+    else mma_16816(o, ao, bo0, bo1);  // (v2,v3) with x2x3, (v6,v7) with x6x7
   }
   s0 = fmaf(o[0], 0.0625f, e[0]);
   s1 = fmaf(o[2], 0.0625f, e[2]);
@@ -141,11 +158,16 @@ __device__ __forceinline__ void st_chunk_bias_tokens(const uint4 xf[4], float b[
 }
 
 // The chunk's bias 1032 XL + 72 XH (gemv_batch.cu chunk_bias) from this
-// lane's 8 bytes of the chunk's x (bytes 8 * lane .. 8 * lane + 7).
-__device__ __forceinline__ float st_chunk_bias(uint2 xw) {
-  const uint32_t a[4] = {0x64086408u, 0x64086408u, 0x54805480u, 0x54805480u};  // 1032 1032 | 72 72
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
-  mma_16816(d, a, xw.x, xw.y);
+// lane's 8 bytes of the chunk's paired x (stage bytes 8 * lane ..): lanes with
+// even t hold two low-position pairs (x0x1, x4x5 of an 8-group), lanes with
+// odd t two high-position pairs, so the lane's A is 1032 or 72 throughout;
+// column n of D sums 16 of the chunk's 128 values, and the 8 columns are
+// summed across the 4 lanes of a row group.
+__device__ __forceinline__ float st_chunk_bias(uint2 xw, int t) {
+  const uint32_t c = (t & 1) ? 0x54805480u : 0x64086408u;  // 72 | 1032
+  const uint32_t a[4] = {c, c, c, c};
+  float d[4];
+  mma_16816_c0(d, a, xw.x, xw.y);
   float bias = d[0] + d[1];
   bias += __shfl_xor_sync(0xffffffffu, bias, 1);
   bias += __shfl_xor_sync(0xffffffffu, bias, 2);
@@ -233,7 +255,14 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
 #pragma unroll
     for (int r = 0; r < 2 * T; ++r) cpa16(st + L::kW + r * 512 + lane * 16, f.wp[r]);
     if constexpr (MT == 1) {
-      cpa8(st + L::kX + lane * 8 + ((lane >> 4) << 4), f.xp[0]);
+      // paired layout: word i of the chunk (4 bytes) goes to slot i with its
+      // two middle words of every 4 swapped, then the t-piece padding
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = 2 * lane + h;
+        const int b = ((i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1)) * 4;
+        cpa4(st + L::kX + b + ((b >> 7) << 4), f.xp[0] + 2 * h);
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < C::kXP; ++i) {
@@ -296,11 +325,11 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_stream_kernel(const __grid_con
     __syncwarp();  // every lane has read the stage: refill it with the chunk D ahead
     fetch(s);
     if constexpr (MT == 1) {
-      const float bias = st_chunk_bias(xb);
+      const float bias = st_chunk_bias(xb, t);
 #pragma unroll
       for (int tt = 0; tt < T; ++tt) {
         float d0, d1;
-        st_chunk_dot(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
+        st_chunk_dot<true>(w[2 * tt], w[2 * tt + 1], xf, uk, d0, d1);
         acc[2 * tt] = fmaf(sc[2 * tt], d0 - bias, acc[2 * tt]);
         acc[2 * tt + 1] = fmaf(sc[2 * tt + 1], d1 - bias, acc[2 * tt + 1]);
       }

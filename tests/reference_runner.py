@@ -40,9 +40,11 @@ def main() -> None:
         g, model, lambda m, li, x, p, kc, vc: g.run_decoder_layer_streaming(pipe, m, li, x, p, kc, vc), seq, max_seq)
     pipe_d = g.WeightPipeline(model, suffixes=g.DIP_DENSE_SUFFIXES)
     bufs = g.DipBuffers.make(model, max_k=dip_k)
+    sel = [[] for _ in range(model.num_layers)]
     res["tf_dip"] = teacher_forced_logits(
-        g, model, lambda m, li, x, p, kc, vc: g.run_decoder_layer_dip(pipe_d, m, li, x, p, kc, vc, dip_k, bufs), seq,
-        max_seq)
+        g, model, lambda m, li, x, p, kc, vc: g.run_decoder_layer_dip(pipe_d, m, li, x, p, kc, vc, dip_k, bufs,
+                                                                      selected_out=sel), seq, max_seq)
+    res["tf_dip_selected"] = sel
     with open(out, "w") as f:
         json.dump(res, f)
 
