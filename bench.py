@@ -503,6 +503,15 @@ def run_ours(args) -> None:
     del layers
     decode = run_decode(args, device) if args.decode and rank == 0 and world == 1 else None
     decode_tp = run_decode_tp(args, device, world, rank, dist) if args.tp_decode else None
+    nccl_sweep = None
+    if world > 1 and args.nccl_sweep:
+        from soinfer.runtime.tp import PeerExchange, allreduce_sweep
+
+        ex = PeerExchange(device=device)
+        nccl_sweep = allreduce_sweep(device, exchange=ex)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        ex.close()
     decode_int8 = run_decode_int8(args, device) if args.int8_decode and world == 1 else None
     dip_blocks = run_dip_blocks(args, device) if args.dip_blocks and world == 1 else None
     ops_b200 = None
@@ -544,6 +553,7 @@ def run_ours(args) -> None:
                    "gemm_m8": gemm_m8,
                    "decode": decode,
                    "decode_14b_tp": decode_tp,
+                   "allreduce_sweep": nccl_sweep,
                    "decode_14b_int8": decode_int8,
                    "dip_blocks": dip_blocks,
                    "ops_b200": ops_b200,
@@ -1041,6 +1051,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-ops", action="store_true", help="reference arm: skip timing its CUDA ops")
+    ap.add_argument("--nccl-sweep", type=int, default=1,
+                    help="N>1: NCCL all-reduce latency / bus bandwidth sweep (10 KB .. 1 GiB) and the peer exchange")
     ap.add_argument("--ops", type=int, default=1, help="also time this build's hot-path ops (config.ops_b200)")
     ap.add_argument("--decode", type=int, default=1, help="also measure configs[3] decode tok/s (reported in config)")
     ap.add_argument("--decode-tokens", type=int, default=128)

@@ -458,3 +458,63 @@ def graph_decoder_tp(model, plan: ShardPlan, group=None, max_seq_len: int = 2048
 __all__ = ["ShardPlan", "shard_packed", "agree_argmax", "build_tp_model", "PeerExchange", "all_reduce_sum",
            "run_decoder_layer_tp", "run_decoder_layer_dip_tp", "generate_dip_tp", "tp_next_token", "generate_tp",
            "graph_decoder_tp"]
+
+
+ALLREDUCE_SWEEP_BYTES = (10 * 1024, 20 * 1024, 40 * 1024, 80 * 1024, 1 << 20, 16 << 20, 1 << 30)
+
+
+def allreduce_sweep(device, group=None, sizes=ALLREDUCE_SWEEP_BYTES, iters: int = 20, warmup: int = 5,
+                    exchange: "PeerExchange | None" = None) -> list[dict]:
+    """Latency / bandwidth of a sum all-reduce of fp16 buffers of each size
+    in bytes over `group` (torch.distributed; NCCL on GPUs), max over ranks.
+    Per size: mean microseconds per all-reduce and the bus bandwidth
+    (bytes x 2 (world - 1) / world / time, the usual ring-normalised figure).
+    With `exchange`, sizes that fit its slot also time the peer exchange
+    (soinfer_tp_allreduce_add_rmsnorm: push to every rank's inbox over NVLink,
+    flag, sum in rank order) on the same buffer.  Collective: every rank of
+    the group calls it with the same arguments."""
+    import time
+
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    dev = torch.device(device)
+    cuda = dev.type == "cuda"
+    out = []
+
+    def timed(fn, n):
+        if cuda:
+            torch.cuda.synchronize(dev)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(n):
+                fn()
+            e.record()
+            torch.cuda.synchronize(dev)
+            ms = s.elapsed_time(e)
+        else:
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            ms = (time.perf_counter() - t0) * 1e3
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        return float(t.item()) * 1e3 / n  # microseconds per call
+
+    for nbytes in sizes:
+        n = nbytes // 2
+        buf = torch.ones(n, dtype=torch.float16, device=dev)
+        reps = iters if nbytes < (64 << 20) else max(3, iters // 5)
+        for _ in range(warmup):
+            dist.all_reduce(buf, group=group)
+        us = timed(lambda: dist.all_reduce(buf, group=group), reps)
+        row = {"bytes": nbytes, "world": world, "nccl_us": round(us, 2),
+               "nccl_busbw_gbs": round(nbytes * 2 * (world - 1) / world / (us * 1e-6) / 1e9, 3)}
+        if exchange is not None and n % 8 == 0 and nbytes <= exchange.slot_bytes:
+            part = torch.randn(n, device=dev).half()
+            for _ in range(warmup):
+                exchange.allreduce_add_rmsnorm(part)
+            row["exchange_us"] = round(timed(lambda: exchange.allreduce_add_rmsnorm(part), iters), 2)
+        out.append(row)
+        del buf
+    return out

@@ -98,3 +98,26 @@ def test_row_parallel_reduce_and_argmax_agreement_gloo():
     assert all(res[r][0] for r in range(world)), res
     assert res[0][1] == res[1][1] == 7          # tie: the lower global index (rank 0's 7 < 500 + 2)
     assert res[0][2] == res[1][2] == 500 + 2    # rank 1's larger logit wins
+
+
+def _sweep_worker(rank, world, port_no, results):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port_no)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from soinfer.runtime.tp import allreduce_sweep
+
+    rows = allreduce_sweep("cpu", sizes=(1024, 64 * 1024), iters=3, warmup=1)
+    results[rank] = rows
+    dist.destroy_process_group()
+
+
+def test_allreduce_sweep_reports_every_size_on_every_rank():
+    """The all-reduce sweep's host logic on two gloo ranks: one row per size,
+    the same (max-over-ranks) time on both ranks, a positive bus bandwidth."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port_no = s.getsockname()[1]
+    results = mp.Manager().dict()
+    mp.spawn(_sweep_worker, args=(2, port_no, results), nprocs=2, join=True)
+    a, b = results[0], results[1]
+    assert [r["bytes"] for r in a] == [1024, 64 * 1024] and a == b
+    assert all(r["world"] == 2 and r["nccl_us"] > 0 and r["nccl_busbw_gbs"] >= 0 for r in a)
