@@ -20,7 +20,7 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("SOINFER_REF_PYTHON", "/root/reference/python")
+REF = os.environ.get("SOINFER_REF_PYTHON", "")  # the reference checkout's python/ directory (required)
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "hot_cache_golden.json")
 
 
