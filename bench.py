@@ -513,6 +513,7 @@ def run_ours(args) -> None:
         dist.barrier()
         ex.close()
     decode_int8 = run_decode_int8(args, device) if args.int8_decode and world == 1 else None
+    decode_b8 = run_decode_batch8(args, device) if args.batch8_decode and world == 1 else None
     dip_blocks = run_dip_blocks(args, device) if args.dip_blocks and world == 1 else None
     ops_b200 = None
     if args.ops and world == 1:
@@ -555,6 +556,7 @@ def run_ours(args) -> None:
                    "decode_14b_tp": decode_tp,
                    "allreduce_sweep": nccl_sweep,
                    "decode_14b_int8": decode_int8,
+                   "decode_14b_batch8": decode_b8,
                    "dip_blocks": dip_blocks,
                    "ops_b200": ops_b200,
                    "parallelism": f"{world} independent replicas (no collective)"},
@@ -791,6 +793,43 @@ def run_decode(args, device) -> dict:
     del model, streamed
     torch.cuda.empty_cache()
     return out
+
+
+def run_decode_batch8(args, device) -> dict:
+    """configs[4] at batch 8: the Qwen3-14B-shaped INT4 model on one GPU,
+    8 random prompts of args.tp_prompt tokens decoded together, then
+    args.tp_tokens new tokens each (4096 context), one CUDA graph per step
+    (soinfer.runtime.batch.BatchDecoder: multi-token INT4 GEMMs, one attention
+    launch over the 8 stacked caches).  tok/s counts every sequence's tokens."""
+    from soinfer.runtime.batch import BatchDecoder
+    from soinfer.runtime.loader import QWEN3_14B, synthetic_streaming_model
+
+    arch, B = QWEN3_14B, 8
+    model = synthetic_streaming_model(arch, seed=2, resident=True, offload=False, include_dip=False, device=device)
+    g = torch.Generator().manual_seed(3)
+    prompts = torch.randint(0, arch.vocab_size, (B, args.tp_prompt), generator=g).tolist()
+    bd = BatchDecoder(model, B, max_seq_len=4096)
+    bd.generate([p[:8] for p in prompts], 4)  # capture + warm-up
+    tm = {}
+    out = bd.generate(prompts, args.tp_tokens, timings=tm)
+    n = args.tp_tokens - 1
+    weight_bytes = sum(t.numel() for t in model.resident.values()) + sum(
+        m.scale.numel() * m.scale.element_size() for m in model.matrices.values())
+    kv_per_pos = 2 * arch.num_key_value_heads * arch.head_dim * 2 * arch.num_layers
+    step_bytes = weight_bytes + arch.vocab_size * arch.hidden_size * 2 + B * kv_per_pos * (
+        args.tp_prompt + args.tp_tokens / 2)
+    ms_step = tm["decode_ms"] / n
+    del bd, model
+    torch.cuda.empty_cache()
+    return {"model": "Qwen3-14B-shaped, INT4 g128, resident; batch 8", "batch": B, "prompt_tokens": args.tp_prompt,
+            "new_tokens": args.tp_tokens, "tok_s": round(B * n / (tm["decode_ms"] / 1e3), 1),
+            "ms_per_step": round(ms_step, 4), "prefill_ms": round(tm["prefill_ms"], 1),
+            "hbm_bytes_per_step": int(step_bytes),
+            "hbm_floor_ms": round(step_bytes / (measured_peaks().get("hbm_gbs") or 6650.0) / 1e6, 4),
+            "distinct_sequences": len({tuple(o) for o in out}),
+            "step": "one CUDA graph per step: per layer rmsnorm, q/k/v/o/gate/up/down as multi-token INT4 GEMMs "
+                    "(soinfer_gemm_w4a16), one head-norm+RoPE+append and one attention launch for the 8 stacked "
+                    "caches, SwiGLU; fp16 LM head as a cuBLAS GEMM"}
 
 
 def run_decode_tp(args, device, world, rank, dist) -> dict:
@@ -1058,6 +1097,7 @@ def main() -> None:
     ap.add_argument("--decode-tokens", type=int, default=128)
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
     ap.add_argument("--gemm-m8", type=int, default=1, help="also measure the batch-8 GEMM stream (in config)")
+    ap.add_argument("--batch8-decode", type=int, default=1, help="also measure configs[4] batch-8 14B decode (N=1)")
     ap.add_argument("--int8-decode", type=int, default=1, help="also measure the 14B INT8 per-channel decode (N=1)")
     ap.add_argument("--dip-blocks", type=int, default=1, help="also measure configs[1] / configs[2] blocks (N=1)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
