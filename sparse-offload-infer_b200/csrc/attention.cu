@@ -15,6 +15,8 @@
 // A combine kernel rescales and sums the splits in a fixed order.  With a
 // single split the CTA writes the output directly.
 //
+// Each lane keeps kU K (then V) row loads in flight per iteration.
+//
 // Split layout: for the attended length c, want = min(cap, ceil(c/16))
 // splits of L = ceil(c/want) positions (cap: enough CTAs to fill the GPU).
 // Both forms compute it in the kernel from c, so the device-position form
@@ -30,7 +32,8 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr int kMaxSplits = 128;
-constexpr int kTargetCtas = 592;
+constexpr int kTargetCtas = 592;   // 4 CTAs per SM (measured best with kU = 4; 8 per SM slowed short contexts)
+constexpr int kU = 4;              // positions per team per iteration (loads in flight per lane)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Attended length of the device-position form: *pos_dev + 1, clamped to [1, max_seq].
@@ -97,33 +100,37 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
 
-  // phase A: scores (trip count uniform across the warp: the team shuffles
-  // below need every lane)
-  for (int tb = t0; tb < t1; tb += kTeams) {
-    const int t = tb + team;
-    const bool pos_on = t < t1;
-    float kf[8];
-    if (lane_on && pos_on) {
-      const uint4 u = ldg_stream_u4(kb + (int64_t)t * hd + d0);
-      const half2* p = reinterpret_cast<const half2*>(&u);
+  // phase A: scores, kU positions per team per iteration (their K rows loaded
+  // together, so each lane has kU 16-byte loads in flight); the trip count is
+  // uniform across the warp (the team shuffles below need every lane)
+  for (int tb = t0; tb < t1; tb += kTeams * kU) {
+    uint4 ku[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u * kTeams + team;
+      ku[u] = (lane_on && t < t1) ? ldg_stream_u4(kb + (int64_t)t * hd + d0) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u * kTeams + team;
+      const bool pos_on = t < t1;
+      float kf[8];
+      const half2* p = reinterpret_cast<const half2*>(&ku[u]);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __half22float2(p[i]);
         kf[2 * i] = f.x;
         kf[2 * i + 1] = f.y;
       }
-    } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) kf[i] = 0.f;
-    }
+      for (int h = 0; h < REP; ++h) {
+        float dot = 0.f;
 #pragma unroll
-    for (int h = 0; h < REP; ++h) {
-      float dot = 0.f;
+        for (int i = 0; i < 8; ++i) dot = fmaf(qf[h][i], kf[i], dot);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) dot = fmaf(qf[h][i], kf[i], dot);
-#pragma unroll
-      for (int o = TEAM / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      if (tl == 0 && pos_on) s_p[h * L + (t - t0)] = dot * scale_log2;
+        for (int o = TEAM / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (tl == 0 && pos_on) s_p[h * L + (t - t0)] = dot * scale_log2;
+      }
     }
   }
   __syncthreads();
@@ -155,22 +162,32 @@ __global__ void __launch_bounds__(kThreads)
   for (int h = 0; h < REP; ++h)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[h][i] = 0.f;
-  for (int t = t0 + team; t < t1; t += kTeams) {
+  for (int tb = t0 + team; tb < t1; tb += kTeams * kU) {
     if (!lane_on) continue;
-    const uint4 u = ldg_stream_u4(vb + (int64_t)t * hd + d0);
-    const half2* p = reinterpret_cast<const half2*>(&u);
-    float vf[8];
+    uint4 vu[kU];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __half22float2(p[i]);
-      vf[2 * i] = f.x;
-      vf[2 * i + 1] = f.y;
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u * kTeams;
+      vu[u] = t < t1 ? ldg_stream_u4(vb + (int64_t)t * hd + d0) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int h = 0; h < REP; ++h) {
-      const float pr = s_p[h * L + (t - t0)];
+    for (int u = 0; u < kU; ++u) {
+      const int t = tb + u * kTeams;
+      if (t >= t1) break;
+      const half2* p = reinterpret_cast<const half2*>(&vu[u]);
+      float vf[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[h][i] = fmaf(pr, vf[i], acc[h][i]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(p[i]);
+        vf[2 * i] = f.x;
+        vf[2 * i + 1] = f.y;
+      }
+#pragma unroll
+      for (int h = 0; h < REP; ++h) {
+        const float pr = s_p[h * L + (t - t0)];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[h][i] = fmaf(pr, vf[i], acc[h][i]);
+      }
     }
   }
   if (lane_on) {
