@@ -8,14 +8,14 @@ pass over LAYERS distinct layer copies (default 64 -> 128 GEMVs over 858 MB of
 packed weights, far above the 126 MB L2, so no L2 flush is needed) through
 soinfer_gemv_w4a16_batch (independent GEMVs: the streaming kernel,
 gemv_stream.cu); one step = LAUNCHES_PER_STEP (16) such launches back to back,
-so that the default 20 timed steps span ~50 ms.  Weights ~N(0, 0.02)
+so that the default 200 timed steps span ~0.5 s.  Weights ~N(0, 0.02)
 quantized to group-128 INT4 on the GPU with soinfer.quant; x ~N(0, 1) fp16;
 seeded.  `value` = algorithmic bytes (packed weights + fp32 scales + x + y
 per GEMV, 6,701,056 B) of all ranks / max rank time, timed with CUDA events.
 The GEMVs of a launch are independent (every x is ready); the same stream
 with each down_proj reading its gate_proj output (a dependency inside the
-launch: the persistent batched kernel, gemv_batch.cu) is reported as
-config.chained_gate_down.
+launch: the streaming kernel numbers every gate unit first and a down unit
+starts once its gate is stored) is reported as config.chained_gate_down.
 
 `e2e`: the same chain through the public streaming API (WeightPipeline: packed
 weights streamed from the pinned host arena by the copy engine, double
@@ -550,7 +550,8 @@ def run_ours(args) -> None:
                    "l2": "inputs larger than L2 (weights far above the 126 MB L2), no flush",
                    "chained_gate_down": {"value": round(chained_gbs, 2), "unit": UNIT, "launches": csteps,
                                          "note": "each down_proj reads its gate_proj output (in-kernel dependency; "
-                                                 "persistent batched kernel gemv_batch_kernel)"},
+                                                 "streaming kernel: gate units first, each down unit waits for its "
+                                                 "gate's completion count)"},
                    "gemm_m8": gemm_m8,
                    "decode": decode,
                    "decode_14b_tp": decode_tp,

@@ -94,6 +94,8 @@ int soinfer_device_errors(int* flags) {
   *flags |= f;
   if (int st = cuda_result(read_and_clear_gemm_w4_error(&f), "device_errors")) return st;
   *flags |= f;
+  if (int st = cuda_result(read_and_clear_gemv_stream_error(&f), "device_errors")) return st;
+  *flags |= f;
   return SOINFER_OK;
 }
 
@@ -102,14 +104,23 @@ int64_t soinfer_gemv_batch_workspace_bytes(int64_t num_tasks) {
   return gemv_batch_workspace_bytes(num_tasks);
 }
 
-// The streaming kernel serves a batch of plain, independent GEMVs (no dep, no
-// epilogue or prologue, no x / y overlap between tasks) that is large enough
-// to give every warp of the GPU at least two units.
+// True if task a waits, directly or through a chain of deps, for task b.
+static bool waits_for(const soinfer_gemv_task* tasks, int64_t a, int64_t b) {
+  for (int64_t d = tasks[a].dep; d >= 0; d = tasks[d].dep)
+    if (d == b) return true;
+  return false;
+}
+
+// The streaming kernel serves a batch of plain GEMVs (no epilogue or
+// prologue; a task may wait for an earlier one) that is large enough to give
+// every warp of the GPU at least two units.  A task's x may overlap another
+// task's y, and two tasks' y may overlap, only when one of the two waits for
+// the other (read after write, write after read, write after write).
 static bool stream_eligible(const soinfer_gemv_task* tasks, int64_t n, int sms) {
   int64_t units = 0;
   for (int64_t i = 0; i < n; ++i) {
     const soinfer_gemv_task& t = tasks[i];
-    if (t.dep >= 0 || t.residual || t.glu_gate || t.norm_weight || !t.y || !aligned(t.x, 8)) return false;
+    if (t.residual || t.glu_gate || t.norm_weight || !t.y || !aligned(t.x, 8)) return false;
     units += cdiv(t.N, 16 * kStreamTiles);
   }
   if (units < 2LL * sms * kStreamWarps) return false;
@@ -117,10 +128,11 @@ static bool stream_eligible(const soinfer_gemv_task* tasks, int64_t n, int sms) 
     const uintptr_t ylo = reinterpret_cast<uintptr_t>(tasks[i].y), yhi = ylo + 2 * tasks[i].N;
     for (int64_t j = 0; j < n; ++j) {
       const uintptr_t xlo = reinterpret_cast<uintptr_t>(tasks[j].x), xhi = xlo + 2 * tasks[j].K;
-      if (xlo < yhi && ylo < xhi) return false;
+      if (xlo < yhi && ylo < xhi && !(j != i && (waits_for(tasks, j, i) || waits_for(tasks, i, j)))) return false;
       if (j != i) {
         const uintptr_t zlo = reinterpret_cast<uintptr_t>(tasks[j].y), zhi = zlo + 2 * tasks[j].N;
-        if (zlo < yhi && ylo < zhi) return false;  // two tasks writing the same rows: keep task order
+        // two tasks writing the same rows: only when one waits for the other
+        if (zlo < yhi && ylo < zhi && !(waits_for(tasks, j, i) || waits_for(tasks, i, j))) return false;
       }
     }
   }
@@ -180,11 +192,13 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
     for (int64_t i = 0; i < num_tasks; ++i) {
       const soinfer_gemv_task& t = tasks[i];
       S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.x), as_half(t.y), (int)t.N, (int)t.K,
-                                  (int)t.num_groups, (int)(t.group_size / 128), (int)t.K, (int)t.N, 0};
+                                  (int)t.num_groups, (int)(t.group_size / 128), (int)t.K, (int)t.N, (int)t.dep,
+                                  0, 0, 0};
     }
     if (plan_gemv_stream(S, sms)) {
-      REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
-              "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes());
+      const int64_t need = gemv_stream_workspace_bytes(num_tasks);
+      REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 4),
+              "%s: workspace too small (need %lld zeroed bytes)", name, (long long)need);
       return cuda_result(launch_gemv_stream(S, reinterpret_cast<int*>(workspace), st), name);
     }
   }
@@ -255,7 +269,7 @@ static int gemv_batch_common(const char* name, const PeerSet* peers, const soinf
   return SOINFER_OK;
 }
 
-int64_t soinfer_gemm_batch_workspace_bytes(void) { return gemv_stream_workspace_bytes(); }
+int64_t soinfer_gemm_batch_workspace_bytes(void) { return gemv_stream_workspace_bytes(0); }
 
 int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, int64_t M, void* workspace,
                              int64_t workspace_bytes, void* stream) {
@@ -282,13 +296,13 @@ int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, 
       return set_error(SOINFER_ERR_UNSUPPORTED, "%s: needs K and group_size multiples of 128, 16-byte aligned "
                        "Wq and X rows, 4-byte aligned scales", tn);
     S.tasks[i] = GemvStreamTask{t.Wq, t.scale, as_half(t.X), as_half(t.Y), (int)t.N, (int)t.K, (int)t.num_groups,
-                                (int)(t.group_size / 128), (int)t.ldx, (int)t.ldy, 0};
+                                (int)(t.group_size / 128), (int)t.ldx, (int)t.ldy, -1, 0, 0, 0};
   }
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   REQUIRE(plan_gemv_stream(S, sms), "%s: batch too large", name);
-  REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes() && aligned(workspace, 4),
-          "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes());
+  REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes(0) && aligned(workspace, 4),
+          "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes(0));
   return cuda_result(launch_gemv_stream(S, reinterpret_cast<int*>(workspace), as_stream(stream)), name);
 }
 

@@ -753,7 +753,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-int64_t gemv_batch_workspace_bytes(int64_t num_tasks) { return ((num_tasks + 1) * 4 + 255) / 256 * 256; }
+// Also large enough for the streaming kernel's counters (gemv_stream_workspace_bytes),
+// which the same batch entry point may choose.
+int64_t gemv_batch_workspace_bytes(int64_t num_tasks) { return ((num_tasks + 2) * 4 + 255) / 256 * 256; }
 
 bool plan_gemv_batch(GemvBatchParams& B, int sms) {
   int max_k = 0;

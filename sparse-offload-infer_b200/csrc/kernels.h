@@ -123,8 +123,10 @@ bool plan_gemv_batch(GemvBatchParams& B, int sms);
 cudaError_t launch_gemv_batch(const GemvBatchParams& B, int* counters, cudaStream_t stream);
 cudaError_t read_and_clear_gemv_batch_error(int* out);
 
-// Streaming INT4 GEMV over independent tasks (gemv_stream.cu): no task reads
-// another task's output, no epilogue, K and group size multiples of 128.
+// Streaming INT4 GEMV over a list of tasks (gemv_stream.cu): no epilogue, K
+// and group size multiples of 128; a task may wait for an earlier one (dep:
+// its x is that task's y), in which case its units start once every unit of
+// that task is stored.
 struct GemvStreamTask {
   const uint8_t* W;
   const float* S;
@@ -132,7 +134,10 @@ struct GemvStreamTask {
   half* y;        // [m, N], row stride ldy
   int N, K, G, cpg;
   int ldx, ldy;   // token strides in elements (multi-token form)
+  int dep;        // index of the task this one waits for, or -1 (caller order; plan_gemv_stream remaps it)
   int ubegin;     // filled by plan_gemv_stream: first unit of the task
+  int dneed;      // filled by plan_gemv_stream: units of the dep task (its completion count)
+  int publish;    // filled by plan_gemv_stream: 1 if another task waits for this one
 };
 template <int MaxTasks>
 struct GemvStreamParamsT {
@@ -153,11 +158,14 @@ using GemvStreamParams = GemvStreamParamsT<kMaxBatchTasks>;
 constexpr int kStreamTiles = SOINFER_STREAM_TILES;    // 16-row tiles per unit
 constexpr int kStreamStages = SOINFER_STREAM_STAGES;  // chunks in flight per warp
 constexpr int kStreamWarps = SOINFER_STREAM_WARPS;    // warps per CTA (one CTA per SM)
-// Zeroed workspace bytes (a unit ticket and an exit count; left zeroed on return).
-int64_t gemv_stream_workspace_bytes();
-// Orders the tasks (decreasing K) and fills the unit offsets; false if the shape is not served.
+// Zeroed workspace bytes for num_tasks tasks (a unit ticket, an exit count and
+// one completion count per task; left zeroed on return).
+int64_t gemv_stream_workspace_bytes(int64_t num_tasks);
+// Orders the tasks (dependency level, then decreasing K), fills the unit
+// offsets and remaps dep to the new order; false if the shape is not served.
 bool plan_gemv_stream(GemvStreamParams& B, int sms);
 cudaError_t launch_gemv_stream(const GemvStreamParams& B, int* ctr, cudaStream_t stream);
+cudaError_t read_and_clear_gemv_stream_error(int* out);
 
 // INT8 GEMV (per-tensor / per-channel / grouped scales).
 cudaError_t launch_gemv_w8(const int8_t* Wq, const float* scale, const half* x, half* y, int64_t N,

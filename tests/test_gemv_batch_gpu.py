@@ -43,7 +43,7 @@ def test_independent_tasks_match_oracle(shapes):
 
 def test_large_independent_batch_takes_the_stream_kernel():
     """A batch of plain, independent GEMVs large enough for the streaming
-    kernel (gemv_stream.cu: one warp per 32-row unit over the full K, units
+    kernel (gemv_stream.cu: one warp per 48-row unit over the full K, units
     handed out by a ticket): 40 tasks over four matrices -- the configs[0]
     gate and down shapes, a ragged N and a group size of 256 -- every task
     against the single-GEMV op, three of them against the float64 oracle, and
@@ -75,6 +75,66 @@ def test_large_independent_batch_takes_the_stream_kernel():
         p, s, pk = mats[i % 4]
         ref = port.gemv_w4a16(p.numpy(), s.numpy(), xs[i].numpy(), pk, shapes[i % 4][2])
         assert_close(tasks[i][3], ref, f"stream task {i} vs oracle")
+
+
+def _kernel_names(fn):
+    """Names of the CUDA kernels fn launches (CUPTI through torch.profiler)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+def test_chained_large_batch_takes_the_stream_kernel():
+    """Dependent tasks on the streaming kernel: 30 gate -> down chains (each
+    down reads its gate's output: the planner numbers every gate unit before
+    any down unit, a waiting warp leaves bubbles instead of blocking), one
+    chain extended by a third task that writes in place over the first gate's
+    output after the down has read it (write after read / write after write,
+    allowed because it waits for both).  Every output against the same chain
+    run as ordered single-GEMV ops, the launch seen to be gemv_stream_kernel,
+    two launches bit-identical and the workspace's counters zero afterwards."""
+    shapes = [(6144, 2048), (2048, 6144)]
+    mats = [int4_weights(n, k, 128, seed=300 + i) for i, (n, k) in enumerate(shapes)]
+    (gw, gs), (dw, ds) = [(p.to(DEV), s.to(DEV)) for p, s, _ in mats]
+    tasks, xs, gates, downs = [], [], [], []
+    for c in range(30):
+        x = fp16_randn(2048, 400 + c).to(DEV)
+        a = torch.empty(6144, dtype=torch.float16, device=DEV)
+        b = torch.empty(2048, dtype=torch.float16, device=DEV)
+        xs.append(x)
+        gates.append(len(tasks))
+        tasks.append((gw, gs, x, a, 2048, 128, -1))
+        downs.append(len(tasks))
+        tasks.append((dw, ds, a, b, 6144, 128, len(tasks) - 1))
+    a0, b0 = tasks[gates[0]][3], tasks[downs[0]][3]
+    tasks.append((gw, gs, b0, a0, 2048, 128, downs[0]))  # b0 -> a0, in place over gate 0's output
+    batch = _C.GemvBatch(tasks)
+    names = _kernel_names(batch.run)
+    assert any("gemv_stream_kernel" in n for n in names), sorted(names)
+    assert _C.device_errors() == 0
+    first = [t[3].clone() for t in tasks]
+    for t in tasks:
+        t[3].fill_(0)
+    batch.run()
+    torch.cuda.synchronize()
+    assert _C.device_errors() == 0
+    for i, t in enumerate(tasks):
+        assert torch.equal(t[3], first[i]), f"task {i}: second launch differs"
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ws = _C._workspaces[("batch", dev.index, _C._stream(dev))]
+    assert int(ws.count_nonzero()) == 0, "stream counters not reset"
+    for c in range(30):
+        a_ref = ops.gemv_w4a16_group_lop3(gw, gs, xs[c], 2048, 128)
+        b_ref = ops.gemv_w4a16_group_lop3(dw, ds, a_ref, 6144, 128)
+        if c > 0:
+            assert_close(tasks[gates[c]][3], a_ref.double().cpu().numpy(), f"chain {c} gate")
+        assert_close(tasks[downs[c]][3], b_ref.double().cpu().numpy(), f"chain {c} down")
+        if c == 0:
+            a2_ref = ops.gemv_w4a16_group_lop3(gw, gs, b_ref, 2048, 128)
+            assert_close(a0, a2_ref.double().cpu().numpy(), "chain 0 third task (in place)")
 
 
 def test_mixed_item_sizes_share_the_ring():
