@@ -55,6 +55,16 @@
 // CTA to finish, so a zeroed workspace stays reusable across launches and
 // CUDA-graph replays; after a reported error the caller re-zeroes it.
 //
+// Launch overlap: a batch without a peer task is launched as a programmatic
+// dependent of the kernel before it, so its CTAs start (and the producer
+// streams weights, which no earlier kernel writes) while that kernel is still
+// finishing; the x loader and the epilogue warp -- the only roles that read
+// an earlier kernel's output (x, residual) or write memory another kernel may
+// still read (y, norm_out, the workspace counters) -- wait for the earlier
+// grid first (griddepcontrol.wait).  The last counter update follows a CTA
+// barrier behind both.  A peer batch keeps the cooperative launch: its CTA 0
+// reads the exchange epoch at entry.
+//
 // Reference semantics per task: csrc/kernels/gemv_w4a16_group.cu:77-127 of
 // sparse-offload-infer.
 #include "common.cuh"
@@ -535,6 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp) {
     producer_loop(B, cta, lane, ring, full, empty, item_off, abort_flag);
   } else if (warp == kLoaderWarp) {
+    pdl_wait();  // x (and the dependency counters) come from earlier kernels
     // ------------------------------------------------------------ x loader
     int a = 0;  // index among this CTA's active (rows > 0) tasks
     bool stop = false;
@@ -616,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (stop) raise_abort(abort_flag);
     asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into this CTA's shared memory outlives it
   } else if (warp == kEpilogueWarp) {
+    pdl_wait();  // residual inputs from earlier kernels; y may alias a buffer they read
     epilogue_loop(B, cta, lane, red, rfull, rempty, s_inbox, counters, abort_flag);
   } else {
     // ------------------------------------------------------------ consumers
@@ -836,8 +848,16 @@ cudaError_t launch_params(const Params& B, int* counters, cudaStream_t stream) {
   cfg.dynamicSmemBytes = (size_t)B.smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: they wait on each other's counters
-  at[0].val.cooperative = 1;
+  if (B.peers.world > 0) {
+    at[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: they wait on each other's counters
+    at[0].val.cooperative = 1;
+  } else {
+    // one CTA per SM and grid = SM count: every CTA becomes resident once the
+    // earlier kernel drains, before any dependency wait (those follow the
+    // grid wait), so the CTAs still meet; start them early to overlap it
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, B, counters);
