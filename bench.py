@@ -746,6 +746,19 @@ def run_decode(args, device) -> dict:
         out[name] = {"tok_s": round(n / (tm["decode_ms"] / 1e3), 1), "ms_per_token": round(tm["decode_ms"] / n, 4),
                      "prefill_ms": round(tm["prefill_ms"], 2)}
         del gd
+    # the dense step as one cooperative kernel for all layers (same bits, same tokens)
+    gd = gen.GraphDecoder(model, max_seq_len=2048, fused=True)
+    gd.generate(prompt, 4)
+    tm = {}
+    ids_f = gd.generate(prompt, n_new, timings=tm)
+    n = n_new - 1
+    out["dense_fused"] = {"tok_s": round(n / (tm["decode_ms"] / 1e3), 1), "ms_per_token": round(tm["decode_ms"] / n, 4),
+                          "prefill_ms": round(tm["prefill_ms"], 2), "tokens_equal_dense": ids_f == toks["dense"],
+                          "note": "one CUDA graph per token whose decoder layers are ONE cooperative kernel "
+                                  "(soinfer_decode_layers_fused: grid barriers between phases, each phase's weights "
+                                  "bulk-copied into shared memory a phase ahead)"}
+    assert ids_f == toks["dense"], "fused decode tokens differ from the per-kernel step's"
+    del gd
     # cache-aware DIP: 20% hot cache resident, misses from the pinned arena
     hot = zipf_hot_set(arch.intermediate_size, 0.2)
     caches = [HotCache.build(model, li, hot) for li in range(arch.num_layers)]

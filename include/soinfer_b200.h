@@ -451,6 +451,47 @@ int64_t soinfer_gemm_batch_workspace_bytes(void);
 int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, int64_t M, void* workspace,
                              int64_t workspace_bytes, void* stream);
 
+/* One decoder layer of soinfer_decode_layers_fused: the packed INT4 weights
+ * (group size 128, scales [N, K/128]) of q, k, v, o, gate, up, down in that
+ * order, the four RMSNorm weights and the layer's KV cache
+ * ([num_kv_heads, max_seq, 128] fp16 each). */
+typedef struct soinfer_fused_layer {
+  const uint8_t* Wq[7];
+  const float* scale[7];
+  const soinfer_half* input_norm;
+  const soinfer_half* post_norm;
+  const soinfer_half* q_norm;
+  const soinfer_half* k_norm;
+  soinfer_half* k_cache;
+  soinfer_half* v_cache;
+} soinfer_fused_layer;
+
+/* Bytes of device workspace soinfer_decode_layers_fused needs (its first 256
+ * bytes must be zero on the first call; every call leaves them zero). */
+int64_t soinfer_decode_fused_workspace_bytes(int64_t hidden, int64_t intermediate, int64_t num_heads,
+                                             int64_t num_kv_heads, int64_t head_dim);
+
+/* Every decoder layer of one batch-1 decode step in ONE cooperative launch
+ * (no reference counterpart: the reference runs the layer as separate kernels,
+ * python/soinfer/runtime/generate.py:141-182, dense streaming layer).  x
+ * [hidden] holds the step's input embedding and receives the last layer's
+ * output; the token's position is read from pos_dev (device int32) when the
+ * kernel runs (CUDA-graph capturable); each layer appends its K / V row at
+ * that position.  Per layer: RMSNorm -> q/k/v -> q/k head norm + RoPE (tables
+ * [max_seq, 64] fp32) -> GQA attention -> o + residual -> RMSNorm -> gate/up
+ * -> SwiGLU -> down + residual, bit-identical to the per-kernel path
+ * (soinfer_gemv_w4a16_batch with its prologue / epilogues,
+ * soinfer_head_norm_rope, soinfer_decode_attention_at).  Needs head_dim 128,
+ * num_heads / num_kv_heads in {1, 2, 4}, hidden and intermediate multiples of
+ * 128, group size 128, at most 64 layers, 16-byte aligned weight rows;
+ * otherwise SOINFER_ERR_UNSUPPORTED.  Grid barriers are bounded (1 s): a wait
+ * that runs out sets a soinfer_device_errors bit. */
+int soinfer_decode_layers_fused(const soinfer_fused_layer* layers, int64_t num_layers, int64_t hidden,
+                                int64_t intermediate, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                int64_t group_size, int64_t max_seq, float eps, const float* cos_table,
+                                const float* sin_table, const int32_t* pos_dev, soinfer_half* x, void* workspace,
+                                int64_t workspace_bytes, void* stream);
+
 /* Load-time INT4 quantization + packing on the GPU (reference
  * python/soinfer/quant/formats.py:77-110 with calibrate.min_max:22-27 and
  * quant/pack.py:31-69): w [N, K] with row stride ld (dtype 0 fp32, 1 fp16,

@@ -96,6 +96,8 @@ int soinfer_device_errors(int* flags) {
   *flags |= f;
   if (int st = cuda_result(read_and_clear_gemv_stream_error(&f), "device_errors")) return st;
   *flags |= f;
+  if (int st = cuda_result(read_and_clear_decode_fused_error(&f), "device_errors")) return st;
+  *flags |= f;
   return SOINFER_OK;
 }
 
@@ -304,6 +306,75 @@ int soinfer_gemm_w4a16_batch(const soinfer_gemm_task* tasks, int64_t num_tasks, 
   REQUIRE(workspace && workspace_bytes >= gemv_stream_workspace_bytes(0) && aligned(workspace, 4),
           "%s: workspace too small (need %lld zeroed bytes)", name, (long long)gemv_stream_workspace_bytes(0));
   return cuda_result(launch_gemv_stream(S, reinterpret_cast<int*>(workspace), as_stream(stream)), name);
+}
+
+int64_t soinfer_decode_fused_workspace_bytes(int64_t hidden, int64_t intermediate, int64_t num_heads,
+                                             int64_t num_kv_heads, int64_t head_dim) {
+  if (hidden < 1 || intermediate < 1 || num_heads < 1 || num_kv_heads < 1 || head_dim < 1) return 0;
+  return decode_fused_workspace_bytes(hidden, intermediate, num_heads, num_kv_heads, head_dim);
+}
+
+int soinfer_decode_layers_fused(const soinfer_fused_layer* layers, int64_t num_layers, int64_t hidden,
+                                int64_t intermediate, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                int64_t group_size, int64_t max_seq, float eps, const float* cos_table,
+                                const float* sin_table, const int32_t* pos_dev, soinfer_half* x, void* workspace,
+                                int64_t workspace_bytes, void* stream) {
+  const char* name = "decode_layers_fused";
+  REQUIRE(layers && x && pos_dev && cos_table && sin_table && workspace, "%s: null pointer", name);
+  REQUIRE(num_layers >= 1 && hidden >= 1 && intermediate >= 1 && num_heads >= 1 && num_kv_heads >= 1 &&
+              max_seq >= 1 && max_seq < (1 << 30),
+          "%s: sizes must be positive", name);
+  if (num_layers > kFusedMaxLayers || head_dim != 128 || group_size != 128 || num_heads % num_kv_heads != 0 ||
+      hidden % 128 != 0 || intermediate % 128 != 0 || hidden > (1 << 20) || intermediate > (1 << 20) ||
+      num_heads > 1024)
+    return set_error(SOINFER_ERR_UNSUPPORTED, "%s: needs head_dim 128, group size 128, hidden / intermediate "
+                     "multiples of 128, num_heads a multiple of num_kv_heads, <= %d layers", name, kFusedMaxLayers);
+  REQUIRE(aligned(x, 16) && aligned(workspace, 256), "%s: x 16-byte and workspace 256-byte aligned", name);
+  static FusedDecodeParams P;  // ~10 KB: not on the stack
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  P.layers = (int)num_layers;
+  P.H = (int)hidden;
+  P.I = (int)intermediate;
+  P.NQ = (int)num_heads;
+  P.NKV = (int)num_kv_heads;
+  P.HD = (int)head_dim;
+  P.max_seq = max_seq;
+  P.eps = eps;
+  P.cos_t = cos_table;
+  P.sin_t = sin_table;
+  P.pos = pos_dev;
+  P.x = as_half(x);
+  for (int64_t i = 0; i < num_layers; ++i) {
+    const soinfer_fused_layer& l = layers[i];
+    FusedLayer& d = P.layer[i];
+    for (int m = 0; m < 7; ++m) {
+      REQUIRE(l.Wq[m] && l.scale[m], "%s[layer %lld]: null weight", name, (long long)i);
+      if (!aligned(l.Wq[m], 16) || !aligned(l.scale[m], 16))
+        return set_error(SOINFER_ERR_UNSUPPORTED, "%s[layer %lld]: weight rows and scales must be 16-byte aligned",
+                         name, (long long)i);
+      d.w[m] = l.Wq[m];
+      d.s[m] = l.scale[m];
+    }
+    REQUIRE(l.input_norm && l.post_norm && l.q_norm && l.k_norm && l.k_cache && l.v_cache,
+            "%s[layer %lld]: null norm weight or cache", name, (long long)i);
+    REQUIRE(aligned(l.input_norm, 16) && aligned(l.post_norm, 16) && aligned(l.k_cache, 16) && aligned(l.v_cache, 16),
+            "%s[layer %lld]: norm weights and caches must be 16-byte aligned", name, (long long)i);
+    d.in_norm = as_half(l.input_norm);
+    d.post_norm = as_half(l.post_norm);
+    d.q_norm = as_half(l.q_norm);
+    d.k_norm = as_half(l.k_norm);
+    d.kc = as_half(l.k_cache);
+    d.vc = as_half(l.v_cache);
+  }
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t need = decode_fused_workspace_bytes(hidden, intermediate, num_heads, num_kv_heads, head_dim);
+  REQUIRE(workspace_bytes >= need, "%s: workspace too small (need %lld bytes)", name, (long long)need);
+  if (!plan_decode_fused(P, workspace, workspace_bytes, sms))
+    return set_error(SOINFER_ERR_UNSUPPORTED, "%s: shape not served by the fused step (num_heads / num_kv_heads "
+                     "in {1, 2, 4}, at most %d tiles per SM per phase, shared memory)", name, 16);
+  return cuda_result(launch_decode_fused(P, sms, as_stream(stream)), name);
 }
 
 int soinfer_gemv_w4a16_batch(const soinfer_gemv_task* tasks, int64_t num_tasks, void* workspace,

@@ -254,4 +254,41 @@ cudaError_t launch_decode_attention(const half* q, const half* kc, const half* v
                                     int64_t nkv, int64_t max_seq, int64_t hd, int64_t cur_len, void* workspace,
                                     cudaStream_t stream);
 
+// Fused dense decode step (decode_fused.cu): every decoder layer of a batch-1
+// Qwen3-style model with HBM-resident INT4 weights (group size 128) in one
+// cooperative launch, phases separated by grid barriers.
+constexpr int kFusedMaxLayers = 64;
+struct FusedLayer {
+  const uint8_t* w[7];  // packed rows of q, k, v, o, gate, up, down
+  const float* s[7];    // their scales [N, K / 128]
+  const half* in_norm;
+  const half* post_norm;
+  const half* q_norm;
+  const half* k_norm;
+  half* kc;             // [NKV, max_seq, HD]
+  half* vc;
+};
+struct FusedDecodeParams {
+  int layers, H, I, NQ, NKV, HD;
+  int cap;    // attention splits per kv head at most (the split kernel's layout)
+  int lmax;   // score-row stride: positions per split at most
+  int64_t max_seq;
+  float eps, scale_log2;
+  const float* cos_t;  // [max_seq, HD / 2]
+  const float* sin_t;
+  const int32_t* pos;  // the token's position (device)
+  half* x;             // [H] hidden state: layer 0's input, the last layer's output
+  half *q, *k, *v, *attn, *h2, *hid;  // scratch activations
+  float* ws_acc;       // [NQ, 128 splits, HD]
+  float* ws_ml;        // [NQ, 128 splits, 2]
+  int* bar;            // [0] barrier arrivals, [1] exit count: zeroed, left zeroed
+  FusedLayer layer[kFusedMaxLayers];
+};
+// Workspace bytes for the fused step (barrier words + activations + attention partials).
+int64_t decode_fused_workspace_bytes(int64_t H, int64_t I, int64_t NQ, int64_t NKV, int64_t HD);
+// Fills the scratch pointers of P from the workspace; checks the shapes; false if not served.
+bool plan_decode_fused(FusedDecodeParams& P, void* workspace, int64_t workspace_bytes, int sms);
+cudaError_t launch_decode_fused(const FusedDecodeParams& P, int sms, cudaStream_t stream);
+cudaError_t read_and_clear_decode_fused_error(int* out);
+
 }  // namespace soinfer

@@ -79,6 +79,9 @@ _SIGNATURES = {
     "soinfer_peer_buffer_reset": (_INT, [_P, _P]),
     "soinfer_gather_rows_device_multi": (_INT, [_P, ctypes.c_int32, _P, _P, _I64, _P]),
     "soinfer_gemm_batch_workspace_bytes": (_I64, []),
+    "soinfer_decode_fused_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64, _I64]),
+    "soinfer_decode_layers_fused": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _F32, _P, _P, _P, _P,
+                                           _P, _I64, _P]),
     "soinfer_gemm_w4a16_batch": (_INT, [_P, _I64, _I64, _P, _I64, _P]),
     "soinfer_tp_allreduce_add_rmsnorm": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _F32, _P]),
     "soinfer_gemv_w4a16_tp_partial": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
@@ -982,6 +985,63 @@ class GemmBatch:
             ws = _workspace("gemm_batch", dev, lib().soinfer_gemm_batch_workspace_bytes())
             _call("soinfer_gemm_w4a16_batch", ctypes.addressof(self._arr), self.n, self.m, ws.data_ptr(), ws.numel(),
                   _stream(dev))
+
+
+class _FusedLayer(ctypes.Structure):
+    _fields_ = [("Wq", _P * 7), ("scale", _P * 7), ("input_norm", _P), ("post_norm", _P), ("q_norm", _P),
+                ("k_norm", _P), ("k_cache", _P), ("v_cache", _P)]
+
+
+class FusedDecode:
+    """Every decoder layer of a batch-1 decode step in one cooperative launch
+    (soinfer_decode_layers_fused).  layers = sequence of dicts with
+    "w" (7 packed INT4 weights: q, k, v, o, gate, up, down; group size 128),
+    "s" (their fp32 scales), "input_norm", "post_norm", "q_norm", "k_norm"
+    (fp16) and "k_cache" / "v_cache" (fp16 [num_kv_heads, max_seq, 128]).
+    run(x, pos_dev) transforms the hidden state x [hidden] in place (the
+    input embedding in, the last layer's output out) at the position held in
+    pos_dev (int32 [1] CUDA).  The tensors must stay alive while it is used."""
+
+    def __init__(self, layers, hidden: int, intermediate: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                 max_seq: int, eps: float, cos_table, sin_table, group_size: int = 128):
+        name = "decode_layers_fused"
+        n = len(layers)
+        _check(n >= 1, name, ": at least one layer")
+        arr = (_FusedLayer * n)()
+        dev = None
+        for i, ly in enumerate(layers):
+            _check(len(ly["w"]) == 7 and len(ly["s"]) == 7, name, ": seven weights per layer")
+            for w, sc in zip(ly["w"], ly["s"]):
+                _check(w.is_cuda and w.dtype == torch.uint8 and w.is_contiguous(), name, ": weights: contiguous uint8 CUDA")
+                _f32(sc, name + "(scale)")
+                dev = dev or w.device
+            for key in ("input_norm", "post_norm", "q_norm", "k_norm", "k_cache", "v_cache"):
+                _f16(ly[key], f"{name}({key})")
+            _check(ly["k_cache"].is_contiguous() and ly["v_cache"].is_contiguous(), name, ": caches must be contiguous")
+            arr[i] = _FusedLayer((_P * 7)(*[w.data_ptr() for w in ly["w"]]), (_P * 7)(*[sc.data_ptr() for sc in ly["s"]]),
+                                 ly["input_norm"].data_ptr(), ly["post_norm"].data_ptr(), ly["q_norm"].data_ptr(),
+                                 ly["k_norm"].data_ptr(), ly["k_cache"].data_ptr(), ly["v_cache"].data_ptr())
+        _check(cos_table.is_cuda and cos_table.dtype == torch.float32 and sin_table.dtype == torch.float32, name,
+               ": cos / sin tables must be fp32 CUDA")
+        self._arr, self.n, self.device = arr, n, dev
+        self.shape = (hidden, intermediate, num_heads, num_kv_heads, head_dim, group_size, max_seq)
+        self.eps = float(eps)
+        self._keep = (list(layers), cos_table, sin_table)
+        self.ws_bytes = lib().soinfer_decode_fused_workspace_bytes(hidden, intermediate, num_heads, num_kv_heads,
+                                                                   head_dim)
+
+    def run(self, x, pos_dev) -> None:
+        H, I, NQ, NKV, HD, G, S = self.shape
+        _f16(x, "decode_layers_fused(x)")
+        _check(x.numel() == H and x.is_contiguous(), "decode_layers_fused", ": x must be contiguous [hidden]")
+        _check_cuda(pos_dev, "decode_layers_fused(pos_dev)", torch.int32, ": must be int32")
+        dev = self.device
+        cos_table, sin_table = self._keep[1], self._keep[2]
+        with torch.cuda.device(dev):
+            ws = _workspace("fused_decode", dev, self.ws_bytes)
+            _call("soinfer_decode_layers_fused", ctypes.addressof(self._arr), self.n, H, I, NQ, NKV, HD, G, S,
+                  self.eps, cos_table.data_ptr(), sin_table.data_ptr(), pos_dev.data_ptr(), x.data_ptr(),
+                  ws.data_ptr(), ws.numel(), _stream(dev))
 
 
 # ------------------------------------------------------------ load-time quantization

@@ -585,13 +585,15 @@ class GraphDecoder:
     generate_dip on the same model (same kernels, same order)."""
 
     def __init__(self, model: StreamingModel, dip_k: int | None = None, max_seq_len: int = 2048, layer_fn=None,
-                 token_fn=None, caches: list[HotCache] | None = None):
+                 token_fn=None, caches: list[HotCache] | None = None, fused: bool = False):
         """layer_fn(pipeline, model, layer_idx, x, where, k_cache, v_cache) -> x and
         token_fn(model, xn) -> int32 [1] replace the dense / DIP layer and the
         fused LM-head argmax (tensor parallelism plugs in here).  caches (with
         dip_k): cache-aware DIP -- up_proj / down_proj_T may stay in the pinned
         arena (misses read zero-copy by the device gather); the per-layer miss
-        counts accumulate in self.miss_counts."""
+        counts accumulate in self.miss_counts.  fused (dense INT4, group size
+        128): every decoder layer of the step runs in one cooperative kernel
+        (soinfer_decode_layers_fused) -- same bits, same tokens."""
         if caches is not None and dip_k is None:
             raise ValueError("GraphDecoder: caches need dip_k (cache-aware DIP)")
         streamed_ok = ("mlp.up_proj.weight", "mlp.down_proj.weight") if caches is not None else ()
@@ -618,11 +620,32 @@ class GraphDecoder:
         self.bufs = DipBuffers.make(model, dip_k) if dip_k is not None else None
         self.graph = None
         self.layer_fn, self.token_fn = layer_fn, token_fn or _next_token
+        self.fused = None
+        if fused:
+            if dip_k is not None or layer_fn is not None or caches is not None:
+                raise ValueError("GraphDecoder: fused runs the dense layer only")
+            if model.group_size != 128 or any(model.matrices[n].bits != 4 for n in names):
+                raise ValueError("GraphDecoder: fused needs INT4 weights with group size 128")
+            layers = []
+            for li in range(model.num_layers):
+                mats = [model.matrices[f"model.layers.{li}.{s}"] for s in LINEAR_SUFFIXES]
+                norms = model.layer_norms[li]
+                layers.append({"w": [model.resident[f"model.layers.{li}.{s}"] for s in LINEAR_SUFFIXES],
+                               "s": [m.scale.contiguous() for m in mats],
+                               "input_norm": norms["input_layernorm"], "post_norm": norms["post_attention_layernorm"],
+                               "q_norm": norms["q_norm"], "k_norm": norms["k_norm"],
+                               "k_cache": self.k_caches[li], "v_cache": self.v_caches[li]})
+            inter = model.matrices["model.layers.0.mlp.gate_proj.weight"].n
+            self.fused = _C.FusedDecode(layers, model.hidden_size, inter, model.num_attention_heads,
+                                        model.num_key_value_heads, model.head_dim, max_seq_len, model.rms_norm_eps,
+                                        cos_t, sin_t)
 
     def _step(self) -> None:
         m, where = self.model, self.where
         x = m.embed_tokens.index_select(0, self.ids.index_select(0, self.pos.long()).long()).view(-1)
-        for li in range(m.num_layers):
+        if self.fused is not None:
+            self.fused.run(x, self.pos)
+        for li in range(m.num_layers if self.fused is None else 0):
             if self.layer_fn is not None:
                 x = self.layer_fn(self.pipeline, m, li, x, where, self.k_caches[li], self.v_caches[li])
             elif self.dip_k is None:
