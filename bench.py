@@ -1093,6 +1093,53 @@ def run_decode_int8(args, device) -> dict:
             "hbm_floor_ms": round(floor_bytes / (measured_peaks().get("hbm_gbs") or 6650.0) / 1e6, 4)}
 
 
+def decode_trace(args) -> None:
+    """--decode-trace: where one graph-replayed decode step's time goes
+    (Qwen3-1.7B-shaped, resident INT4, 70-token prompt then 40 tokens):
+    CUPTI kernel records of 5 replays (torch.profiler), per kernel name its
+    launches, mean duration and its increment of the step's end time (kernels
+    launched as programmatic dependents overlap, so durations overstate);
+    for the per-kernel, fused and DIP steps.  Prints a table; no JSON line."""
+    from torch.profiler import ProfilerActivity, profile
+
+    from soinfer.runtime import generate as gen
+    from soinfer.runtime.loader import QWEN3_1_7B, synthetic_streaming_model
+
+    device = torch.device("cuda", 0)
+    model = synthetic_streaming_model(QWEN3_1_7B, seed=1, resident=True, offload=False, include_dip=True,
+                                      device=device)
+    prompt = torch.randint(0, QWEN3_1_7B.vocab_size, (70,), generator=torch.Generator().manual_seed(0)).tolist()
+    for name, dip_k, fused in (("per-kernel dense", None, False), ("fused dense", None, True),
+                               ("per-kernel DIP k/I=0.5", 3072, False)):
+        gd = gen.GraphDecoder(model, dip_k=dip_k, max_seq_len=2048, fused=fused)
+        tm = {}
+        gd.generate(prompt, 40, timings=tm)
+        reps = 5
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            with torch.cuda.stream(gd.stream):
+                for _ in range(reps):
+                    gd.graph.replay()
+            torch.cuda.synchronize(device)
+        ev = sorted((e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA),
+                    key=lambda e: e.time_range.start)
+        span = (ev[-1].time_range.end - ev[0].time_range.start) / reps
+        agg, prev_end = {}, ev[0].time_range.start
+        for e in ev:
+            k = e.name.replace("(anonymous namespace)::", "").replace("void ", "").replace("soinfer::", "")
+            k = k.split("(")[0][:56]
+            a = agg.setdefault(k, [0, 0.0, 0.0])
+            a[0] += 1
+            a[1] += e.time_range.elapsed_us()
+            a[2] += max(0.0, e.time_range.end - prev_end)
+            prev_end = max(prev_end, e.time_range.end)
+        print(f"== {name}: {tm['decode_ms'] / 39:.4f} ms/token (CUDA events); traced {span:.1f} us/step, "
+              f"{len(ev) // reps} kernels/step")
+        print(f"   {'increment us/step':>18s} {'launches/step':>14s} {'mean us':>8s}  kernel")
+        for k, (n, t, c) in sorted(agg.items(), key=lambda kv: -kv[1][2])[:10]:
+            print(f"   {c / reps:18.1f} {n // reps:14d} {t / n:8.2f}  {k}")
+        del gd
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1112,12 +1159,16 @@ def main() -> None:
     ap.add_argument("--tp-decode", type=int, default=1, help="also measure configs[4] 14B TP decode (in config)")
     ap.add_argument("--gemm-m8", type=int, default=1, help="also measure the batch-8 GEMM stream (in config)")
     ap.add_argument("--batch8-decode", type=int, default=1, help="also measure configs[4] batch-8 14B decode (N=1)")
+    ap.add_argument("--decode-trace", action="store_true", help="print where a 1.7B decode step's time goes and exit")
     ap.add_argument("--int8-decode", type=int, default=1, help="also measure the 14B INT8 per-channel decode (N=1)")
     ap.add_argument("--dip-blocks", type=int, default=1, help="also measure configs[1] / configs[2] blocks (N=1)")
     ap.add_argument("--tp-prompt", type=int, default=3840)
     ap.add_argument("--tp-tokens", type=int, default=256)
     ap.add_argument("--tp-nccl", type=int, default=0, help="TP collectives through NCCL instead of the peer exchange")
     args = ap.parse_args()
+    if args.decode_trace:
+        decode_trace(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
