@@ -418,9 +418,11 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
  * reference GEMV applied to M tokens): Y[m, 0:N] = dequant(W) X[m, 0:K] for
  * m < M <= 8, X fp16 with row stride ldx, Y fp16 with row stride ldy, the
  * weights / scales of soinfer_gemv_w4a16_group.  One pass over the weights:
- * the tensor-core MMA's 8 columns carry the M tokens.  Shapes outside the
- * one-pass kernel (K or group size not multiples of 128, scale rows not
- * 16-byte multiples, M*K*2 > 112 KiB) run the single-token GEMV per row. */
+ * the tensor-core MMA's 8 columns carry the M tokens (a long K whose X does
+ * not fit in shared memory is staged K-segment by K-segment, same sums).
+ * Shapes outside the one-pass kernel (K or group size not multiples of 128,
+ * scale rows not 16-byte multiples, more shared memory than an SM has) run
+ * the single-token GEMV per row. */
 int soinfer_gemm_w4a16(const uint8_t* Wq_packed, const float* scale, const soinfer_half* X, int64_t ldx,
                        soinfer_half* Y, int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size,
                        int64_t num_groups, void* stream);

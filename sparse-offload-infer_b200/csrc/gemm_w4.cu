@@ -14,7 +14,11 @@
 // output rows; warp 0 streams 16-row x 24-chunk pieces of it into a ring of
 // shared-memory stages with cp.async.bulk (one copy per row piece, mbarrier
 // per stage, bounded waits); X [M, K] and the slab's scale rows are staged
-// once in shared memory; the 16 warps split each piece's 128-K chunks, unpack
+// once in shared memory (long K, where X [M, K] does not fit: the pieces run
+// K-segment by K-segment over the slab's tiles, X is staged one segment at a
+// time and each warp keeps its per-tile partial rows in shared memory between
+// segments -- the same per-warp accumulation order, so the same bits); the
+// 16 warps split each piece's 128-K chunks, unpack
 // each packed word to exact fp16 values (LOP3 + one half2 op per pair) and
 // run two MMA chains; at each tile's end the per-warp partials [16 rows x 8
 // tokens] are summed in warp order (deterministic) and written.
@@ -37,7 +41,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 
 struct GemmPlan {
   int rows_per_cta, chunks, piece_chunks, pieces, stages, cpg, G, slot_stride;
-  int m;  // tokens
+  int m;    // tokens
+  int seg;  // 1: K-segment-major order, X staged one piece's chunks at a time
   int smem_x, smem_scale, smem_stage, smem_red, smem_total;
 };
 
@@ -99,9 +104,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   pdl_launch_dependents();
 
+  // stage s -> (tile, piece): tile-major, or K-segment-major for long K
+  auto coords = [&](int s, int& tile, int& piece) {
+    if (p.seg) {
+      piece = s / n_tiles;
+      tile = s - piece * n_tiles;
+    } else {
+      tile = s / p.pieces;
+      piece = s - tile * p.pieces;
+    }
+  };
   auto issue = [&](int s) {  // warp 0: lane r < 16 copies row r of stage s's piece
     const int slot = s % p.stages;
-    const int tile = s / p.pieces, piece = s - tile * p.pieces;
+    int tile, piece;
+    coords(s, tile, piece);
     const int c0 = piece * p.piece_chunks;
     const int pc = min(p.piece_chunks, p.chunks - c0);
     const int valid = min(16, rows_here - tile * 16);
@@ -120,13 +136,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < first; ++s) issue(s);
   }
   pdl_wait();  // X may come from the previous kernel
-  {
-    const int k16 = K / 8;
+  // X chunks [c0, c0 + nc) of every token into shared memory (token stride xk16 uint4)
+  const int xk16 = p.seg ? p.piece_chunks * 16 : K / 8;
+  auto load_x = [&](int c0, int nc) {
+    const int k16 = nc * 16;
     for (int i = tid; i < p.m * k16; i += kThreads) {
       const int m = i / k16, q = i - m * k16;
-      xs[m * k16 + x_slot(q)] = __ldcg(reinterpret_cast<const uint4*>(X + m * ldx) + q);
+      xs[m * xk16 + x_slot(q)] = __ldcg(reinterpret_cast<const uint4*>(X + m * ldx) + c0 * 16 + q);
     }
-  }
+  };
+  if (!p.seg) load_x(0, p.chunks);
   if (total == 0) return;
   const bool scales_ok = mbar_wait_bounded(scale_bar, 0, kWaitNs);
   if (__syncthreads_or(!scales_ok)) {
@@ -136,11 +155,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   // this lane's token (columns past M read token 0; their outputs are dropped)
-  const uint4* xtok = xs + (g < p.m ? g : 0) * (K / 8);
+  const uint4* xtok = xs + (g < p.m ? g : 0) * xk16;
   const int lr0 = g, lr1 = g + 8;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int s = 0; s < total; ++s) {
     const int slot = s % p.stages;
+    int tile, piece;
+    coords(s, tile, piece);
+    if (p.seg && tile == 0) {  // a new K segment: its X (every warp is done with the previous one)
+      __syncthreads();
+      load_x(piece * p.piece_chunks, min(p.piece_chunks, p.chunks - piece * p.piece_chunks));
+      __syncthreads();
+    }
     const bool ok = mbar_wait_bounded(&bars[slot], (uint32_t)((s / p.stages) & 1), kWaitNs);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) atomicOr(&g_gemm_w4_error, kErrCopyTimeout);
@@ -148,7 +174,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         (void)mbar_wait_bounded(&bars[q % p.stages], (uint32_t)((q / p.stages) & 1), kWaitNs / 4);
       return;
     }
-    const int tile = s / p.pieces, piece = s - tile * p.pieces;
     const int c0 = piece * p.piece_chunks;
     const int pc = min(p.piece_chunks, p.chunks - c0);
     const uint8_t* sb = stage_base + slot * slot_bytes;
@@ -159,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint4 wb = *reinterpret_cast<const uint4*>(sb + lr1 * p.slot_stride + c * 64 + t * 16);
       const int cg = c0 + c;
       uint4 xf[4];
-      const uint4* xc = xtok + cg * 16 + t * 4;
+      const uint4* xc = xtok + (p.seg ? c : cg) * 16 + t * 4;
 #pragma unroll
       for (int j = 0; j < 4; ++j) xf[j] = xc[j ^ ((t >> 1) & 1)];
       float d[4];
@@ -172,8 +197,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc[3] = fmaf(s1, d[3], acc[3]);
     }
     const bool tile_end = (piece == p.pieces - 1);
-    if (tile_end) {
-      float* rw = red + warp * (16 * kTokens);
+    // this warp's partial rows of the tile: written at the tile's end, or (long
+    // K) carried across segments in the tile's own region (same sums, in order)
+    float* tred = red + (p.seg ? tile * (kWarps * 16 * kTokens) : 0);
+    if (p.seg || tile_end) {
+      float* rw = tred + warp * (16 * kTokens);
+      if (p.seg && piece > 0) {
+        acc[0] += rw[lr0 * kTokens + 2 * t];
+        acc[1] += rw[lr0 * kTokens + 2 * t + 1];
+        acc[2] += rw[lr1 * kTokens + 2 * t];
+        acc[3] += rw[lr1 * kTokens + 2 * t + 1];
+      }
       rw[lr0 * kTokens + 2 * t] = acc[0];
       rw[lr0 * kTokens + 2 * t + 1] = acc[1];
       rw[lr1 * kTokens + 2 * t] = acc[2];
@@ -187,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (m < p.m && lr < rows_here) {
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) sum += red[w * (16 * kTokens) + r * kTokens + m];
+        for (int w = 0; w < kWarps; ++w) sum += tred[w * (16 * kTokens) + r * kTokens + m];
         Y[m * ldy + row_begin + lr] = __float2half_rn(sum);
       }
     }
@@ -195,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       issue(s + p.stages);
     }
-    if (tile_end) __syncthreads();  // partials read before the next tile overwrites them
+    if (tile_end && !p.seg) __syncthreads();  // partials read before the next tile overwrites them
   }
 }
 
@@ -209,7 +243,7 @@ int sms_now() {
 
 bool plan_gemm_w4(int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t G) {
   return M >= 1 && M <= kTokens && K % 128 == 0 && group_size % 128 == 0 && (G * 4) % 16 == 0 &&
-         N >= 1 && N < (1ll << 31) && M * K * 2 <= 112 * 1024;
+         N >= 1 && N < (1ll << 31) && K < (1 << 24);
 }
 
 cudaError_t launch_gemm_w4(const uint8_t* W, const float* S, const half* X, int64_t ldx, half* Y, int64_t ldy,
@@ -227,10 +261,11 @@ cudaError_t launch_gemm_w4(const uint8_t* W, const float* S, const half* X, int6
   p.pieces = (p.chunks + p.piece_chunks - 1) / p.piece_chunks;
   p.slot_stride = p.piece_chunks * 64 + kSlotPad;
   p.stages = kStages;
-  p.smem_x = (int)(M * K * 2);
+  p.seg = M * K * 2 > 112 * 1024 ? 1 : 0;
+  p.smem_x = p.seg ? (int)(M * p.piece_chunks * 256) : (int)(M * K * 2);
   p.smem_scale = (int)(((int64_t)p.rows_per_cta * G * 4 + 127) / 128 * 128);
   p.smem_stage = p.stages * 16 * p.slot_stride;
-  p.smem_red = kWarps * 16 * kTokens * 4;
+  p.smem_red = (p.seg ? (p.rows_per_cta + 15) / 16 : 1) * kWarps * 16 * kTokens * 4;
   p.smem_total = p.smem_x + p.smem_scale + p.smem_stage + p.smem_red;
   if (p.smem_total > 226 * 1024) return cudaErrorNotSupported;
   if (cudaError_t e = ensure_smem_attr<gemm_w4_kernel>(p.smem_total); e != cudaSuccess) return e;

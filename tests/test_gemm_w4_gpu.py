@@ -25,7 +25,7 @@ def _case(n, k, g, m, seed):
 
 @pytest.mark.parametrize("n,k,g", [(6144, 2048, 128), (2048, 6144, 128), (3072, 2048, 128), (17408, 5120, 128),
                                    (5120, 2560, 128), (4352, 5120, 128), (1024, 4096, 256), (33, 256, 128),
-                                   (5120, 17408, 128), (40, 300, 32)])
+                                   (5120, 17408, 128), (40, 300, 32), (1024, 20480, 256), (33, 19200, 128)])
 @pytest.mark.parametrize("m", [1, 3, 8])
 def test_tokens_match_oracle(n, k, g, m):
     p, s, pk, X = _case(n, k, g, m, seed=n + k + m)
