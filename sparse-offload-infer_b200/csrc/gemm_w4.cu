@@ -269,8 +269,10 @@ cudaError_t launch_gemm_w4(const uint8_t* W, const float* S, const half* X, int6
   p.smem_total = p.smem_x + p.smem_scale + p.smem_stage + p.smem_red;
   if (p.smem_total > 226 * 1024) return cudaErrorNotSupported;
   if (cudaError_t e = ensure_smem_attr<gemm_w4_kernel>(p.smem_total); e != cudaSuccess) return e;
-  gemm_w4_kernel<<<grid, kThreads, p.smem_total, stream>>>(W, S, X, ldx, Y, ldy, (int)N, (int)K, p);
-  return cudaGetLastError();
+  // a programmatic dependent of the previous kernel: the weight copies and
+  // scale rows start while it drains; X is read after griddepcontrol.wait
+  return launch_ex(gemm_w4_kernel, dim3(grid), dim3(kThreads), (size_t)p.smem_total, stream, 1, true, W, S, X, ldx,
+                   Y, ldy, (int)N, (int)K, p);
 }
 
 cudaError_t read_and_clear_gemm_w4_error(int* out) {
