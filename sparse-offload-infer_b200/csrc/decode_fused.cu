@@ -284,27 +284,34 @@ __host__ __device__ __forceinline__ int split_want(int c, int cap) {
 // One head row: RMSNorm with the head norm weights (rounded to fp16), then
 // RoPE at the position (cos / sin rows cv / sv) -- glue.cu head_norm_rope's
 // per-warp arithmetic; src read from L2 (written earlier in this launch).
+// Every load the row needs is issued first (one round trip), then the math.
 __device__ __forceinline__ void head_norm_rope_row(const half* src, const half* w, const float* cv, const float* sv,
                                                    half* dst, float eps, int lane, half* dst2 = nullptr) {
   constexpr int half_dim = kHD / 2;
-  float ss = 0.f;
-  for (int i = lane; i < kHD; i += 32) {
-    const float f = __half2float(ld_cg_half(src + i));
-    ss = fmaf(f, f, ss);
+  float xv[4], wv[4], cs[2], sn[2];
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    xv[n] = __half2float(ld_cg_half(src + lane + 32 * n));
+    wv[n] = __half2float(w[lane + 32 * n]);
   }
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+    cs[n] = cv[lane + 32 * n];
+    sn[n] = sv[lane + 32 * n];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) ss = fmaf(xv[n], xv[n], ss);
   ss = warp_sum(ss);
   const float inv = rsqrtf(ss / (float)kHD + eps);
-  float x1[2], x2[2];
-  int n = 0;
-  for (int i = lane; i < half_dim; i += 32, ++n) {
-    x1[n] = __half2float(__float2half_rn(__half2float(ld_cg_half(src + i)) * inv * __half2float(w[i])));
-    x2[n] = __half2float(
-        __float2half_rn(__half2float(ld_cg_half(src + i + half_dim)) * inv * __half2float(w[i + half_dim])));
-  }
-  n = 0;
-  for (int i = lane; i < half_dim; i += 32, ++n) {
-    const float c = cv[i], sn = sv[i];
-    const half lo = __float2half_rn(x1[n] * c - x2[n] * sn), hi = __float2half_rn(x2[n] * c + x1[n] * sn);
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {  // pairs (i, i + 64), i = lane + 32 n
+    // explicit roundings (no contraction): the same bits as glue.cu's kernel
+    const float x1 = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(xv[n], inv), wv[n])));
+    const float x2 = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(xv[n + 2], inv), wv[n + 2])));
+    const half lo = __float2half_rn(__fsub_rn(__fmul_rn(x1, cs[n]), __fmul_rn(x2, sn[n])));
+    const half hi = __float2half_rn(__fadd_rn(__fmul_rn(x2, cs[n]), __fmul_rn(x1, sn[n])));
+    const int i = lane + 32 * n;
     dst[i] = lo;
     dst[i + half_dim] = hi;
     if (dst2 != nullptr) {
@@ -357,10 +364,11 @@ __device__ void attn_unit(const FusedDecodeParams& P, const FusedLayer& Ly, int 
   for (int h = gwarp; h < REP; h += kAttnThreads / 32)
     head_norm_rope_row(P.q + (int64_t)(qh0 + h) * kHD, Ly.q_norm, cv, sv, s_q + h * kHD, P.eps, lane);
   if (split == nsplit - 1) {  // this unit attends to the new position: append its K / V row first
-    if (gwarp == 0) {
+    // on warps without a q row when there are any (REP < 4), so the rows run side by side
+    if (gwarp == REP % 4) {
       head_norm_rope_row(P.k + (int64_t)kvh * kHD, Ly.k_norm, cv, sv, Ly.kc + ((int64_t)kvh * P.max_seq + pos) * kHD,
                          P.eps, lane, s_kv);
-    } else if (gwarp == 1) {
+    } else if (gwarp == (REP + 1) % 4) {
       for (int i = lane; i < kHD; i += 32) {
         const half v = ld_cg_half(P.v + (int64_t)kvh * kHD + i);
         Ly.vc[((int64_t)kvh * P.max_seq + pos) * kHD + i] = v;

@@ -135,15 +135,17 @@ __global__ void __launch_bounds__(kHeadRowsPerBlock * 32)
   float x1[4], x2[4];
   int n = 0;
   for (int i = lane; i < half_dim; i += 32, ++n) {
-    x1[n] = __half2float(__float2half_rn(__half2float(src[i]) * inv * __half2float(w[i])));
-    x2[n] = __half2float(__float2half_rn(__half2float(src[i + half_dim]) * inv * __half2float(w[i + half_dim])));
+    x1[n] = __half2float(__float2half_rn(__fmul_rn(__fmul_rn(__half2float(src[i]), inv), __half2float(w[i]))));
+    x2[n] = __half2float(
+        __float2half_rn(__fmul_rn(__fmul_rn(__half2float(src[i + half_dim]), inv), __half2float(w[i + half_dim]))));
   }
   __syncwarp();  // every lane has read its q values before any lane rewrites q in place
   n = 0;
   for (int i = lane; i < half_dim; i += 32, ++n) {
     const float c = cv[i], s = sv[i];
-    dst[i] = __float2half_rn(x1[n] * c - x2[n] * s);
-    dst[i + half_dim] = __float2half_rn(x2[n] * c + x1[n] * s);
+    // explicit roundings (no contraction), so every kernel that rotates a head row gets the same bits
+    dst[i] = __float2half_rn(__fsub_rn(__fmul_rn(x1[n], c), __fmul_rn(x2[n], s)));
+    dst[i + half_dim] = __float2half_rn(__fadd_rn(__fmul_rn(x2[n], c), __fmul_rn(x1[n], s)));
   }
 }
 

@@ -61,7 +61,7 @@ __device__ __forceinline__ float warp_rmsnorm_inv(const uint4* x, int n16, int K
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 f = __half22float2(h[j]);
-      ss += f.x * f.x + f.y * f.y;
+      ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));  // no contraction: same bits everywhere
     }
   }
 #pragma unroll
