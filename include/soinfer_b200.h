@@ -414,6 +414,20 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                                 const int32_t* pos_dev, void* workspace, int64_t workspace_bytes,
                                 void* stream);
 
+/* The graph decode step's token bookkeeping on the device (no reference
+ * counterpart: the reference embeds and appends the token on the host,
+ * python/soinfer/runtime/generate.py:446-458).  embed: x [hidden] =
+ * embed[ids[*pos_dev]] (fp16 [vocab, hidden]); a position outside
+ * [0, ids_len) or a token id outside [0, vocab) writes nothing.  advance: once
+ * the step's token is in *next (int32, e.g. the LM head's argmax),
+ * ids[*pos_dev + 1] = *next unless *pos_dev + 1 < *prompt_len (a prompt token
+ * stays), then *pos_dev += 1; nothing when *pos_dev + 1 is outside
+ * [0, ids_len). */
+int soinfer_decode_step_embed(const soinfer_half* embed, int64_t vocab, int64_t hidden, const int32_t* ids,
+                              int64_t ids_len, const int32_t* pos_dev, soinfer_half* x, void* stream);
+int soinfer_decode_step_advance(int32_t* ids, int64_t ids_len, int32_t* pos_dev, const int32_t* prompt_len,
+                                const int32_t* next, void* stream);
+
 /* Multi-token INT4 GEMM for batched decode (no reference counterpart; the
  * reference GEMV applied to M tokens): Y[m, 0:N] = dequant(W) X[m, 0:K] for
  * m < M <= 8, X fp16 with row stride ldx, Y fp16 with row stride ldy, the

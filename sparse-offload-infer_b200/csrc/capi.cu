@@ -851,6 +851,24 @@ int soinfer_decode_attention_at(const soinfer_half* q, const soinfer_half* k_cac
                      name);
 }
 
+int soinfer_decode_step_embed(const soinfer_half* embed, int64_t vocab, int64_t hidden, const int32_t* ids,
+                              int64_t ids_len, const int32_t* pos_dev, soinfer_half* x, void* stream) {
+  const char* name = "decode_step_embed";
+  REQUIRE(vocab >= 1 && hidden >= 1 && ids_len >= 1 && hidden < (1ll << 31), "%s: invalid sizes", name);
+  REQUIRE(embed && ids && pos_dev && x, "%s: null pointer", name);
+  return cuda_result(launch_step_embed(as_half(embed), vocab, hidden, ids, ids_len, pos_dev, as_half(x),
+                                       as_stream(stream)),
+                     name);
+}
+
+int soinfer_decode_step_advance(int32_t* ids, int64_t ids_len, int32_t* pos_dev, const int32_t* prompt_len,
+                                const int32_t* next, void* stream) {
+  const char* name = "decode_step_advance";
+  REQUIRE(ids_len >= 1, "%s: ids_len must be >= 1", name);
+  REQUIRE(ids && pos_dev && prompt_len && next, "%s: null pointer", name);
+  return cuda_result(launch_step_advance(ids, ids_len, pos_dev, prompt_len, next, as_stream(stream)), name);
+}
+
 int soinfer_gemm_w4a16(const uint8_t* Wq, const float* scale, const soinfer_half* X, int64_t ldx, soinfer_half* Y,
                        int64_t ldy, int64_t M, int64_t N, int64_t K, int64_t group_size, int64_t num_groups,
                        void* stream) {

@@ -15,9 +15,10 @@
 // Why: in the per-kernel decode step each launch pays the launch, the first
 // weight fetch from HBM and the drain of its tail, and a 1.7B-class layer's
 // kernels move only a few MB each, so launch latency -- not bandwidth -- set
-// the step time.  Here the weights of the coming phases are prefetched into
-// L2 (cp.async.bulk.prefetch.L2) a phase or more ahead, so a phase reads its
-// weights from L2 and costs a barrier plus one on-chip round trip.
+// the step time.  Here each CTA bulk-copies its tiles of the coming GEMV phase
+// (cp.async.bulk into one of two shared-memory weight buffers, completing on
+// an mbarrier) a phase or more ahead, so a phase finds its weights on chip
+// and costs a barrier plus one round trip for its input vector.
 //
 // Arithmetic: every value equals the per-kernel path's (gemv_batch.cu with
 // its RMSNorm prologue and SwiGLU / residual epilogues, glue.cu's head norm +

@@ -192,6 +192,43 @@ __global__ void kv_append_kernel(half* __restrict__ kc, half* __restrict__ vc, c
   }
 }
 
+// The graph decode step's input row: x = embed[ids[*pos_dev]] (fp16 [vocab, H]),
+// the position and the token id read when the kernel runs; an out-of-range
+// position or id writes nothing.  VEC16: 16-byte pieces.
+template <bool VEC16>
+__global__ void step_embed_kernel(const half* __restrict__ embed, const int64_t vocab, const int64_t H,
+                                  const int32_t* __restrict__ ids, const int64_t ids_len,
+                                  const int32_t* __restrict__ pos_dev, half* __restrict__ x) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t pos = *pos_dev;
+  if (pos < 0 || pos >= ids_len) return;
+  const int64_t id = ids[pos];
+  if (id < 0 || id >= vocab) return;
+  const int64_t n = VEC16 ? H / 8 : H;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (VEC16)
+      reinterpret_cast<uint4*>(x)[i] = reinterpret_cast<const uint4*>(embed + id * H)[i];
+    else
+      x[i] = embed[id * H + i];
+  }
+}
+
+// Advances the graph decode step's device state once the step's token is in
+// *next: ids[pos + 1] = *next unless pos + 1 is still a prompt position
+// (< *prompt_len, the prompt's token stays), then pos += 1.  Nothing when
+// pos + 1 is outside [0, ids_len).
+__global__ void step_advance_kernel(int32_t* __restrict__ ids, const int64_t ids_len, int32_t* __restrict__ pos_dev,
+                                    const int32_t* __restrict__ prompt_len, const int32_t* __restrict__ next) {
+  pdl_launch_dependents();
+  pdl_wait();
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int64_t p = *pos_dev;
+  if (p < 0 || p + 1 >= ids_len) return;
+  if (p + 1 >= *prompt_len) ids[p + 1] = *next;
+  *pos_dev = (int32_t)(p + 1);
+}
+
 template <bool VEC16>
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ matrix, const int64_t num_rows, const int64_t row_nbytes,
                                    const int32_t* __restrict__ rows, const int64_t k, uint8_t* __restrict__ dst) {
@@ -331,6 +368,25 @@ cudaError_t launch_kv_append_at(half* kc, half* vc, const half* kn, const half* 
   int threads = hd < 32 ? 32 : (hd > 256 ? 256 : (int)hd);
   return launch_ex(kv_append_kernel, dim3((unsigned)nkv), dim3(threads), 0, stream, 1, kPdl, kc, vc, kn, vn, max_seq,
                    hd, (int64_t)0, pos_dev);
+}
+
+cudaError_t launch_step_embed(const half* embed, int64_t vocab, int64_t H, const int32_t* ids, int64_t ids_len,
+                              const int32_t* pos_dev, half* x, cudaStream_t stream) {
+  const bool vec = H % 8 == 0 && ((reinterpret_cast<uintptr_t>(embed) | reinterpret_cast<uintptr_t>(x)) & 15u) == 0;
+  const int64_t n = vec ? H / 8 : H;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 64) blocks = 64;
+  if (vec)
+    return launch_ex(step_embed_kernel<true>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, kPdl, embed, vocab, H,
+                     ids, ids_len, pos_dev, x);
+  return launch_ex(step_embed_kernel<false>, dim3((unsigned)blocks), dim3(256), 0, stream, 1, kPdl, embed, vocab, H,
+                   ids, ids_len, pos_dev, x);
+}
+
+cudaError_t launch_step_advance(int32_t* ids, int64_t ids_len, int32_t* pos_dev, const int32_t* prompt_len,
+                                const int32_t* next, cudaStream_t stream) {
+  return launch_ex(step_advance_kernel, dim3(1), dim3(32), 0, stream, 1, kPdl, ids, ids_len, pos_dev, prompt_len,
+                   next);
 }
 
 cudaError_t launch_gather_rows_device(const uint8_t* matrix, int64_t num_rows, int64_t row_nbytes,

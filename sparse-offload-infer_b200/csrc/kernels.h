@@ -246,6 +246,11 @@ cudaError_t launch_rope_at(half* x, const float* cos_table, const float* sin_tab
                            int64_t head_dim, const int32_t* pos_dev, cudaStream_t stream);
 cudaError_t launch_kv_append_at(half* kc, half* vc, const half* kn, const half* vn, int64_t nkv, int64_t max_seq,
                                 int64_t hd, const int32_t* pos_dev, cudaStream_t stream);
+// The graph decode step's embedding lookup and state advance (glue.cu).
+cudaError_t launch_step_embed(const half* embed, int64_t vocab, int64_t H, const int32_t* ids, int64_t ids_len,
+                              const int32_t* pos_dev, half* x, cudaStream_t stream);
+cudaError_t launch_step_advance(int32_t* ids, int64_t ids_len, int32_t* pos_dev, const int32_t* prompt_len,
+                                const int32_t* next, cudaStream_t stream);
 int64_t attention_workspace_bytes(int64_t nq, int64_t max_seq, int64_t hd);
 cudaError_t launch_decode_attention_at(const half* q, const half* kc, const half* vc, half* out, int64_t nq,
                                        int64_t nkv, int64_t max_seq, int64_t hd, const int32_t* pos_dev,

@@ -68,6 +68,8 @@ _SIGNATURES = {
                                       _F32, _P]),
     "soinfer_rope_apply_at": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
     "soinfer_kv_cache_append_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "soinfer_decode_step_embed": (_INT, [_P, _I64, _I64, _P, _I64, _P, _P, _P]),
+    "soinfer_decode_step_advance": (_INT, [_P, _I64, _P, _P, _P, _P]),
     "soinfer_decode_attention_at": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
     "soinfer_quantize_pack_int4": (_INT, [_P, ctypes.c_int32, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "soinfer_gemm_w4a16": (_INT, [_P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
@@ -770,6 +772,38 @@ def kv_cache_append(k_cache, v_cache, k_new, v_new, pos: int) -> None:
 def _check_pos_dev(pos_dev, name):
     _check(pos_dev.is_cuda and pos_dev.dtype == torch.int32 and pos_dev.numel() == 1, name,
            "(pos_dev): must be a one-element int32 CUDA tensor")
+
+
+def decode_step_embed(embed, ids, pos_dev, x) -> None:
+    """x [hidden] = embed[ids[*pos_dev]] on the device (the graph decode step's
+    input row); an out-of-range position or token id writes nothing."""
+    name = "decode_step_embed"
+    _f16(embed, f"{name}(embed)")
+    _f16(x, f"{name}(x)")
+    _check(embed.dim() == 2 and embed.is_contiguous(), name, "(embed): must be a contiguous 2D [vocab, hidden] tensor")
+    _check(x.is_contiguous() and x.numel() == embed.size(1), name, "(x): must be contiguous with hidden elements")
+    _check(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 1 and ids.is_contiguous(), name,
+           "(ids): must be a contiguous 1D int32 CUDA tensor")
+    _check_pos_dev(pos_dev, name)
+    dev = _same_device(embed, ids, pos_dev, x)
+    with torch.cuda.device(dev):
+        _call("soinfer_decode_step_embed", _ptr(embed), embed.size(0), embed.size(1), _ptr(ids), ids.numel(),
+              _ptr(pos_dev), _ptr(x), _stream(dev))
+
+
+def decode_step_advance(ids, pos_dev, prompt_len, next_token) -> None:
+    """ids[*pos_dev + 1] = *next_token unless that position is still in the
+    prompt (< *prompt_len), then *pos_dev += 1 -- on the device."""
+    name = "decode_step_advance"
+    _check(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 1 and ids.is_contiguous(), name,
+           "(ids): must be a contiguous 1D int32 CUDA tensor")
+    for t, n in ((pos_dev, "pos_dev"), (prompt_len, "prompt_len"), (next_token, "next_token")):
+        _check(t.is_cuda and t.dtype == torch.int32 and t.numel() == 1, name,
+               f"({n}): must be a one-element int32 CUDA tensor")
+    dev = _same_device(ids, pos_dev, prompt_len, next_token)
+    with torch.cuda.device(dev):
+        _call("soinfer_decode_step_advance", _ptr(ids), ids.numel(), _ptr(pos_dev), _ptr(prompt_len),
+              _ptr(next_token), _stream(dev))
 
 
 def add_rmsnorm(x, x2, weight, eps: float = 1e-6):

@@ -612,6 +612,7 @@ class GraphDecoder:
         self.ids = torch.zeros(max_seq_len + 1, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.prompt_len = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.x_in = torch.empty(model.hidden_size, dtype=torch.float16, device=dev)  # the step's input row
         cos_t, sin_t = ops.precompute_rope_table(model.head_dim, model.rope_theta, max_seq_len, dev)
         self.where = DevicePosition(self.pos, cos_t, sin_t)
         self.k_caches, self.v_caches = _kv_caches(model, max_seq_len)
@@ -642,7 +643,8 @@ class GraphDecoder:
 
     def _step(self) -> None:
         m, where = self.model, self.where
-        x = m.embed_tokens.index_select(0, self.ids.index_select(0, self.pos.long()).long()).view(-1)
+        x = self.x_in
+        _C.decode_step_embed(m.embed_tokens, self.ids, self.pos, x)  # x = embed[ids[pos]], on the device
         if self.fused is not None:
             self.fused.run(x, self.pos)
         for li in range(m.num_layers if self.fused is None else 0):
@@ -658,10 +660,10 @@ class GraphDecoder:
                                           self.dip_k, self.bufs)
         xn = ops.rmsnorm(x.unsqueeze(0), m.final_norm, m.rms_norm_eps).squeeze(0)
         nxt = self.token_fn(m, xn)
-        at = (self.pos + 1).long()
-        keep = (self.pos + 1) < self.prompt_len  # still inside the prompt: keep its token
-        self.ids.index_copy_(0, at, torch.where(keep, self.ids.index_select(0, at), nxt))
-        self.pos.add_(1)
+        if nxt.dtype != torch.int32:
+            nxt = nxt.to(torch.int32)
+        # ids[pos + 1] = nxt unless still inside the prompt (its token stays); pos += 1
+        _C.decode_step_advance(self.ids, self.pos, self.prompt_len, nxt.reshape(1))
 
     def _capture(self) -> None:
         # the buffers, caches and weights were made on the caller's stream
