@@ -148,32 +148,61 @@ __global__ void __launch_bounds__(kThreads)
   for (int i = 0; i < kCols; ++i) acc[i] = 0.f;
 
   if (active) {
-    for (int64_t j = j0 + phase; j < j1; j += kPhases) {
-      const uint8_t* w;
-      const float* s;
-      down_row<M>(src, j, w, s);
-      const float hj = __half2float(h[j]);
+    // kBatch rows per pass: every row's index, weight, scale and h loads are
+    // issued before the first FMA (one latency chain per pass, not per row);
+    // the FMAs still run in ascending j, so the sums are unchanged.
+    constexpr int kBatch = 4;
+    for (int64_t jb = j0 + phase; jb < j1; jb += (int64_t)kPhases * kBatch) {
+      const uint8_t* w[kBatch];
+      const float* s[kBatch];
+      float hj[kBatch];
+#pragma unroll
+      for (int r = 0; r < kBatch; ++r) {
+        const int64_t j = jb + (int64_t)r * kPhases;
+        const int64_t jj = j < j1 ? j : jb;  // past the slab: reload row jb, its terms are skipped
+        down_row<M>(src, jj, w[r], s[r]);
+        hj[r] = __half2float(h[jj]);
+      }
+      float sc[kBatch];
       if constexpr (VEC == 4) {
-        const uint4 q = ldg_stream_u4(w + chunk * 16);
-        float c[5];
-        c[0] = hj * __ldg(s + grp);
-        c[1] = c[0] * 0.0625f;
-        c[2] = c[0] * 0.00390625f;
-        c[3] = c[0] * 0.000244140625f;
-        c[4] = c[0] * 0.0000152587890625f;
-        fma_word(q.x, c, acc + 0);
-        fma_word(q.y, c, acc + 8);
-        fma_word(q.z, c, acc + 16);
-        fma_word(q.w, c, acc + 24);
+        uint4 q[kBatch];
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+          q[r] = ldg_stream_u4(w[r] + chunk * 16);
+          sc[r] = __ldg(s[r] + grp);
+        }
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+          if (jb + (int64_t)r * kPhases >= j1) break;
+          float c[5];
+          c[0] = hj[r] * sc[r];
+          c[1] = c[0] * 0.0625f;
+          c[2] = c[0] * 0.00390625f;
+          c[3] = c[0] * 0.000244140625f;
+          c[4] = c[0] * 0.0000152587890625f;
+          fma_word(q[r].x, c, acc + 0);
+          fma_word(q[r].y, c, acc + 8);
+          fma_word(q[r].z, c, acc + 16);
+          fma_word(q[r].w, c, acc + 24);
+        }
       } else {
-        const uint32_t q = ldg_stream_u32(w + chunk * 4);
-        float c[5];
-        c[0] = hj * __ldg(s + col0 / gsz);
-        c[1] = c[0] * 0.0625f;
-        c[2] = c[0] * 0.00390625f;
-        c[3] = c[0] * 0.000244140625f;
-        c[4] = c[0] * 0.0000152587890625f;
-        fma_word(q, c, acc);
+        uint32_t q[kBatch];
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+          q[r] = ldg_stream_u32(w[r] + chunk * 4);
+          sc[r] = __ldg(s[r] + col0 / gsz);
+        }
+#pragma unroll
+        for (int r = 0; r < kBatch; ++r) {
+          if (jb + (int64_t)r * kPhases >= j1) break;
+          float c[5];
+          c[0] = hj[r] * sc[r];
+          c[1] = c[0] * 0.0625f;
+          c[2] = c[0] * 0.00390625f;
+          c[3] = c[0] * 0.000244140625f;
+          c[4] = c[0] * 0.0000152587890625f;
+          fma_word(q[r], c, acc);
+        }
       }
     }
   }
@@ -202,9 +231,17 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t col = slab_col0 + c;
     if (col >= H) continue;
     float sum = 0.f;
-    const int64_t slabs = gridDim.y;
-#pragma unroll 8
-    for (int64_t r = 0; r < slabs; ++r) sum += __ldcg(partials + r * H + col);
+    const int slabs = (int)gridDim.y;
+    constexpr int kLoads = 32;  // partial rows loaded per pass, summed in row-slab order
+    for (int r0 = 0; r0 < slabs; r0 += kLoads) {
+      float v[kLoads];
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i)
+        v[i] = r0 + i < slabs ? __ldcg(partials + (int64_t)(r0 + i) * H + col) : 0.f;
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i)
+        if (r0 + i < slabs) sum += v[i];
+    }
     half out = __float2half_rn(sum);
     if (resid != nullptr) out = __float2half_rn(__half2float(resid[col]) + __half2float(out));  // residual epilogue
     y[col] = out;

@@ -33,6 +33,7 @@ constexpr int kThreads = 1024;
 constexpr int kWarpsPerBlock = kThreads / 32;
 constexpr int64_t kSmemKeysMax = 49152;
 constexpr int kBisectionSteps = 24;  // reference topk_select.cu:7
+constexpr int kLoadBatch = 4;        // 16-byte input loads in flight per thread
 
 // Order-preserving map float -> uint32 (larger float -> larger key).
 // NaN -> 0 (below -inf), -0 -> +0.
@@ -79,7 +80,7 @@ template <bool EXACT, bool SMEM, bool HALF_ABS>
 __global__ void __launch_bounds__(kThreads)
     topk_kernel(const void* __restrict__ v, const int n, const int k, int32_t* __restrict__ out_idx,
                 int32_t* __restrict__ out_count) {
-  extern __shared__ uint32_t skeys[];
+  extern __shared__ __align__(16) uint32_t skeys[];
   __shared__ uint32_t hist[256];
   __shared__ int s_warp[kWarpsPerBlock];
   __shared__ int s_warp2[kWarpsPerBlock];
@@ -95,10 +96,33 @@ __global__ void __launch_bounds__(kThreads)
 
   // 1) keys (+ max for the reference's upper bisection bound)
   float lmax = 0.f;  // reference: local_max starts at 0 (topk_select.cu:19)
-  for (int i = tid; i < n; i += kThreads) {
-    const float f = sel_value<HALF_ABS>(v, i);
-    lmax = fmaxf(lmax, f);
-    if (SMEM) skeys[i] = float_key(f);
+  if (SMEM && !HALF_ABS && (n & 3) == 0 && (reinterpret_cast<uintptr_t>(v) & 15u) == 0) {
+    // 16-byte loads, kLoadBatch per thread in flight before the first use
+    const float4* v4 = static_cast<const float4*>(v);
+    const int n4 = n >> 2;
+    for (int i0 = tid; i0 < n4; i0 += kThreads * kLoadBatch) {
+      float4 f[kLoadBatch];
+#pragma unroll
+      for (int r = 0; r < kLoadBatch; ++r) {
+        const int i = i0 + r * kThreads;
+        f[r] = i < n4 ? __ldcg(v4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int r = 0; r < kLoadBatch; ++r) {
+        const int i = i0 + r * kThreads;
+        if (i < n4) {
+          lmax = fmaxf(fmaxf(lmax, fmaxf(f[r].x, f[r].y)), fmaxf(f[r].z, f[r].w));
+          reinterpret_cast<uint4*>(skeys)[i] =
+              make_uint4(float_key(f[r].x), float_key(f[r].y), float_key(f[r].z), float_key(f[r].w));
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < n; i += kThreads) {
+      const float f = sel_value<HALF_ABS>(v, i);
+      lmax = fmaxf(lmax, f);
+      if (SMEM) skeys[i] = float_key(f);
+    }
   }
   lmax = warp_max(lmax);
   if (lane == 0) s_wmax[warp] = lmax;
@@ -247,7 +271,7 @@ __device__ __forceinline__ void pick_bin(const uint32_t* hist, int remaining, ui
 __global__ void __launch_bounds__(kThreads)
     topk_abs_half_kernel(const half* __restrict__ v, const int n, const int k, int32_t* __restrict__ out_idx,
                          int32_t* __restrict__ out_count) {
-  extern __shared__ uint16_t sbits[];  // [n] raw fp16 bits
+  extern __shared__ __align__(16) uint16_t sbits[];  // [n] raw fp16 bits
   __shared__ uint32_t hist[256];
   __shared__ int s_warp[kWarpsPerBlock];
   __shared__ int s_total;
@@ -260,10 +284,37 @@ __global__ void __launch_bounds__(kThreads)
   pdl_wait();
   const uint16_t* vb = reinterpret_cast<const uint16_t*>(v);
   float lmax = 0.f;  // reference: local_max starts at 0 (topk_select.cu:19)
-  for (int i = tid; i < n; i += kThreads) {
-    const uint16_t b = vb[i];
-    sbits[i] = b;
-    lmax = fmaxf(lmax, fabsf(__half2float(__ushort_as_half(b))));
+  if ((n & 7) == 0 && (reinterpret_cast<uintptr_t>(v) & 15u) == 0) {
+    // 16-byte loads, kLoadBatch per thread in flight before the first use
+    const uint4* v8 = reinterpret_cast<const uint4*>(v);
+    const int n8 = n >> 3;
+    for (int i0 = tid; i0 < n8; i0 += kThreads * kLoadBatch) {
+      uint4 u[kLoadBatch];
+#pragma unroll
+      for (int r = 0; r < kLoadBatch; ++r) {
+        const int i = i0 + r * kThreads;
+        u[r] = i < n8 ? __ldcg(v8 + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int r = 0; r < kLoadBatch; ++r) {
+        const int i = i0 + r * kThreads;
+        if (i < n8) {
+          reinterpret_cast<uint4*>(sbits)[i] = u[r];
+          const half2* hp = reinterpret_cast<const half2*>(&u[r]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(hp[e]);
+            lmax = fmaxf(lmax, fmaxf(fabsf(f.x), fabsf(f.y)));
+          }
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < n; i += kThreads) {
+      const uint16_t b = vb[i];
+      sbits[i] = b;
+      lmax = fmaxf(lmax, fabsf(__half2float(__ushort_as_half(b))));
+    }
   }
   for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
   lmax = warp_max(lmax);
