@@ -17,7 +17,8 @@
 // for the packed rows, one for their scale rows) completing on one mbarrier.
 // A tile too long for one item (K above ~6K, e.g. a 14B down_proj) is cut
 // along K into segments of ks 128-chunks, one item each (one bulk copy per
-// row); the consumers accumulate a tile's segments in their partial rows.
+// row); a warp carries its chain for a tile from segment to segment through
+// its partial rows, so the sums do not depend on where the segments fall.
 // Scale rows that are not whole 16-byte pieces (tensor-parallel shards with
 // 5, 10, 17 or 34 groups per row) are staged with 4-byte cp.async copies that
 // arrive on the item's barrier; segment scales go as one bulk copy per row.  Items of any size
@@ -236,7 +237,9 @@ __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint
     const float* sa = s0p;
     if (ct.g > last) wa -= (ct.g - last) * ct.row_bytes, sa -= (ct.g - last) * ct.G;
     if (ct.g + 8 > last) w1 -= (ct.g + 8 - last) * ct.row_bytes, s1p -= (ct.g + 8 - last) * ct.G;
-    float acc0 = 0.f, acc1 = 0.f;
+    // a later K-segment continues the warp's chain from its stored partial,
+    // so the sums are those of the unsegmented tile (the same fma sequence)
+    float acc0 = accum ? ct.rr[tt * 16 + ct.g] : 0.f, acc1 = accum ? ct.rr[tt * 16 + ct.g + 8] : 0.f;
     if (NM > 0) {
 #pragma unroll
       for (int i = 0; i < NM; ++i) consume_unit(xr[i], wa, w1, sa[i * kGroupWarps], s1p[i * kGroupWarps], br[i], i, acc0, acc1);
@@ -273,10 +276,6 @@ __device__ __forceinline__ void consume_tiles(const ConsumerTask& ct, const uint
         const int sc = G128 ? i * kGroupWarps : (ct.c_first + i * kGroupWarps) / ct.cpg;
         consume_unit(xf, wa, w1, sa[sc], s1p[sc], ct.sbias[i], i, acc0, acc1);
       }
-    }
-    if (accum) {  // a later K-segment of the tile
-      acc0 += ct.rr[tt * 16 + ct.g];
-      acc1 += ct.rr[tt * 16 + ct.g + 8];
     }
     ct.rr[tt * 16 + ct.g] = acc0;
     ct.rr[tt * 16 + ct.g + 8] = acc1;

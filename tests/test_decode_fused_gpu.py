@@ -5,9 +5,10 @@ It must reproduce the per-kernel CUDA-graph decode step bit for bit: the
 same greedy tokens, and -- a stronger check, since every layer's K / V rows
 depend on all earlier layers' outputs -- identical KV caches after the run.
 Cases: the Qwen3-1.7B layer shape (16 q / 8 kv heads) and two other GQA
-ratios (1 and 4), prompts short enough for a single attention split and long
-enough for many (the combine phase), and two generate calls in a row (the
-barrier counters reset themselves)."""
+ratios (1 and 4), a down_proj long enough for the per-kernel batch to cut its
+tiles into K-segments, prompts short enough for a single attention split and
+long enough for many (the combine phase), and two generate calls in a row
+(the barrier counters reset themselves)."""
 import pytest
 import torch
 
@@ -23,6 +24,9 @@ pytestmark = pytest.mark.gpu
     (Architecture(2, 2048, 6144, 16, 8, 128, 1024), 300, 8),    # many splits: the combine phase
     (Architecture(2, 1024, 3072, 8, 8, 128, 512), 40, 8),       # one query head per kv head
     (Architecture(2, 2048, 5120, 16, 4, 128, 512), 70, 8),      # four query heads per kv head
+    # down_proj K = 7168: the per-kernel batch cuts its 16-row tiles into K-segments,
+    # the fused step does not -- the sums must not depend on the segmentation
+    (Architecture(2, 1024, 7168, 8, 8, 128, 512), 40, 8),
 ])
 def test_fused_step_equals_per_kernel_step(arch, prompt_len, n_new):
     model = synthetic_streaming_model(arch, seed=3, resident=True, offload=False, include_dip=False)
