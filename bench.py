@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the soinfer B200 decode hot path on BASELINE.json's headline
+"""Benchmark of the soinfer B200 decode hot path on the reference's headline
 metric: INT4 g128 GEMV HBM throughput (GB/s, % of measured HBM peak).
 
 Workload (configs[0] shapes, run on the GPU): per layer copy one gate_proj
@@ -172,7 +172,7 @@ def cpu_gemv_sample(seconds: float, threads: int):
 
 
 def op_suite(ops, formats, pack, device, capturable: bool, iters: int = 200) -> dict:
-    """Per-call latency of the hot-path ops at the BASELINE config shapes,
+    """Per-call latency of the hot-path ops at the benchmark configs' shapes,
     through the given `ops` module with the same names and arguments -- this
     build's soinfer.ops, or the reference's own (its extension compiled for
     sm_100a, baseline/_ref) in the reference arm.  Inputs come from the
@@ -296,7 +296,7 @@ def run_reference(args) -> None:
     tests/test_m4_kernels.py:157-168) -- from the reference package installed
     under baseline/_ref, or the oracle's numpy restatement when that install
     is absent.  Also times the reference's own CUDA ops (its extension built
-    for sm_100a) at the BASELINE shapes on this GPU (config.ref_ops_b200)."""
+    for sm_100a) at the benchmark configs' shapes on this GPU (config.ref_ops_b200)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
