@@ -186,3 +186,53 @@ def test_peer_set_and_exchange_arguments():
     assert bt(ctypes.byref(ps), ctypes.addressof(arr), n, None, 0, None) == 1 and "no epilogue" in _err()
     arr, n = _tasks(_task(N=4096, y=None))
     assert bt(ctypes.byref(ps), ctypes.addressof(arr), n, None, 0, None) == 1 and "exceed the exchange slot" in _err()
+
+
+def test_graph_step_bookkeeping_arguments():
+    lib = _C.lib()
+    # embedding row: sizes and pointers are checked before anything is launched
+    assert lib.soinfer_decode_step_embed(P, 0, 2048, P, 16, P, P2, None) == 1 and "invalid sizes" in _err()
+    assert lib.soinfer_decode_step_embed(P, 1000, 2048, P, 0, P, P2, None) == 1 and "invalid sizes" in _err()
+    assert lib.soinfer_decode_step_embed(P, 1000, 2048, None, 16, P, P2, None) == 1 and "null pointer" in _err()
+    assert lib.soinfer_decode_step_embed(P, 1000, 2048, P, 16, None, P2, None) == 1 and "null pointer" in _err()
+    # token / position advance
+    assert lib.soinfer_decode_step_advance(P, 0, P, P, P, None) == 1 and "ids_len" in _err()
+    assert lib.soinfer_decode_step_advance(P, 16, P, P, None, None) == 1 and "null pointer" in _err()
+    assert lib.soinfer_decode_step_advance(None, 16, P, P, P, None) == 1 and "null pointer" in _err()
+
+
+def _fused_layers(n=1, misaligned_weight=False, null_cache=False):
+    arr = (_C._FusedLayer * n)()
+    for layer in arr:
+        for m in range(7):
+            layer.Wq[m] = 0x10008 if misaligned_weight else 0x10000
+            layer.scale[m] = 0x20000
+        layer.input_norm = layer.post_norm = layer.q_norm = layer.k_norm = 0x30000
+        layer.k_cache = 0 if null_cache else 0x40000
+        layer.v_cache = 0x50000
+    return arr
+
+
+def test_fused_decode_arguments():
+    lib = _C.lib()
+    f = lib.soinfer_decode_layers_fused
+    ok = dict(num_layers=1, hidden=2048, intermediate=6144, heads=16, kv=8, hd=128, g=128, max_seq=64)
+
+    def call(layers, x=P, ws=P, **over):
+        a = {**ok, **over}
+        return f(ctypes.addressof(layers) if layers is not None else None, a["num_layers"], a["hidden"],
+                 a["intermediate"], a["heads"], a["kv"], a["hd"], a["g"], a["max_seq"], ctypes.c_float(1e-6), P, P, P,
+                 x, ws, 1 << 24, None)
+
+    layers = _fused_layers()
+    assert call(None) == 1 and "null pointer" in _err()
+    assert call(layers, max_seq=0) == 1 and "sizes must be positive" in _err()
+    # shapes this build does not serve: SOINFER_ERR_UNSUPPORTED, nothing launched
+    assert call(layers, hd=64) == 3 and "head_dim 128" in _err()
+    assert call(layers, g=64) == 3
+    assert call(layers, heads=12) == 3  # not a multiple of num_kv_heads
+    assert call(layers, hidden=2000) == 3
+    assert call(layers, num_layers=65) == 3 and "64 layers" in _err()
+    assert call(layers, x=ctypes.c_void_p(0x10002)) == 1 and "aligned" in _err()
+    assert call(_fused_layers(misaligned_weight=True)) == 3 and "16-byte aligned" in _err()
+    assert call(_fused_layers(null_cache=True)) == 1 and "null norm weight or cache" in _err()
