@@ -54,14 +54,21 @@ __device__ __forceinline__ void chunk_dot(const uint4 wa, const uint4 wb, const 
 // rmsnorm_piece -- x = fp16(x * inv * w) per 16-byte piece, the rmsnorm
 // kernel's expression (any thread, any order).
 __device__ __forceinline__ float warp_rmsnorm_inv(const uint4* x, int n16, int K, float eps, int lane) {
+  constexpr int kB = 4;  // pieces loaded ahead of the (in-order) accumulation
   float ss = 0.f;
-  for (int u = lane; u < n16; u += 32) {
-    const uint4 v = x[u];
-    const half2* h = reinterpret_cast<const half2*>(&v);
+  for (int u0 = lane; u0 < n16; u0 += 32 * kB) {
+    uint4 v[kB];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __half22float2(h[j]);
-      ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));  // no contraction: same bits everywhere
+    for (int r = 0; r < kB; ++r) v[r] = u0 + 32 * r < n16 ? x[u0 + 32 * r] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int r = 0; r < kB; ++r) {
+      if (u0 + 32 * r >= n16) break;
+      const half2* h = reinterpret_cast<const half2*>(&v[r]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(f.x, f.x), __fmul_rn(f.y, f.y)));  // no contraction: same bits everywhere
+      }
     }
   }
 #pragma unroll
@@ -86,10 +93,19 @@ __device__ __forceinline__ uint4 rmsnorm_piece(const uint4 v, const uint4 wv, fl
 __device__ __forceinline__ void warp_rmsnorm_inplace(uint4* x, const uint4* w, int n16, int K, float eps, int lane,
                                                      uint4* out) {
   const float inv = warp_rmsnorm_inv(x, n16, K, eps, lane);
-  for (int u = lane; u < n16; u += 32) {
-    const uint4 o = rmsnorm_piece(x[u], w[u], inv);
-    x[u] = o;
-    if (out != nullptr) out[u] = o;
+  constexpr int kB = 4;
+  for (int u0 = lane; u0 < n16; u0 += 32 * kB) {
+    uint4 xv[kB], wv[kB];
+#pragma unroll
+    for (int r = 0; r < kB; ++r)
+      if (u0 + 32 * r < n16) xv[r] = x[u0 + 32 * r], wv[r] = w[u0 + 32 * r];
+#pragma unroll
+    for (int r = 0; r < kB; ++r) {
+      if (u0 + 32 * r >= n16) break;
+      const uint4 o = rmsnorm_piece(xv[r], wv[r], inv);
+      x[u0 + 32 * r] = o;
+      if (out != nullptr) out[u0 + 32 * r] = o;
+    }
   }
 }
 
